@@ -1,0 +1,303 @@
+// C-ABI entry points (include/frank_moe.h) and the orchestration of the MoE
+// FFN block / mul_mat_id out of the kernels in routing.cu, elementwise.cu,
+// gemm_simt.cu and gemm_tc.cu.
+#include <mutex>
+#include <vector>
+
+#include "common.cuh"
+
+namespace frank {
+
+// ---- kernels implemented in the other translation units ----
+int launch_softmax_topk(const float*, int64_t, int64_t, int64_t, int, float*, int32_t*, cudaStream_t);
+int launch_router_topk(int, const void*, int, const void*, int64_t, int64_t, int64_t, int64_t, int, float*, int32_t*,
+                       cudaStream_t);
+size_t permute_workspace_size(int64_t, int64_t);
+int launch_permute(const int32_t*, int64_t, int64_t, int32_t*, int32_t*, int32_t*, int32_t*, void*, size_t,
+                   cudaStream_t);
+int launch_swiglu(int, const void*, const void*, void*, int64_t, cudaStream_t);
+int launch_prepack(int, const void*, int64_t, int64_t, int64_t, int, void*, cudaStream_t);
+int launch_gather_rows(int, const void*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
+int launch_gather_cols(int, const void*, const int32_t*, int64_t, int64_t, void*, cudaStream_t);
+int launch_scatter_out(const float*, const int32_t*, int64_t, int64_t, float*, cudaStream_t);
+int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
+int launch_sorted_weights(const float*, const int32_t*, int64_t, float*, cudaStream_t);
+int launch_grouped_gemm_f32(int, const float*, const float*, const float*, const int32_t*, int64_t, int64_t, int64_t,
+                            int64_t, const float*, float*, cudaStream_t);
+int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int32_t*, int64_t, int64_t, int64_t,
+                           int64_t, const float*, void*, cudaStream_t);
+int check_tc_shapes(int64_t, int64_t, int64_t, int64_t);
+
+// ---- error state ----
+static thread_local std::string g_err;
+
+void set_error(const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+}
+
+__device__ int32_t g_device_error = 0;
+
+int32_t* device_error_word() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::vector<int32_t*> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, nullptr);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_device_error) != cudaSuccess) return nullptr;
+    cache[dev] = static_cast<int32_t*>(p);
+  }
+  return cache[dev];
+}
+
+int num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::vector<int> cache;
+  std::lock_guard<std::mutex> lk(mu);
+  if ((int)cache.size() <= dev) cache.resize(dev + 1, 0);
+  if (!cache[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 1;
+  }
+  return cache[dev];
+}
+
+// ---- workspace layouts ----
+struct MoeWs {
+  float* w;
+  int32_t* ids;
+  int32_t* sorted_slots;
+  int32_t* offsets;
+  int32_t* slot_pos;
+  int32_t* err;
+  float* wsorted;
+  void* xs;
+  void* hs;
+  float* ds;
+  void* perm_ws;
+  size_t perm_bytes;
+};
+
+static size_t moe_layout(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k, void* base, size_t cap,
+                         MoeWs* L) {
+  const int64_t n = k * T;
+  const size_t esz = dtype == FRANK_F32 ? 4 : 2;
+  Carve c(base, cap);
+  MoeWs l;
+  l.w = c.take<float>(n);
+  l.ids = c.take<int32_t>(n);
+  l.sorted_slots = c.take<int32_t>(n);
+  l.offsets = c.take<int32_t>(E + 1);
+  l.slot_pos = c.take<int32_t>(n);
+  l.err = c.take<int32_t>(1);
+  l.wsorted = c.take<float>(n);
+  l.xs = c.take<char>(n * H * esz);
+  l.hs = c.take<char>(n * F * esz);
+  l.ds = c.take<float>(n * H);
+  l.perm_bytes = permute_workspace_size(n, E);
+  l.perm_ws = c.take<char>(l.perm_bytes);
+  if (L) *L = l;
+  return align_up(c.used, 256);
+}
+
+struct MmidWs {
+  int32_t* sorted_slots;
+  int32_t* offsets;
+  int32_t* slot_pos;
+  void* xs;
+  float* ys;
+  void* perm_ws;
+  size_t perm_bytes;
+};
+
+static size_t mmid_layout(int dtype, int64_t O, int64_t I, int64_t E, int64_t k, int64_t T, void* base, size_t cap,
+                          MmidWs* L) {
+  const int64_t n = k * T;
+  const size_t esz = dtype == FRANK_F32 ? 4 : 2;
+  Carve c(base, cap);
+  MmidWs l;
+  l.sorted_slots = c.take<int32_t>(n);
+  l.offsets = c.take<int32_t>(E + 1);
+  l.slot_pos = c.take<int32_t>(n);
+  l.xs = c.take<char>(n * I * esz);
+  l.ys = c.take<float>(n * O);
+  l.perm_bytes = permute_workspace_size(n, E);
+  l.perm_ws = c.take<char>(l.perm_bytes);
+  if (L) *L = l;
+  return align_up(c.used, 256);
+}
+
+static int check_dtype(int d, const char* what) {
+  if (d != FRANK_F32 && d != FRANK_BF16) {
+    set_error("%s: dtype %d is neither FRANK_F32 (0) nor FRANK_BF16 (1)", what, d);
+    return FRANK_EINVAL;
+  }
+  return FRANK_OK;
+}
+
+}  // namespace frank
+
+using namespace frank;
+
+extern "C" {
+
+const char* frank_last_error(void) { return g_err.c_str(); }
+
+int frank_abi_version(void) { return 100; }
+
+int frank_num_sms(void) { return num_sms(); }
+
+int frank_swiglu(int dtype, const void* gate, const void* up, void* out, int64_t n, void* stream) {
+  FRANK_TRY(check_dtype(dtype, "swiglu"));
+  FRANK_CHECK_ARG(n >= 0, "swiglu: n=%lld < 0", (long long)n);
+  FRANK_CHECK_ARG(n == 0 || (gate && up && out), "swiglu: null pointer");
+  return launch_swiglu(dtype, gate, up, out, n, as_stream(stream));
+}
+
+int frank_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k, int normalize, float* weights,
+                       int32_t* ids, void* stream) {
+  FRANK_CHECK_ARG(E >= 1 && E <= 256, "softmax_topk: E=%lld outside [1, 256]", (long long)E);
+  FRANK_CHECK_ARG(k >= 1 && k <= E && k <= 32, "softmax_topk: k=%lld outside [1, min(E, 32)]", (long long)k);
+  FRANK_CHECK_ARG(T >= 0, "softmax_topk: T < 0");
+  return launch_softmax_topk(logits, T, E, k, normalize, weights, ids, as_stream(stream));
+}
+
+int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H, int64_t E,
+                      int64_t k, int normalize, float* weights, int32_t* ids, void* stream) {
+  FRANK_TRY(check_dtype(x_dtype, "router_topk"));
+  FRANK_TRY(check_dtype(wr_dtype, "router_topk"));
+  FRANK_CHECK_ARG(E >= 1 && E <= 256, "router_topk: E=%lld outside [1, 256]", (long long)E);
+  FRANK_CHECK_ARG(k >= 1 && k <= E && k <= 32, "router_topk: k=%lld outside [1, min(E, 32)]", (long long)k);
+  FRANK_CHECK_ARG(T >= 0 && H >= 1, "router_topk: bad T=%lld / H=%lld", (long long)T, (long long)H);
+  return launch_router_topk(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, weights, ids, as_stream(stream));
+}
+
+size_t frank_permute_workspace_size(int64_t n_slots, int64_t E) { return permute_workspace_size(n_slots, E); }
+
+int frank_permute(const int32_t* ids, int64_t n_slots, int64_t E, int32_t* sorted_slots, int32_t* offsets,
+                  int32_t* slot_pos, int32_t* err_flag, void* workspace, size_t ws_bytes, void* stream) {
+  FRANK_CHECK_ARG(n_slots >= 0 && n_slots < 0x7fffffffLL, "permute: n_slots=%lld out of range", (long long)n_slots);
+  return launch_permute(ids, n_slots, E, sorted_slots, offsets, slot_pos, err_flag, workspace, ws_bytes,
+                        as_stream(stream));
+}
+
+int frank_prepack_experts(int in_dtype, const void* w_oie, int64_t O, int64_t I, int64_t E, int out_dtype,
+                          void* w_eoi, void* stream) {
+  FRANK_TRY(check_dtype(in_dtype, "prepack"));
+  FRANK_TRY(check_dtype(out_dtype, "prepack"));
+  FRANK_CHECK_ARG(O >= 0 && I >= 0 && E >= 0, "prepack: negative extent");
+  return launch_prepack(in_dtype, w_oie, O, I, E, out_dtype, w_eoi, as_stream(stream));
+}
+
+size_t frank_mul_mat_id_workspace_size(int dtype, int64_t O, int64_t I, int64_t E, int64_t k, int64_t T) {
+  return mmid_layout(dtype, O, I, E, k, T, nullptr, 0, nullptr);
+}
+
+int frank_mul_mat_id(int dtype, const void* w_eoi, const void* input, const int32_t* ids, int64_t O, int64_t I,
+                     int64_t E, int64_t k, int64_t T, float* out, int32_t* err_flag, void* workspace,
+                     size_t ws_bytes, void* stream) {
+  FRANK_TRY(check_dtype(dtype, "mul_mat_id"));
+  FRANK_CHECK_ARG(O >= 1 && I >= 1 && E >= 1 && k >= 1 && T >= 0, "mul_mat_id: bad shape O=%lld I=%lld E=%lld k=%lld T=%lld",
+                  (long long)O, (long long)I, (long long)E, (long long)k, (long long)T);
+  cudaStream_t st = as_stream(stream);
+  const int64_t n = k * T;
+  if (n == 0) return FRANK_OK;
+  if (dtype == FRANK_BF16) FRANK_TRY(check_tc_shapes(n, O, I, E));
+  size_t need = mmid_layout(dtype, O, I, E, k, T, nullptr, 0, nullptr);
+  if (ws_bytes < need) {
+    set_error("mul_mat_id: workspace %zu < %zu bytes", ws_bytes, need);
+    return FRANK_ENOSPC;
+  }
+  MmidWs L;
+  mmid_layout(dtype, O, I, E, k, T, workspace, ws_bytes, &L);
+  FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, err_flag, L.perm_ws, L.perm_bytes, st));
+  FRANK_TRY(launch_gather_cols(dtype, input, L.sorted_slots, n, I, L.xs, st));
+  if (dtype == FRANK_F32) {
+    FRANK_TRY(launch_grouped_gemm_f32(0, (const float*)L.xs, (const float*)w_eoi, nullptr, L.offsets, E, n, O, I,
+                                      nullptr, L.ys, st));
+  } else {
+    FRANK_TRY(launch_tc_grouped_gemm(2, L.xs, w_eoi, nullptr, L.offsets, E, n, O, I, nullptr, L.ys, st));
+  }
+  return launch_scatter_out(L.ys, L.slot_pos, n, O, out, st);
+}
+
+size_t frank_moe_ffn_block_workspace_size(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
+  return moe_layout(dtype, T, H, F, E, k, nullptr, 0, nullptr);
+}
+
+int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, const void* w_up_p,
+                        const void* w_gate_p, const void* w_down_p, int64_t T, int64_t E, int64_t k, int64_t H,
+                        int64_t F, int normalize, void* y, float* route_w, int32_t* route_ids, void* workspace,
+                        size_t ws_bytes, void* stream) {
+  FRANK_TRY(check_dtype(dtype, "moe_ffn_block"));
+  FRANK_TRY(check_dtype(wr_dtype, "moe_ffn_block"));
+  FRANK_CHECK_ARG(E >= 1 && E <= 256, "moe_ffn_block: n_expert=%lld outside [1, 256]", (long long)E);
+  FRANK_CHECK_ARG(k >= 1 && k <= E && k <= 32, "moe_ffn_block: n_expert_used=%lld outside [1, min(E, 32)]",
+                  (long long)k);
+  FRANK_CHECK_ARG(T >= 0 && H >= 1 && F >= 1, "moe_ffn_block: bad T=%lld H=%lld F=%lld", (long long)T, (long long)H,
+                  (long long)F);
+  cudaStream_t st = as_stream(stream);
+  if (T == 0) return FRANK_OK;
+  const int64_t n = k * T;
+  if (dtype == FRANK_BF16) {
+    FRANK_TRY(check_tc_shapes(n, F, H, E));
+    FRANK_TRY(check_tc_shapes(n, H, F, E));
+    FRANK_CHECK_ARG(H % 4 == 0, "moe_ffn_block bf16: n_embd %% 4 != 0");
+  }
+  size_t need = moe_layout(dtype, T, H, F, E, k, nullptr, 0, nullptr);
+  if (ws_bytes < need) {
+    set_error("moe_ffn_block: workspace %zu < %zu bytes", ws_bytes, need);
+    return FRANK_ENOSPC;
+  }
+  MoeWs L;
+  moe_layout(dtype, T, H, F, E, k, workspace, ws_bytes, &L);
+  float* w = route_w ? route_w : L.w;
+  int32_t* ids = route_ids ? route_ids : L.ids;
+  // 1. router + softmax + top-k (+ renorm)          moe_ffn_block.mlir:54-128
+  FRANK_TRY(launch_router_topk(dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, st));
+  // 2. stable expert permutation                    mul_mat_id.mlir:51-61
+  FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, nullptr, L.perm_ws, L.perm_bytes, st));
+  FRANK_TRY(launch_sorted_weights(w, L.sorted_slots, n, L.wsorted, st));
+  // 3. expert-sorted activation rows (replicate + permute, :130-144, mul_mat_id.mlir:64-84)
+  FRANK_TRY(launch_gather_rows(dtype, x, L.sorted_slots, n, T, H, L.xs, st));
+  if (dtype == FRANK_F32) {
+    // 4. h = gate(x) * silu(up(x))                   :146-156
+    FRANK_TRY(launch_grouped_gemm_f32(2, (const float*)L.xs, (const float*)w_gate_p, (const float*)w_up_p, L.offsets,
+                                      E, n, F, H, nullptr, (float*)L.hs, st));
+    // 5. d = down(h) * w                             :158-177
+    FRANK_TRY(launch_grouped_gemm_f32(1, (const float*)L.hs, (const float*)w_down_p, nullptr, L.offsets, E, n, H, F,
+                                      L.wsorted, L.ds, st));
+  } else {
+    FRANK_TRY(launch_tc_grouped_gemm(0, L.xs, w_gate_p, w_up_p, L.offsets, E, n, F, H, nullptr, L.hs, st));
+    FRANK_TRY(launch_tc_grouped_gemm(1, L.hs, w_down_p, nullptr, L.offsets, E, n, H, F, L.wsorted, L.ds, st));
+  }
+  // 6. y[t] = sum_j d[slot j of t]                   :179-206
+  return launch_combine(dtype, L.ds, L.slot_pos, T, k, H, y, st);
+}
+
+int frank_read_device_error(int32_t* out, void* stream) {
+  int32_t* p = device_error_word();
+  if (!p) {
+    set_error("device error word unavailable");
+    return FRANK_ECUDA;
+  }
+  cudaStream_t st = as_stream(stream);
+  int32_t v = 0;
+  FRANK_CUDA_TRY(cudaMemcpyAsync(&v, p, sizeof(v), cudaMemcpyDeviceToHost, st));
+  FRANK_CUDA_TRY(cudaMemsetAsync(p, 0, sizeof(v), st));
+  FRANK_CUDA_TRY(cudaStreamSynchronize(st));
+  if (out) *out = v;
+  return FRANK_OK;
+}
+
+}  // extern "C"

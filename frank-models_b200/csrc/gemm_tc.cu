@@ -1,0 +1,499 @@
+// Grouped expert GEMM on the 5th-generation tensor cores (tcgen05 + TMEM),
+// fed by TMA: the bf16 path of mul_mat_id and moe_ffn_block.
+//
+//   C[r, n] = sum_k A[r, k] * B_e[n, k]   for the rows r of expert e
+//   A  : expert-sorted activation rows [rows, K] bf16 (K-major)
+//   B_e: packed expert weights [E, N, K] bf16 (K-major)
+//
+// Replaces the gather of whole expert matrices + per-slot mat-vec of
+// components/moe/mul_mat_id.mlir:58-94 (oracles/moe.py:33-44) with one
+// GEMM per expert over the rows routed to it.
+//
+// Structure (one persistent CTA per SM, 192 threads, 1 CTA/SM):
+//   warp 0      TMA producer: A tile 128x64 + B tile 256x64 per stage
+//               (SWIZZLE_128B), 4-stage mbarrier ring.
+//   warp 1      TMEM allocator + MMA issuer: tcgen05.mma.cta_group::1
+//               kind::f16, M=128 N=256 K=16, fp32 accumulator in TMEM,
+//               two accumulator buffers (2 x 256 columns).
+//   warps 2..5  epilogue: tcgen05.ld 32x32b, fused activation, stores.
+// Tiles are (expert, m-tile, n-tile) with m fastest inside an expert so the
+// CTAs running at the same time share weight tiles through L2; the per-
+// expert tile prefix is computed on the device from the permutation's
+// offsets, so the host never synchronises.
+//
+// Epilogue modes
+//   SWIGLU: B tile = 128 gate rows + 128 up rows of the same n range; the
+//           epilogue writes h = gate * silu(up) as bf16 [rows, N]
+//           (swiglu.mlir:37-47, silu on `up`).
+//   SCALE : 256 output columns scaled by the row's gate weight, fp32 out
+//           (moe_ffn_block.mlir:162-177).
+//   PLAIN : 256 output columns, fp32 out (mul_mat_id).
+// Every mbarrier wait is bounded (about 2 s); on expiry the CTA records
+// FRANK_ETIMEOUT in the device error word and unwinds, freeing its TMEM.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192;
+constexpr uint32_t A_BYTES = BM * BK * 2;        // 16 KiB
+constexpr uint32_t B_HALF_BYTES = 128 * BK * 2;  // 16 KiB
+constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KiB
+constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr uint32_t TMEM_COLS = 512;
+constexpr int kMaxExperts = 1024;
+
+enum Mode { SWIGLU = 0, SCALE = 1, PLAIN = 2 };
+
+struct Params {
+  const int32_t* offsets;  // [E+1] expert row offsets (permutation output)
+  int E;
+  int n_tiles;             // output column tiles per expert
+  int N_out;               // output columns
+  int K;
+  void* out;               // SWIGLU: bf16 [rows, ldo]; SCALE/PLAIN: fp32 [rows, ldo]
+  int64_t ldo;
+  const float* wrow;       // SCALE: per sorted row weight
+  int32_t* err;            // device error word
+};
+
+// ------------------------------------------------------------ PTX glue --
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bounded wait: ~2 s of wall time, or until another role raised *abort.
+__device__ __noinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int32_t* err) {
+  uint64_t t0 = 0;
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u) {
+      if (*abort) return false;
+      uint64_t now = global_ns();
+      if (t0 == 0) {
+        t0 = now;
+      } else if (now - t0 > 2000000000ull) {
+        *abort = 1;
+        atomicExch(err, FRANK_ETIMEOUT);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(
+          dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand, 128-byte swizzle: rows of 128 B, 8-row groups 1024 B apart.
+// Fields: start>>4 [0,14), LBO>>4 [16,30) (=1, unused for swizzled K-major),
+// SBO>>4 [32,46) (=1024>>4), version 1 [46,48), layout SWIZZLE_128B=2 [61,64).
+__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16: D fp32 [4,6)=1, A bf16 [7,10)=1,
+// B bf16 [10,13)=1, both K-major, N>>3 at [17,23), M>>4 at [24,29).
+constexpr uint32_t kIdesc = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(kIdesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ------------------------------------------------------------- kernel --
+struct Tile {
+  int e, m0, m_end, n;
+};
+
+__device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int32_t* offsets, int E) {
+  int lo = 0, hi = E;  // find e: prefix[e] <= t < prefix[e+1]
+  while (hi - lo > 1) {
+    int mid = (lo + hi) >> 1;
+    if (prefix[mid] <= t) lo = mid; else hi = mid;
+  }
+  const int e = lo;
+  const int r0 = offsets[e], r1 = offsets[e + 1];
+  const int mt = (r1 - r0 + BM - 1) / BM;
+  const int local = t - prefix[e];
+  Tile tl;
+  tl.e = e;
+  tl.m0 = r0 + (local % mt) * BM;
+  tl.m_end = r1;
+  tl.n = local / mt;
+  return tl;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(THREADS, 1)
+tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                       const __grid_constant__ CUtensorMap tmB2, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  // bars[0..S) full, [S..2S) empty, [2S, 2S+2) tmem_full, [2S+2, 2S+4) tmem_empty
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* prefix = reinterpret_cast<int*>(tmem_slot + 4);  // [E+1]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES + 2 + a); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 0) {
+    // tile prefix over experts: prefix[e] = sum_{e'<e} ceil(cnt_e'/BM) * n_tiles
+    int carry = 0;
+    for (int base = 0; base < p.E; base += 32) {
+      int e = base + lane;
+      int v = 0;
+      if (e < p.E) v = ((p.offsets[e + 1] - p.offsets[e] + BM - 1) / BM) * p.n_tiles;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (e < p.E) prefix[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) prefix[p.E] = carry;
+  } else if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total = prefix[p.E];
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------ TMA producer --
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        Tile tl = decode_tile(t, prefix, p.offsets, p.E);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+          uint8_t* st = smem + s * STAGE_BYTES;
+          mbar_expect_tx(full_bar(s), STAGE_BYTES);
+          tma_load_2d(smem_u32(st), &tmA, kb * BK, tl.m0, full_bar(s));
+          if (MODE == SWIGLU) {
+            tma_load_3d(smem_u32(st + A_BYTES), &tmB, kb * BK, tl.n * 128, tl.e, full_bar(s));
+            tma_load_3d(smem_u32(st + A_BYTES + B_HALF_BYTES), &tmB2, kb * BK, tl.n * 128, tl.e, full_bar(s));
+          } else {
+            tma_load_3d(smem_u32(st + A_BYTES), &tmB, kb * BK, tl.n * BN, tl.e, full_bar(s));
+            tma_load_3d(smem_u32(st + A_BYTES + B_HALF_BYTES), &tmB, kb * BK, tl.n * BN + 128, tl.e, full_bar(s));
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ------------------------------------------------- MMA issuer --
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total && ok; t += gridDim.x, ++tc) {
+        const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
+        if (!mbar_wait(tempty_bar(a), aph ^ 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + a * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(full_bar(s), ph, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
+          const uint64_t adesc = make_sw128_desc(sa);
+          const uint64_t bdesc = make_sw128_desc(sa + A_BYTES);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j) {
+            // advance 16 bf16 = 32 B along K inside the 128-B swizzle row
+            mma_bf16(d, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), (kb | j) != 0);
+          }
+          mma_commit(empty_bar(s));
+        }
+        if (ok) mma_commit(tfull_bar(a));
+      }
+    }
+  } else {
+    // ------------------------------------------------------ epilogue --
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    uint32_t tc = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
+      Tile tl = decode_tile(t, prefix, p.offsets, p.E);
+      const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
+      if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = tl.m0 + q * 32 + lane;
+      const bool valid = row < tl.m_end;
+      const uint32_t taddr = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
+      if (MODE == SWIGLU) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 16) {
+          float g[16], u[16];
+          tmem_ld16(taddr + c, g);
+          tmem_ld16(taddr + 128 + c, u);
+          tmem_wait_ld();
+          const int col = tl.n * 128 + c;
+          if (valid && col < p.N_out) {
+            uint32_t pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              pk[i] = pack_bf16x2(g[2 * i] * silu_ref(u[2 * i]), g[2 * i + 1] * silu_ref(u[2 * i + 1]));
+            uint4* dst = reinterpret_cast<uint4*>(out + col);
+            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+          }
+        }
+      } else {
+        float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+        const float s = (MODE == SCALE && valid) ? p.wrow[row] : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float v[16];
+          tmem_ld16(taddr + c, v);
+          tmem_wait_ld();
+          const int col = tl.n * BN + c;
+          if (valid && col < p.N_out) {
+            float4* dst = reinterpret_cast<float4*>(out + col);
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              dst[i] = make_float4(v[4 * i] * s, v[4 * i + 1] * s, v[4 * i + 2] * s, v[4 * i + 3] * s);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(a));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------ host side --
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+// 2-D bf16 map [rows, K], box {64, 128}, 128-B swizzle.
+int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t K) {
+  auto enc = get_encode();
+  if (!enc) {
+    frank::set_error("cuTensorMapEncodeTiled unavailable");
+    return FRANK_ECUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  cuuint32_t box[2] = {BK, 128};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    frank::set_error("cuTensorMapEncodeTiled(2d rows=%lld K=%lld) failed: %d", (long long)rows, (long long)K, (int)r);
+    return FRANK_ECUDA;
+  }
+  return FRANK_OK;
+}
+
+// 3-D bf16 map [E, N, K], box {64, 128, 1}, 128-B swizzle.
+int make_map_3d(CUtensorMap* m, const void* base, int64_t E, int64_t N, int64_t K) {
+  auto enc = get_encode();
+  if (!enc) {
+    frank::set_error("cuTensorMapEncodeTiled unavailable");
+    return FRANK_ECUDA;
+  }
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)N, (cuuint64_t)E};
+  cuuint64_t strides[2] = {(cuuint64_t)K * 2, (cuuint64_t)N * K * 2};
+  cuuint32_t box[3] = {BK, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    frank::set_error("cuTensorMapEncodeTiled(3d E=%lld N=%lld K=%lld) failed: %d", (long long)E, (long long)N,
+                     (long long)K, (int)r);
+    return FRANK_ECUDA;
+  }
+  return FRANK_OK;
+}
+
+size_t smem_bytes(int E) { return 1024 + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 4) + 16 + 4 * (E + 1) + 64; }
+
+}  // namespace
+
+namespace frank {
+
+// Constraints checked here: K % 8 == 0 (16-byte TMA strides), N_out % 16 == 0,
+// 16-byte aligned base pointers, rows and E*N within int32 coordinates.
+int check_tc_shapes(int64_t rows, int64_t N, int64_t K, int64_t E) {
+  if (K % 8 != 0 || K <= 0) {
+    set_error("bf16 tensor-core path needs n_in %% 8 == 0 (got %lld)", (long long)K);
+    return FRANK_EINVAL;
+  }
+  if (N % 16 != 0 || N <= 0) {
+    set_error("bf16 tensor-core path needs n_out %% 16 == 0 (got %lld)", (long long)N);
+    return FRANK_EINVAL;
+  }
+  if (E > kMaxExperts || rows > 0x7fffffffLL || N > 0x7fffffffLL) {
+    set_error("bf16 tensor-core path: E=%lld rows=%lld N=%lld out of range", (long long)E, (long long)rows,
+              (long long)N);
+    return FRANK_EINVAL;
+  }
+  return FRANK_OK;
+}
+
+// mode: 0 SWIGLU (B = gate, B2 = up, out bf16 [rows, N]), 1 SCALE, 2 PLAIN
+// (out fp32 [rows, N]).  A: bf16 [rows, K]; B/B2: bf16 [E, N, K].
+int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B2, const int32_t* offsets, int64_t E,
+                           int64_t rows, int64_t N, int64_t K, const float* wrow, void* out, cudaStream_t st) {
+  if (rows == 0) return FRANK_OK;
+  FRANK_TRY(check_tc_shapes(rows, N, K, E));
+  if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)(B2 ? B2 : B) | (uintptr_t)out) % 16 != 0) {
+    set_error("bf16 tensor-core path needs 16-byte aligned buffers");
+    return FRANK_EINVAL;
+  }
+  CUtensorMap ma, mb, mb2;
+  FRANK_TRY(make_map_2d(&ma, A, rows, K));
+  FRANK_TRY(make_map_3d(&mb, B, E, N, K));
+  if (mode == SWIGLU) FRANK_TRY(make_map_3d(&mb2, B2, E, N, K));
+  else mb2 = mb;
+  Params p;
+  p.offsets = offsets;
+  p.E = (int)E;
+  p.n_tiles = (int)(mode == SWIGLU ? (N + 127) / 128 : (N + BN - 1) / BN);
+  p.N_out = (int)N;
+  p.K = (int)K;
+  p.out = out;
+  p.ldo = N;
+  p.wrow = wrow;
+  p.err = device_error_word();
+  size_t smem = smem_bytes((int)E);
+  dim3 grid(num_sms()), block(THREADS);
+  switch (mode) {
+    case SWIGLU:
+      FRANK_CUDA_TRY(cudaFuncSetAttribute(tc_grouped_gemm_kernel<SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+      tc_grouped_gemm_kernel<SWIGLU><<<grid, block, smem, st>>>(ma, mb, mb2, p);
+      break;
+    case SCALE:
+      FRANK_CUDA_TRY(cudaFuncSetAttribute(tc_grouped_gemm_kernel<SCALE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+      tc_grouped_gemm_kernel<SCALE><<<grid, block, smem, st>>>(ma, mb, mb2, p);
+      break;
+    default:
+      FRANK_CUDA_TRY(cudaFuncSetAttribute(tc_grouped_gemm_kernel<PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+      tc_grouped_gemm_kernel<PLAIN><<<grid, block, smem, st>>>(ma, mb, mb2, p);
+  }
+  FRANK_LAUNCH_CHECK();
+  return FRANK_OK;
+}
+
+}  // namespace frank

@@ -1,0 +1,339 @@
+// Routing kernels: router logits + softmax + top-k (+ renorm), and the
+// atomic-free stable expert permutation.
+//
+// Reference semantics:
+//   router matmul        components/moe/moe_ffn_block.mlir:54-70, oracles/moe.py:87
+//   softmax over experts moe_ffn_block.mlir:72-75, oracles/moe.py:90-91
+//   top-k (ogt, desc.)   moe_ffn_block.mlir:77-89, oracles/moe.py:95-100
+//   renormalisation      moe_ffn_block.mlir:91-128, oracles/moe.py:103-105
+//   slot flattening      components/moe/mul_mat_id.mlir:51-53 (s = j*T + t)
+#include "common.cuh"
+
+namespace {
+
+constexpr int kMaxE = 256;        // experts handled by the router
+constexpr int kMaxK = 32;         // top-k bound
+constexpr int kRouterTok = 32;    // tokens per router block
+constexpr int kRouterHc = 32;     // H chunk staged in shared memory
+constexpr int kRouterThreads = 256;
+
+// One warp: softmax over E logits held in shared memory (stride 1), then k
+// rounds of arg-max.  Ties resolve to the lowest expert index.  Lane l owns
+// experts l, l+32, ...
+__device__ void warp_softmax_topk(const float* lg, int E, int k, int normalize,
+                                  float* w_out, int32_t* id_out, int64_t T, int64_t t) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kPer = kMaxE / 32;
+  float p[kPer];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    int e = lane + 32 * i;
+    p[i] = (e < E) ? lg[e] : -INFINITY;
+    mx = fmaxf(mx, p[i]);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  float sum = 0.f;
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    int e = lane + 32 * i;
+    p[i] = (e < E) ? expf(p[i] - mx) : 0.f;
+    sum += p[i];
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    int e = lane + 32 * i;
+    p[i] = (e < E) ? p[i] / sum : -1.f;  // probabilities are >= 0; -1 marks "absent"
+  }
+  float chosen[kMaxK];
+  float wsum = 0.f;
+  for (int j = 0; j < k; ++j) {
+    // lane-local best (lowest index on ties: scan ascending, strict >)
+    float bv = -2.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      if (p[i] > bv) { bv = p[i]; bi = lane + 32 * i; }
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    // remove the winner from its owner lane
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (lane + 32 * i == bi) p[i] = -2.f;
+    chosen[j] = bv;
+    wsum += bv;  // ascending j, as numpy's sum over a short axis
+    if (lane == 0) id_out[(int64_t)j * T + t] = bi;
+  }
+  if (lane == 0) {
+    for (int j = 0; j < k; ++j)
+      w_out[(int64_t)j * T + t] = normalize ? chosen[j] / wsum : chosen[j];
+  }
+}
+
+__global__ void softmax_topk_kernel(const float* __restrict__ logits, int64_t T, int E, int k,
+                                    int normalize, float* __restrict__ w, int32_t* __restrict__ ids) {
+  __shared__ float lg[8][kMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int64_t t = (int64_t)blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  for (int e = lane; e < E; e += 32) lg[warp][e] = logits[(int64_t)e * T + t];
+  __syncwarp();
+  warp_softmax_topk(lg[warp], E, k, normalize, w, ids, T, t);
+}
+
+// Router: a block handles kRouterTok tokens.  x and wr are staged through
+// shared memory in H chunks (converted to fp32); every thread accumulates a
+// few (expert, token) logits in fp32 in ascending h order.
+template <class TX, class TW>
+__global__ void __launch_bounds__(kRouterThreads)
+router_topk_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int64_t H, int E,
+                   int k, int normalize, float* __restrict__ w, int32_t* __restrict__ ids) {
+  extern __shared__ float sm[];
+  float* xs = sm;                                  // [kRouterTok][kRouterHc+1]
+  float* ws = xs + kRouterTok * (kRouterHc + 1);   // [E][kRouterHc+1]
+  float* lg = ws + E * (kRouterHc + 1);            // [kRouterTok][E]
+  const int tid = threadIdx.x;
+  const int64_t t0 = (int64_t)blockIdx.x * kRouterTok;
+  const int nout = E * kRouterTok;                 // outputs of this block
+  const int per = (nout + kRouterThreads - 1) / kRouterThreads;  // <= 32
+  constexpr int kAcc = kMaxE * kRouterTok / kRouterThreads;
+  float acc[kAcc];
+#pragma unroll
+  for (int i = 0; i < kAcc; ++i) acc[i] = 0.f;
+  for (int64_t h0 = 0; h0 < H; h0 += kRouterHc) {
+    for (int i = tid; i < kRouterTok * kRouterHc; i += kRouterThreads) {
+      int r = i / kRouterHc, c = i % kRouterHc;
+      int64_t t = t0 + r, h = h0 + c;
+      xs[r * (kRouterHc + 1) + c] = (t < T && h < H) ? load_as_f32(x, t * H + h) : 0.f;
+    }
+    for (int i = tid; i < E * kRouterHc; i += kRouterThreads) {
+      int r = i / kRouterHc, c = i % kRouterHc;
+      int64_t h = h0 + c;
+      ws[r * (kRouterHc + 1) + c] = (h < H) ? load_as_f32(wr, (int64_t)r * H + h) : 0.f;
+    }
+    __syncthreads();
+    int hc = (H - h0) < kRouterHc ? (int)(H - h0) : kRouterHc;
+#pragma unroll
+    for (int i = 0; i < kAcc; ++i) {
+      int o = tid + i * kRouterThreads;
+      if (i < per && o < nout) {
+        int tt = o % kRouterTok, e = o / kRouterTok;
+        const float* xr = xs + tt * (kRouterHc + 1);
+        const float* wrow = ws + e * (kRouterHc + 1);
+        float a = acc[i];
+        for (int c = 0; c < hc; ++c) a = fmaf(wrow[c], xr[c], a);
+        acc[i] = a;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < kAcc; ++i) {
+    int o = tid + i * kRouterThreads;
+    if (i < per && o < nout) {
+      int tt = o % kRouterTok, e = o / kRouterTok;
+      lg[tt * E + e] = acc[i];
+    }
+  }
+  __syncthreads();
+  const int warp = tid >> 5;
+  for (int tt = warp; tt < kRouterTok; tt += kRouterThreads / 32) {
+    int64_t t = t0 + tt;
+    if (t < T) warp_softmax_topk(lg + tt * E, E, k, normalize, w, ids, T, t);
+  }
+}
+
+// ---------------------------------------------------------------- permute --
+// Three passes, no atomics:
+//  A) per chunk of kChunk slots: stable local rank of each slot among the
+//     chunk's slots of the same expert, and the chunk's per-expert counts;
+//  B) one block: per-(chunk, expert) base rows and the expert offsets;
+//  C) scatter: pos = base[chunk][e] + local_rank.
+constexpr int kPermThreads = 256;
+constexpr int kChunk = 1024;
+constexpr int kPermMaxE = 1024;
+
+__global__ void __launch_bounds__(kPermThreads)
+permute_rank_kernel(const int32_t* __restrict__ ids, int64_t n, int E, int32_t* __restrict__ local_rank,
+                    int32_t* __restrict__ chunk_counts, int32_t* __restrict__ err) {
+  __shared__ int32_t running[kPermMaxE];
+  __shared__ int32_t warp_cnt[kPermThreads / 32][kPermMaxE];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E; e += kPermThreads) {
+    running[e] = 0;
+    for (int w = 0; w < kPermThreads / 32; ++w) warp_cnt[w][e] = 0;
+  }
+  __syncthreads();
+  const int64_t c0 = (int64_t)blockIdx.x * kChunk;
+  for (int base = 0; base < kChunk; base += kPermThreads) {
+    int64_t s = c0 + base + tid;
+    int e = -1;
+    if (s < n) {
+      e = ids[s];
+      if (e < 0 || e >= E) {
+        if (err) *err = 1;
+        e = e < 0 ? 0 : E - 1;
+      }
+    }
+    unsigned peers = __match_any_sync(0xffffffffu, e);
+    int rank_w = __popc(peers & ((1u << lane) - 1u));
+    int leader = __ffs(peers) - 1;
+    if (e >= 0 && lane == leader) warp_cnt[warp][e] = __popc(peers);
+    __syncthreads();
+    int pos = 0;
+    bool last = false;
+    if (e >= 0) {
+      int before = 0;
+      for (int w = 0; w < warp; ++w) before += warp_cnt[w][e];
+      pos = running[e] + before + rank_w;
+      local_rank[s] = pos;
+      bool last_in_warp = (lane == 31 - __clz(peers));
+      last = last_in_warp;
+      for (int w = warp + 1; w < kPermThreads / 32 && last; ++w)
+        if (warp_cnt[w][e] != 0) last = false;
+    }
+    __syncthreads();
+    if (last) running[e] = pos + 1;
+    if (e >= 0 && lane == leader) warp_cnt[warp][e] = 0;
+    __syncthreads();
+  }
+  for (int e = tid; e < E; e += kPermThreads) chunk_counts[(int64_t)blockIdx.x * E + e] = running[e];
+}
+
+// chunk_counts[nc][E] -> chunk_base[nc][E] (absolute rows), offsets[E+1].
+__global__ void __launch_bounds__(1024)
+permute_scan_kernel(const int32_t* __restrict__ chunk_counts, int nc, int E,
+                    int32_t* __restrict__ chunk_base, int32_t* __restrict__ offsets) {
+  __shared__ int32_t tot[kPermMaxE];
+  __shared__ int32_t warp_sums[32];
+  const int e = threadIdx.x;
+  int32_t run = 0;
+  if (e < E) {
+    for (int c = 0; c < nc; ++c) {
+      chunk_base[(int64_t)c * E + e] = run;
+      run += chunk_counts[(int64_t)c * E + e];
+    }
+  }
+  tot[e] = (e < E) ? run : 0;
+  __syncthreads();
+  // exclusive scan of tot over the block (1024 threads)
+  const int lane = e & 31, warp = e >> 5;
+  int v = tot[e];
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int ws = warp_sums[lane];
+    int wi = ws;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      int u = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += u;
+    }
+    warp_sums[lane] = wi - ws;
+  }
+  __syncthreads();
+  int excl = warp_sums[warp] + incl - v;
+  if (e < E) {
+    offsets[e] = excl;
+    if (e == E - 1) offsets[E] = excl + v;
+    for (int c = 0; c < nc; ++c) chunk_base[(int64_t)c * E + e] += excl;
+  }
+}
+
+__global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int64_t n, int E,
+                                       const int32_t* __restrict__ local_rank,
+                                       const int32_t* __restrict__ chunk_base,
+                                       int32_t* __restrict__ sorted_slots,
+                                       int32_t* __restrict__ slot_pos) {
+  int64_t s = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= n) return;
+  int e = ids[s];
+  e = e < 0 ? 0 : (e >= E ? E - 1 : e);
+  int64_t c = s / kChunk;
+  int32_t pos = chunk_base[c * E + e] + local_rank[s];
+  sorted_slots[pos] = (int32_t)s;
+  if (slot_pos) slot_pos[s] = pos;
+}
+
+}  // namespace
+
+namespace frank {
+
+int launch_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k, int normalize,
+                        float* w, int32_t* ids, cudaStream_t st) {
+  if (T == 0) return FRANK_OK;
+  softmax_topk_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(logits, T, (int)E, (int)k, normalize, w, ids);
+  FRANK_LAUNCH_CHECK();
+  return FRANK_OK;
+}
+
+int launch_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H,
+                       int64_t E, int64_t k, int normalize, float* w, int32_t* ids, cudaStream_t st) {
+  if (T == 0) return FRANK_OK;
+  size_t smem = sizeof(float) * (kRouterTok * (kRouterHc + 1) + E * (kRouterHc + 1) + kRouterTok * E);
+  dim3 grid((unsigned)((T + kRouterTok - 1) / kRouterTok));
+#define FRANK_ROUTER_CASE(TX, TW)                                                                 \
+  {                                                                                               \
+    auto kern = router_topk_kernel<TX, TW>;                                                       \
+    FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+    kern<<<grid, kRouterThreads, smem, st>>>((const TX*)x, (const TW*)wr, T, H, (int)E, (int)k,   \
+                                             normalize, w, ids);                                  \
+  }
+  if (x_dtype == FRANK_F32 && wr_dtype == FRANK_F32) FRANK_ROUTER_CASE(float, float)
+  else if (x_dtype == FRANK_F32) FRANK_ROUTER_CASE(float, __nv_bfloat16)
+  else if (wr_dtype == FRANK_F32) FRANK_ROUTER_CASE(__nv_bfloat16, float)
+  else FRANK_ROUTER_CASE(__nv_bfloat16, __nv_bfloat16)
+#undef FRANK_ROUTER_CASE
+  FRANK_LAUNCH_CHECK();
+  return FRANK_OK;
+}
+
+size_t permute_workspace_size(int64_t n, int64_t E) {
+  int64_t nc = (n + kChunk - 1) / kChunk;
+  return align_up(n * 4, 256) + 2 * align_up(nc * E * 4, 256) + 256;
+}
+
+int launch_permute(const int32_t* ids, int64_t n, int64_t E, int32_t* sorted_slots, int32_t* offsets,
+                   int32_t* slot_pos, int32_t* err, void* ws, size_t ws_bytes, cudaStream_t st) {
+  if (E < 1 || E > kPermMaxE) {
+    set_error("permute: E=%lld outside [1, %d]", (long long)E, kPermMaxE);
+    return FRANK_EINVAL;
+  }
+  if (ws_bytes < permute_workspace_size(n, E)) {
+    set_error("permute: workspace %zu < %zu bytes", ws_bytes, permute_workspace_size(n, E));
+    return FRANK_ENOSPC;
+  }
+  if (n == 0) {
+    FRANK_CUDA_TRY(cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int32_t), st));
+    return FRANK_OK;
+  }
+  int64_t nc = (n + kChunk - 1) / kChunk;
+  Carve c(ws, ws_bytes);
+  int32_t* local_rank = c.take<int32_t>(n);
+  int32_t* counts = c.take<int32_t>(nc * E);
+  int32_t* base = c.take<int32_t>(nc * E);
+  permute_rank_kernel<<<(unsigned)nc, kPermThreads, 0, st>>>(ids, n, (int)E, local_rank, counts, err);
+  FRANK_LAUNCH_CHECK();
+  permute_scan_kernel<<<1, 1024, 0, st>>>(counts, (int)nc, (int)E, base, offsets);
+  FRANK_LAUNCH_CHECK();
+  permute_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ids, n, (int)E, local_rank, base,
+                                                                       sorted_slots, slot_pos);
+  FRANK_LAUNCH_CHECK();
+  return FRANK_OK;
+}
+
+}  // namespace frank

@@ -1,0 +1,267 @@
+"""Thin, typed wrappers over the C ABI that take and return torch tensors.
+
+Every function launches on the current torch CUDA stream and returns
+without synchronising.  Buffers (outputs and workspaces) are allocated here
+with torch and handed to the library, which never allocates.
+"""
+
+from __future__ import annotations
+
+from collections import OrderedDict
+
+import torch
+
+from . import _lib
+
+_DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+
+
+def _dt(t: torch.Tensor) -> int:
+    try:
+        return _DT[t.dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {t.dtype}; expected float32 or bfloat16") from None
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else t.data_ptr()
+
+
+def _cuda_contig(t: torch.Tensor, name: str) -> torch.Tensor:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name}: expected a torch.Tensor, got {type(t).__name__}")
+    if not t.is_cuda:
+        raise ValueError(f"{name}: tensor must be on a CUDA device")
+    return t.contiguous()
+
+
+def num_sms() -> int:
+    return _lib.load().frank_num_sms()
+
+
+def swiglu(gate: torch.Tensor, up: torch.Tensor) -> torch.Tensor:
+    """gate * silu(up) (components/activation/swiglu.mlir:16-51)."""
+    gate = _cuda_contig(gate, "gate")
+    up = _cuda_contig(up, "up")
+    if gate.shape != up.shape or gate.dtype != up.dtype:
+        raise ValueError(f"swiglu: gate {tuple(gate.shape)}/{gate.dtype} vs up {tuple(up.shape)}/{up.dtype}")
+    out = torch.empty_like(gate)
+    _lib.check(_lib.load().frank_swiglu(_dt(gate), _ptr(gate), _ptr(up), _ptr(out), gate.numel(), _stream()))
+    return out
+
+
+def softmax_topk(logits: torch.Tensor, k: int, normalize: bool):
+    """Softmax over experts + top-k from fp32 logits [E, T] -> (w [k,T] f32, ids [k,T] i32)."""
+    logits = _cuda_contig(logits, "logits")
+    if logits.dtype != torch.float32 or logits.dim() != 2:
+        raise ValueError("softmax_topk: logits must be fp32 [E, T]")
+    E, T = logits.shape
+    w = torch.empty((k, T), dtype=torch.float32, device=logits.device)
+    ids = torch.empty((k, T), dtype=torch.int32, device=logits.device)
+    _lib.check(_lib.load().frank_softmax_topk(_ptr(logits), T, E, k, int(bool(normalize)), _ptr(w), _ptr(ids),
+                                              _stream()))
+    return w, ids
+
+
+def router_topk(x: torch.Tensor, wr: torch.Tensor, k: int, normalize: bool):
+    """Router logits + softmax + top-k (+ renorm) -> (w [k,T] f32, ids [k,T] i32)."""
+    x = _cuda_contig(x, "x")
+    wr = _cuda_contig(wr, "wr")
+    T, H = x.shape
+    E = wr.shape[0]
+    if wr.shape[1] != H:
+        raise ValueError(f"router_topk: wr {tuple(wr.shape)} does not match n_embd={H}")
+    w = torch.empty((k, T), dtype=torch.float32, device=x.device)
+    ids = torch.empty((k, T), dtype=torch.int32, device=x.device)
+    _lib.check(_lib.load().frank_router_topk(_dt(x), _ptr(x), _dt(wr), _ptr(wr), T, H, E, k, int(bool(normalize)),
+                                             _ptr(w), _ptr(ids), _stream()))
+    return w, ids
+
+
+def permute(ids: torch.Tensor, n_expert: int):
+    """Stable expert permutation of ids [k, T] -> (sorted_slots, offsets, slot_pos, err_flag)."""
+    ids = _cuda_contig(ids, "ids")
+    if ids.dtype != torch.int32:
+        raise TypeError("permute: ids must be int32")
+    n = ids.numel()
+    lib = _lib.load()
+    dev = ids.device
+    sorted_slots = torch.empty(n, dtype=torch.int32, device=dev)
+    offsets = torch.empty(n_expert + 1, dtype=torch.int32, device=dev)
+    slot_pos = torch.empty(n, dtype=torch.int32, device=dev)
+    err = torch.zeros(1, dtype=torch.int32, device=dev)
+    ws_bytes = lib.frank_permute_workspace_size(n, n_expert)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    _lib.check(lib.frank_permute(_ptr(ids), n, n_expert, _ptr(sorted_slots), _ptr(offsets), _ptr(slot_pos),
+                                 _ptr(err), _ptr(ws), ws_bytes, _stream()))
+    return sorted_slots, offsets, slot_pos, err
+
+
+def prepack_experts(w_oie: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+    """[O, I, E] expert-innermost weights -> packed [E, O, I] in out_dtype."""
+    w_oie = _cuda_contig(w_oie, "weights")
+    if w_oie.dim() != 3:
+        raise ValueError("prepack_experts: weights must be 3-D [n_out, n_in, n_expert]")
+    O, I, E = w_oie.shape
+    out = torch.empty((E, O, I), dtype=out_dtype, device=w_oie.device)
+    _lib.check(_lib.load().frank_prepack_experts(_dt(w_oie), _ptr(w_oie), O, I, E, _DT[out_dtype], _ptr(out),
+                                                 _stream()))
+    return out
+
+
+class PackedExperts:
+    """Expert weights already in the packed [E, O, I] layout."""
+
+    def __init__(self, packed: torch.Tensor):
+        if packed.dim() != 3:
+            raise ValueError("PackedExperts: expected [E, O, I]")
+        self.packed = packed.contiguous()
+
+    @classmethod
+    def from_reference(cls, w_oie: torch.Tensor, dtype: torch.dtype) -> "PackedExperts":
+        return cls(prepack_experts(w_oie, dtype))
+
+    @property
+    def n_expert(self):
+        return self.packed.shape[0]
+
+    @property
+    def n_out(self):
+        return self.packed.shape[1]
+
+    @property
+    def n_in(self):
+        return self.packed.shape[2]
+
+
+class _PackCache:
+    """Prepacked weights keyed by (storage pointer, version, shape, dtypes):
+    a weight tensor is packed once and reused until it is modified.  Each
+    entry keeps its source tensor alive so that its address cannot be reused
+    by another tensor while the entry exists."""
+
+    def __init__(self, capacity: int = 24):
+        self.cap = capacity
+        self.d: OrderedDict = OrderedDict()
+
+    def get(self, w: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+        key = (w.data_ptr(), w._version, tuple(w.shape), tuple(w.stride()), w.dtype, dtype, w.device)
+        hit = self.d.get(key)
+        if hit is not None:
+            self.d.move_to_end(key)
+            return hit[1]
+        p = prepack_experts(w, dtype)
+        self.d[key] = (w, p)
+        if len(self.d) > self.cap:
+            self.d.popitem(last=False)
+        return p
+
+
+PACK_CACHE = _PackCache()
+
+
+def _packed(w, dtype: torch.dtype, name: str) -> torch.Tensor:
+    if isinstance(w, PackedExperts):
+        if w.packed.dtype != dtype:
+            raise TypeError(f"{name}: packed dtype {w.packed.dtype} != compute dtype {dtype}")
+        return w.packed
+    return PACK_CACHE.get(_cuda_contig(w, name), dtype)
+
+
+def mul_mat_id(weights, inp: torch.Tensor, ids: torch.Tensor, check_ids: bool = True) -> torch.Tensor:
+    """Expert-selected matmul (components/moe/mul_mat_id.mlir:22-120).
+
+    weights: [O, I, E] (reference layout) or PackedExperts; inp [I, k, T];
+    ids [k, T] int32.  Returns fp32 [O, k, T].  fp32 inputs run the FFMA
+    path; bf16 inputs the tcgen05 path.  With check_ids, out-of-range ids
+    raise FrankError(EIDS) (this synchronises the stream).
+    """
+    inp = _cuda_contig(inp, "input")
+    ids = _cuda_contig(ids, "ids")
+    dtype = inp.dtype
+    wp = _packed(weights, dtype, "weights")
+    E, O, I = wp.shape
+    if inp.dim() != 3 or inp.shape[0] != I:
+        raise ValueError(f"mul_mat_id: input {tuple(inp.shape)} does not match n_in={I}")
+    k, T = inp.shape[1], inp.shape[2]
+    if tuple(ids.shape) != (k, T) or ids.dtype != torch.int32:
+        raise ValueError(f"mul_mat_id: ids must be int32 [{k}, {T}], got {tuple(ids.shape)} {ids.dtype}")
+    lib = _lib.load()
+    out = torch.empty((O, k, T), dtype=torch.float32, device=inp.device)
+    err = torch.zeros(1, dtype=torch.int32, device=inp.device)
+    ws_bytes = lib.frank_mul_mat_id_workspace_size(_dt(inp), O, I, E, k, T)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=inp.device)
+    _lib.check(lib.frank_mul_mat_id(_dt(inp), _ptr(wp), _ptr(inp), _ptr(ids), O, I, E, k, T, _ptr(out), _ptr(err),
+                                    _ptr(ws), ws_bytes, _stream()))
+    if check_ids and int(err.item()) != 0:
+        raise _lib.FrankError(_lib.EIDS, f"mul_mat_id: an expert id is outside [0, {E})")
+    return out
+
+
+class MoEFFNBlock:
+    """The MoE FFN block with weights packed once and a reusable workspace.
+
+    Mirrors @moe_ffn_components.moe_ffn_block (moe_ffn_block.mlir:34-209):
+    the weights are given in the reference layouts (router [E, H], up/gate
+    [F, H, E], down [H, F, E]) and packed at construction.
+    """
+
+    def __init__(self, gate_inp_w, up_exps_w, gate_exps_w, down_exps_w, n_expert: int, n_expert_used: int,
+                 normalize_weights: bool, dtype: torch.dtype = torch.bfloat16):
+        if dtype not in _DT:
+            raise TypeError(f"MoEFFNBlock: unsupported compute dtype {dtype}")
+        self.dtype = dtype
+        self.E = int(n_expert)
+        self.k = int(n_expert_used)
+        self.normalize = bool(normalize_weights)
+        self.wr = _cuda_contig(gate_inp_w, "gate_inp_w")
+        self.w_up = _packed(up_exps_w, dtype, "up_exps_w")
+        self.w_gate = _packed(gate_exps_w, dtype, "gate_exps_w")
+        self.w_down = _packed(down_exps_w, dtype, "down_exps_w")
+        E, F, H = self.w_up.shape
+        if E != self.E or tuple(self.w_gate.shape) != (E, F, H) or tuple(self.w_down.shape) != (E, H, F):
+            raise ValueError("MoEFFNBlock: expert weight shapes disagree")
+        if tuple(self.wr.shape) != (E, H):
+            raise ValueError(f"MoEFFNBlock: gate_inp_w {tuple(self.wr.shape)} != [{E}, {H}]")
+        self.H, self.F = H, F
+        self._ws = None
+
+    def workspace_bytes(self, T: int) -> int:
+        return _lib.load().frank_moe_ffn_block_workspace_size(_DT[self.dtype], T, self.H, self.F, self.E, self.k)
+
+    def _workspace(self, T: int, device) -> torch.Tensor:
+        need = self.workspace_bytes(T)
+        if self._ws is None or self._ws.numel() < need or self._ws.device != device:
+            self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+        return self._ws
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, return_routing: bool = False):
+        x = _cuda_contig(x, "input")
+        if x.dtype != self.dtype or x.dim() != 2 or x.shape[1] != self.H:
+            raise ValueError(f"moe_ffn_block: input must be {self.dtype} [T, {self.H}], got {x.dtype} "
+                             f"{tuple(x.shape)}")
+        T = x.shape[0]
+        y = out if out is not None else torch.empty((T, self.H), dtype=self.dtype, device=x.device)
+        rw = torch.empty((self.k, T), dtype=torch.float32, device=x.device) if return_routing else None
+        rid = torch.empty((self.k, T), dtype=torch.int32, device=x.device) if return_routing else None
+        ws = self._workspace(T, x.device)
+        _lib.check(_lib.load().frank_moe_ffn_block(
+            _DT[self.dtype], _ptr(x), _dt(self.wr), _ptr(self.wr), _ptr(self.w_up), _ptr(self.w_gate),
+            _ptr(self.w_down), T, self.E, self.k, self.H, self.F, int(self.normalize), _ptr(y), _ptr(rw), _ptr(rid),
+            _ptr(ws), ws.numel(), _stream()))
+        if return_routing:
+            return y, rw, rid
+        return y
+
+
+def read_device_error() -> int:
+    """Return and clear the device error word of bounded in-kernel waits."""
+    import ctypes
+
+    v = ctypes.c_int32(0)
+    _lib.check(_lib.load().frank_read_device_error(ctypes.byref(v), _stream()))
+    return v.value

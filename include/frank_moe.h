@@ -1,0 +1,166 @@
+/*
+ * frank_moe.h -- C ABI of the B200 (sm_100a) MoE FFN hot path.
+ *
+ * This library replaces three IREE-compiled components of frank-models:
+ *   @moe_components.mul_mat_id      components/moe/mul_mat_id.mlir:22-120
+ *   @moe_ffn_components.moe_ffn_block components/moe/moe_ffn_block.mlir:34-209
+ *   @activation_components.swiglu   components/activation/swiglu.mlir:16-51
+ * which the reference reaches through its test harness
+ * (tests/utils.py:171-223, IREEModule.invoke / __getattr__) and, in MLIR,
+ * from architectures/llm/transformer_layer_moe_prefill.mlir:216-224 and
+ * transformer_layer_moe_decode.mlir:234-241.
+ *
+ * Conventions
+ *  - Every pointer is a DEVICE pointer unless stated otherwise; the caller
+ *    owns all buffers (inputs, outputs, workspace).  The library never
+ *    allocates device memory.
+ *  - Calls are asynchronous and ordered on the given CUDA stream
+ *    (cudaStream_t passed as void*; NULL = legacy default stream).
+ *  - Return 0 on success or a negative FRANK_E* code; frank_last_error()
+ *    returns a thread-local message for the last failure on this thread.
+ *  - Shapes follow the reference exactly:
+ *      x        [T, H]      row-major                 (moe_ffn_block.mlir:35)
+ *      wr       [E, H]      router weights            (moe_ffn_block.mlir:36)
+ *      W_up/gate[F, H, E]   expert-innermost          (moe_ffn_block.mlir:37-38)
+ *      W_down   [H, F, E]                             (moe_ffn_block.mlir:39)
+ *      mul_mat_id weights [O, I, E], input [I, k, T], ids [k, T] int32,
+ *      output [O, k, T]                               (mul_mat_id.mlir:23-26)
+ *    Expert weights are consumed in a prepacked [E, O, I] layout made once
+ *    by frank_prepack_experts (the reference re-transposes them on every
+ *    call, mul_mat_id.mlir:38-48).
+ */
+#ifndef FRANK_MOE_H_
+#define FRANK_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* element types */
+#define FRANK_F32 0
+#define FRANK_BF16 1
+
+/* status codes */
+#define FRANK_OK 0
+#define FRANK_EINVAL (-1)   /* bad shape / dtype / pointer / alignment */
+#define FRANK_EIDS (-2)     /* an expert id outside [0, E) */
+#define FRANK_ECUDA (-3)    /* a CUDA runtime or driver call failed */
+#define FRANK_ENOSPC (-4)   /* workspace smaller than *_workspace_size() */
+#define FRANK_ETIMEOUT (-5) /* a bounded device-side wait gave up */
+#define FRANK_ENCCL (-6)    /* reserved for the expert-parallel layer */
+
+/* Thread-local message describing the last failure on this thread. */
+const char* frank_last_error(void);
+
+/* ABI version of this library (major*100 + minor). */
+int frank_abi_version(void);
+
+/* Number of SMs of the current device (used to size persistent grids). */
+int frank_num_sms(void);
+
+/*
+ * out = gate * silu(up), silu(u) = u / (1 + exp(-u)), n elements.
+ * Replaces @activation_components.swiglu (swiglu.mlir:16-51; oracle
+ * oracles/activation.py:11-21).  dtype FRANK_F32 or FRANK_BF16 (all three
+ * buffers share it; bf16 computes in fp32).
+ */
+int frank_swiglu(int dtype, const void* gate, const void* up, void* out,
+                 int64_t n, void* stream);
+
+/*
+ * Softmax over experts then descending top-k, starting from fp32 logits
+ * [E, T] (moe_ffn_block.mlir:72-128, oracles/moe.py:90-105).
+ * Ties go to the lowest expert index.  Writes weights [k, T] fp32 and
+ * ids [k, T] int32.  Exported so routing can be tested bit-exactly on
+ * identical logits.
+ */
+int frank_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k,
+                       int normalize, float* weights, int32_t* ids,
+                       void* stream);
+
+/*
+ * Router: logits = wr @ x.T in fp32, then frank_softmax_topk's rule
+ * (moe_ffn_block.mlir:54-128, oracles/moe.py:87-105).
+ * x_dtype / wr_dtype: FRANK_F32 or FRANK_BF16.  E <= 256, 1 <= k <= min(E, 32).
+ */
+int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr,
+                      int64_t T, int64_t H, int64_t E, int64_t k, int normalize,
+                      float* weights, int32_t* ids, void* stream);
+
+/*
+ * Atomic-free, stable expert permutation of the flattened slots
+ * s = j*T + t (slot-major, mul_mat_id.mlir:51-53).  Equivalent to
+ * argsort(ids.reshape(-1), stable) and a bincount prefix:
+ *   sorted_slots[k*T]  flat slot at each expert-sorted row
+ *   offsets[E+1]       first sorted row of each expert
+ *   slot_pos[k*T]      sorted row of each flat slot
+ * workspace: frank_permute_workspace_size(k*T, E) bytes.  err_flag (device
+ * int32, may be NULL) receives 1 when an id is outside [0, E); such ids are
+ * clamped so that the call stays memory-safe.
+ */
+size_t frank_permute_workspace_size(int64_t n_slots, int64_t E);
+int frank_permute(const int32_t* ids, int64_t n_slots, int64_t E,
+                  int32_t* sorted_slots, int32_t* offsets, int32_t* slot_pos,
+                  int32_t* err_flag, void* workspace, size_t ws_bytes,
+                  void* stream);
+
+/*
+ * One-time weight prepack: [O, I, E] (expert innermost, in_dtype) ->
+ * [E, O, I] (out_dtype).  Replaces the per-call transpose of
+ * mul_mat_id.mlir:38-48.  FRANK_F32 -> FRANK_F32 or FRANK_BF16;
+ * FRANK_BF16 -> FRANK_BF16.
+ */
+int frank_prepack_experts(int in_dtype, const void* w_oie, int64_t O,
+                          int64_t I, int64_t E, int out_dtype, void* w_eoi,
+                          void* stream);
+
+/*
+ * Expert-selected matmul, @moe_components.mul_mat_id (mul_mat_id.mlir:22-120,
+ * oracles/moe.py:9-48):  out[:, j, t] = W[:, :, ids[j, t]] @ in[:, j, t].
+ *   dtype FRANK_F32: w_eoi fp32 [E,O,I], input fp32 [I,k,T]  (fp32 FFMA path)
+ *   dtype FRANK_BF16: w_eoi bf16 [E,O,I], input bf16 [I,k,T] (tcgen05 path)
+ * out is fp32 [O, k, T].  err_flag as in frank_permute (may be NULL).
+ */
+size_t frank_mul_mat_id_workspace_size(int dtype, int64_t O, int64_t I,
+                                       int64_t E, int64_t k, int64_t T);
+int frank_mul_mat_id(int dtype, const void* w_eoi, const void* input,
+                     const int32_t* ids, int64_t O, int64_t I, int64_t E,
+                     int64_t k, int64_t T, float* out, int32_t* err_flag,
+                     void* workspace, size_t ws_bytes, void* stream);
+
+/*
+ * Full MoE FFN block, @moe_ffn_components.moe_ffn_block
+ * (moe_ffn_block.mlir:34-209, oracles/moe.py:51-132):
+ *   route -> permute -> h = gate(x) * silu(up(x)) -> d = down(h) * w
+ *   -> y[t] = sum_j d[slot j of t]  (j = 0..k-1 in order).
+ *   dtype FRANK_F32 : x fp32 [T,H], packed weights fp32, y fp32 (FFMA path)
+ *   dtype FRANK_BF16: x bf16 [T,H], packed weights bf16, y bf16 (tcgen05
+ *                     path, fp32 accumulation)
+ * wr [E, H] is fp32 or bf16 (wr_dtype).  Packed weights:
+ *   w_up_p, w_gate_p [E, F, H]; w_down_p [E, H, F]  (frank_prepack_experts)
+ * Optional outputs (may be NULL): route_w [k,T] fp32, route_ids [k,T] int32.
+ */
+size_t frank_moe_ffn_block_workspace_size(int dtype, int64_t T, int64_t H,
+                                          int64_t F, int64_t E, int64_t k);
+int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr,
+                        const void* w_up_p, const void* w_gate_p,
+                        const void* w_down_p, int64_t T, int64_t E, int64_t k,
+                        int64_t H, int64_t F, int normalize, void* y,
+                        float* route_w, int32_t* route_ids, void* workspace,
+                        size_t ws_bytes, void* stream);
+
+/*
+ * Device error word written by bounded waits inside the persistent GEMM
+ * kernels (0 = none).  frank_read_device_error copies it to *out and resets
+ * it; synchronises the stream.
+ */
+int frank_read_device_error(int32_t* out, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FRANK_MOE_H_ */

@@ -1,0 +1,126 @@
+"""bf16 tensor-core (tcgen05) path vs the oracle.
+
+Reference values are the oracle evaluated in float64 on the same
+bf16-rounded inputs.  Tolerance: max-abs <= 2e-2 x output RMS for the block
+(bf16 h and y), tighter for mul_mat_id (fp32 output, only the accumulation
+order differs).  Routing is taken from the GPU for the block comparison so
+that near-tied tokens cannot swap experts between the two sides; routing
+itself is checked in test_routing_gpu.py.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from frank_b200 import configs, ops
+from oracle import moe_oracle as O
+from tests.utils import rms_rel_maxabs
+
+pytestmark = pytest.mark.gpu
+
+BLOCK_TOL = 2e-2
+MMID_TOL = 1e-3
+
+
+def _bf16(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda().bfloat16()
+
+
+def _f64(t):
+    return t.float().cpu().numpy().astype(np.float64)
+
+
+@pytest.mark.parametrize("O_,I,E,k,T,kind", [
+    (512, 256, 8, 2, 300, "uniform"),
+    (256, 128, 4, 1, 1, "uniform"),        # one token
+    (144, 72, 6, 2, 129, "one"),           # ragged N (144 % 256 != 0), K % 64 != 0, all on one expert
+    (256, 64, 16, 4, 200, "sparse"),       # empty experts
+    (1024, 512, 8, 2, 1000, "uniform"),
+])
+def test_mul_mat_id_bf16(O_, I, E, k, T, kind):
+    rng = np.random.default_rng(O_ + T)
+    w = (rng.standard_normal((O_, I, E)) * 0.05).astype(np.float32)
+    x = rng.standard_normal((I, k, T)).astype(np.float32)
+    if kind == "uniform":
+        ids = rng.integers(0, E, size=(k, T))
+    elif kind == "one":
+        ids = np.full((k, T), E // 2)
+    else:
+        ids = rng.choice([1, E - 1], size=(k, T))
+    ids = ids.astype(np.int32)
+    wb, xb = _bf16(w), _bf16(x)
+    out = ops.mul_mat_id(wb, xb, torch.from_numpy(ids).cuda())
+    ref = O.mul_mat_id_grouped(_f64(wb), _f64(xb), ids)
+    assert rms_rel_maxabs(out.cpu().numpy(), ref) <= MMID_TOL
+    assert ops.read_device_error() == 0
+
+
+def _block_check(cfg, seed):
+    x, wr, wu, wg, wd = configs.block_inputs_numpy(cfg, seed=seed)
+    xb = _bf16(x)
+    tb = [_bf16(w) for w in (wu, wg, wd)]
+    block = ops.MoEFFNBlock(torch.from_numpy(wr).cuda(), *tb, cfg.E, cfg.k, cfg.normalize)
+    y, rw, rid = block(xb, return_routing=True)
+    ref = O.moe_ffn_block_grouped(_f64(xb), wr.astype(np.float64), *(_f64(t) for t in tb), cfg.E, cfg.k, cfg.H,
+                                  cfg.F, cfg.normalize, routing=(rw.cpu().numpy().astype(np.float64),
+                                                                 rid.cpu().numpy()))
+    err = rms_rel_maxabs(y.float().cpu().numpy(), ref)
+    assert err <= BLOCK_TOL, f"{cfg.name}: max-abs/rms {err:.3e}"
+    # the GPU's routing equals the oracle's on the same logits except near ties
+    logits = wr.astype(np.float64) @ _f64(xb).T
+    _, oids = O.route_from_logits(logits, cfg.k, cfg.normalize)
+    agree = np.all(oids == rid.cpu().numpy(), axis=0).mean()
+    assert agree >= 0.99
+    assert ops.read_device_error() == 0
+    return y
+
+
+@pytest.mark.parametrize("cfg", [
+    configs.BlockConfig("bf16_small", T=200, H=256, F=384, E=8, k=2, normalize=True, dtype="bf16"),
+    configs.BlockConfig("bf16_fg", T=256, H=2048, F=768, E=128, k=8, normalize=False, dtype="bf16"),
+    configs.BlockConfig("bf16_zipf", T=512, H=512, F=256, E=128, k=8, normalize=False, dtype="bf16", zipf=1.2),
+    configs.c5(1), configs.c5(8), configs.c5(32), configs.c5(64),
+], ids=lambda c: c.name)
+def test_block_bf16(cfg):
+    _block_check(cfg, seed=0)
+
+
+def test_block_bf16_deterministic():
+    cfg = configs.BlockConfig("det", T=300, H=512, F=256, E=16, k=4, normalize=False, dtype="bf16")
+    x, wr, wu, wg, wd = configs.block_inputs_numpy(cfg, seed=2)
+    block = ops.MoEFFNBlock(torch.from_numpy(wr).cuda(), *(_bf16(w) for w in (wu, wg, wd)), cfg.E, cfg.k, False)
+    a = block(_bf16(x))
+    b = block(_bf16(x))
+    assert torch.equal(a, b)
+
+
+@pytest.mark.slow
+def test_mixtral_full_size_token_subset():
+    """C3 at full size (T=16384, H=4096, F=14336, E=8, k=2): a seeded subset of
+    256 tokens is recomputed in fp32 torch on the GPU (TF32 off) from the same
+    bf16 weights and routing."""
+    cfg = configs.C3
+    dev = torch.device("cuda")
+    wr, wu_p, wg_p, wd_p = configs.block_weights_packed_torch(cfg, dev, seed=0)
+    x = configs.block_x_torch(cfg, dev, seed=0)
+    block = ops.MoEFFNBlock(wr, ops.PackedExperts(wu_p), ops.PackedExperts(wg_p), ops.PackedExperts(wd_p), cfg.E,
+                            cfg.k, cfg.normalize)
+    y, rw, rid = block(x, return_routing=True)
+    torch.backends.cuda.matmul.allow_tf32 = False
+    sel = torch.from_numpy(np.random.default_rng(0).choice(cfg.T, 256, replace=False)).to(dev)
+    xs = x[sel].float()
+    ref = torch.zeros((256, cfg.H), dtype=torch.float32, device=dev)
+    for j in range(cfg.k):
+        for e in range(cfg.E):
+            m = rid[j, sel] == e
+            if not bool(m.any()):
+                continue
+            xe = xs[m]
+            g = xe @ wg_p[e].float().T
+            u = xe @ wu_p[e].float().T
+            h = (g * (u / (1 + torch.exp(-u)))).bfloat16().float()  # kernel stores h in bf16
+            ref[m] += (h @ wd_p[e].float().T) * rw[j, sel][m][:, None]
+    got = y[sel].float()
+    err = (got - ref).abs().max().item() / ref.pow(2).mean().sqrt().item()
+    assert err <= BLOCK_TOL
+    assert ops.read_device_error() == 0
