@@ -1,0 +1,360 @@
+"""Benchmark of the MoE FFN block (the ``moe_ffn_block`` hot path).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config c3] [--impl frank|reference]
+
+One step = one ``moe_ffn_block`` call over one batch of synthetic tokens.
+At N=1 the workload is the Mixtral-8x7B block (T=16384, H=4096, F=14336,
+E=8, top-2, bf16, fp32 accumulation).  With N>1 (launched by torchrun, one
+process per GPU, NCCL) every rank holds T tokens and E/N experts and the
+block runs expert-parallel: tokens are dispatched to the ranks owning their
+experts and the results combined back (weak scaling: T tokens per rank).
+
+Printed (rank 0, one JSON line):
+  value       tokens/s over all ranks, inputs resident in HBM, device-timed with
+              CUDA events, max over ranks
+  e2e         the same through the public API with the step's x copied from
+              pinned host memory and y copied back inside the timed region
+  roofline    the gate/up GEMM (dominant kernel): algorithmic flops per launch /
+              its CUDA-event duration inside the timed region, against the
+              measured dense bf16 peak
+  cpu_baseline the CPU restatement of the reference (NumPy, grouped form) on a
+              bounded token sample, rank 0 at N=1
+--impl reference times that CPU restatement alone (the reference is a NumPy
+oracle + IREE-compiled MLIR; IREE is not installable offline).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (REPO, REPO / "frank-models_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "moe_ffn_block tokens/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMM launch,
+# from the ncu capture summarised in profiles/ (None until captured).
+GATE_UP_TRAFFIC_BYTES = {"c3_mixtral_8x7b": None}
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return FALLBACK_PEAKS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = str(gpu_index)
+        try:
+            import torch
+
+            self.idx = "GPU-" + str(torch.cuda.get_device_properties(gpu_index).uuid)
+        except Exception:
+            pass
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in getattr(self, "lines", []):
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+
+        n = [i.get("num_threads") for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n and n[0]:
+            return int(n[0])
+    except Exception:
+        pass
+    return len(os.sched_getaffinity(0))
+
+
+# ----------------------------------------------------------------- CPU arm --
+def cpu_block_sample(cfg, x_f32, wr, w_up_p, w_gate_p, w_down_p, T_sample, reps=1):
+    """Time the oracle's grouped restatement on the first T_sample tokens.
+    Weights are packed [E, O, I] host arrays; the oracle reads them through
+    [O, I, E] views (no copy).  Returns seconds per call."""
+    from oracle import moe_oracle as O
+
+    xs = x_f32[:T_sample]
+    wu, wg, wd = (w.transpose(1, 2, 0) for w in (w_up_p, w_gate_p, w_down_p))
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        O.moe_ffn_block_grouped(xs, wr, wu, wg, wd, cfg.E, cfg.k, cfg.H, cfg.F, cfg.normalize)
+        times.append(time.perf_counter() - t0)
+    return min(times)
+
+
+def host_weights_numpy(cfg, seed=0):
+    import numpy as np
+
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((max(cfg.T, 1), cfg.H), dtype=np.float32)
+    wr = (rng.standard_normal((cfg.E, cfg.H), dtype=np.float32) * 0.02)
+    wg = rng.standard_normal((cfg.E, cfg.F, cfg.H), dtype=np.float32)
+    wg *= 0.02
+    wu = rng.standard_normal((cfg.E, cfg.F, cfg.H), dtype=np.float32)
+    wu *= 0.02
+    wd = rng.standard_normal((cfg.E, cfg.H, cfg.F), dtype=np.float32)
+    wd *= 0.02
+    return x, wr, wu, wg, wd
+
+
+def sample_tokens(cfg):
+    return min(cfg.T, 256 if cfg.T >= 4096 else cfg.T)
+
+
+def run_reference(args, cfg):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    x, wr, wu, wg, wd = host_weights_numpy(cfg)
+    Ts = sample_tokens(cfg)
+    for _ in range(args.warmup):
+        cpu_block_sample(cfg, x, wr, wu, wg, wd, Ts)
+    times = [cpu_block_sample(cfg, x, wr, wu, wg, wd, Ts) for _ in range(args.steps)]
+    sec = sum(times) / len(times)
+    v = Ts / sec
+    cores = cpu_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_dict(cfg, world),
+        "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
+                         "sample": f"{Ts} of {cfg.T} tokens per step, full H/F/E weights; the NumPy oracle's "
+                                   f"grouped restatement (oracle/moe_oracle.py) on {cores} BLAS threads"},
+        "e2e": {"value": v, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_dict(cfg, world):
+    return {"workload": cfg.name, "tokens_per_rank": cfg.T, "global_batch": cfg.T * world, "n_embd": cfg.H,
+            "n_ff": cfg.F, "n_expert": cfg.E, "n_expert_used": cfg.k, "normalize_weights": cfg.normalize,
+            "parallelism": f"ep{world}",
+            "l2": "inputs larger than L2: expert weights and per-step activations exceed the 126 MB L2"}
+
+
+# ----------------------------------------------------------------- GPU arm --
+def run_frank(args, cfg):
+    import numpy as np
+    import torch
+
+    from frank_b200 import configs, ops
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev)
+        from frank_b200 import ep
+
+        runner = ep.ExpertParallelMoE.synthetic(cfg, rank, world, dev, seed=0)
+        block_call = runner.__call__
+    else:
+        dist = None
+        wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, dev, seed=0)
+        block = ops.MoEFFNBlock(wr, ops.PackedExperts(wu), ops.PackedExperts(wg), ops.PackedExperts(wd), cfg.E,
+                                cfg.k, cfg.normalize, dtype=torch.bfloat16, out_dtype=torch.float32)
+        block_call = block.__call__
+    x = configs.block_x_torch(cfg, dev, seed=rank)
+    y = torch.empty((cfg.T, cfg.H), dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(v: float) -> float:
+        if dist is None:
+            return v
+        t = torch.tensor([v], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    for _ in range(args.warmup):
+        block_call(x, out=y)
+    barrier()
+
+    # ---- value: inputs resident in HBM -------------------------------------
+    ops.profile_stages(True)
+    l0 = ops.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            block_call(x, out=y)
+        ev1.record(stream)
+        barrier()
+    launches = ops.launch_count() - l0
+    ops.profile_stages(False)
+    stage_ms = ops.profile_read() if world == 1 else {}
+    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    value = cfg.T * world / (ms / 1e3)
+
+    # ---- e2e: host x in, host y out, through the public API ---------------
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((cfg.T, cfg.H), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+    for _ in range(min(args.warmup, 2)):
+        x_dev.copy_(x_host, non_blocking=True)
+        block_call(x_dev, out=y)
+        y_host.copy_(y, non_blocking=True)
+    barrier()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        x_dev.copy_(x_host, non_blocking=True)
+        block_call(x_dev, out=y)
+        y_host.copy_(y, non_blocking=True)
+    ev1.record(stream)
+    barrier()
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    e2e = {"value": cfg.T * world / (e2e_ms / 1e3), "unit": "tokens/s",
+           "h2d_bytes_per_step": x_host.numel() * x_host.element_size() * world,
+           "d2h_bytes_per_step": y_host.numel() * y_host.element_size() * world}
+
+    if rank != 0:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    pk, pk_kind = peaks()
+    line = {
+        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; no dataset)",
+        "config": config_dict(cfg, world),
+        "tflops": cfg.flops * world / (ms / 1e3) / 1e12,
+    }
+    if stage_ms:
+        gu_flops = 4.0 * cfg.k * cfg.T * cfg.H * cfg.F
+        gu_ms = stage_ms["gate_up_gemm"]
+        achieved = gu_flops / (gu_ms / 1e3) / 1e12
+        peak = float(pk["bf16_tflops_sustained"])
+        line["roofline"] = {
+            "kernel": "tc_grouped_gemm<SWIGLU> (gate/up GEMM + swiglu)", "bound": "tensor",
+            "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+            "peak_source": f"{pk_kind} bf16_tflops_sustained", "traffic": GATE_UP_TRAFFIC_BYTES.get(cfg.name),
+            "flops_per_launch": gu_flops, "ms_per_launch": gu_ms,
+        }
+        line["stage_ms"] = stage_ms
+        line["block_frac_of_peak"] = line["tflops"] / peak
+    line["e2e"] = e2e
+    line["gpu_launches"] = int(launches)
+    line["clocks"] = clk.summary()
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_from_device(cfg, x, block if world == 1 else None)
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def cpu_baseline_from_device(cfg, x, block):
+    """The oracle on the same weights (copied from the device) and the first
+    sample tokens, on all host BLAS threads."""
+    import numpy as np
+
+    Ts = sample_tokens(cfg)
+    xs = x[:Ts].float().cpu().numpy()
+    wr = block.wr.float().cpu().numpy()
+    wu, wg, wd = (t.float().cpu().numpy() for t in (block.w_up, block.w_gate, block.w_down))
+    cpu_block_sample(cfg, xs, wr, wu, wg, wd, Ts)  # warm caches / thread pool
+    sec = cpu_block_sample(cfg, xs, wr, wu, wg, wd, Ts, reps=2)
+    cores = cpu_threads()
+    return {"value": Ts / sec, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": f"{Ts} of {cfg.T} tokens, same weights; NumPy grouped restatement of oracles/moe.py "
+                      f"(oracle/moe_oracle.py), {cores} BLAS threads"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--config", default="c3_mixtral_8x7b")
+    ap.add_argument("--impl", default="frank", choices=["frank", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
+    from frank_b200 import configs
+
+    cfg = configs.BLOCK_CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_frank(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

@@ -35,7 +35,12 @@ void set_error(const char* fmt, ...);
     }                                                                          \
   } while (0)
 
-#define FRANK_LAUNCH_CHECK() FRANK_CUDA_TRY(cudaGetLastError())
+void count_launch();
+#define FRANK_LAUNCH_CHECK()               \
+  do {                                     \
+    ::frank::count_launch();               \
+    FRANK_CUDA_TRY(cudaGetLastError());    \
+  } while (0)
 
 #define FRANK_TRY(expr)        \
   do {                         \

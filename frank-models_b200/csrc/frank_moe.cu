@@ -1,6 +1,7 @@
 // C-ABI entry points (include/frank_moe.h) and the orchestration of the MoE
 // FFN block / mul_mat_id out of the kernels in routing.cu, elementwise.cu,
 // gemm_simt.cu and gemm_tc.cu.
+#include <atomic>
 #include <mutex>
 #include <vector>
 
@@ -41,6 +42,37 @@ void set_error(const char* fmt, ...) {
 }
 
 __device__ int32_t g_device_error = 0;
+
+static std::atomic<uint64_t> g_launches{0};
+void count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+
+// Stage timing (frank_profile_stages / frank_profile_read): one set of
+// events per profiled call, kept for up to kProfCalls calls; reading
+// averages over the recorded calls and starts a new window.
+constexpr int kStages = 6;
+constexpr int kProfCalls = 64;
+struct StageProfiler {
+  bool on = false;
+  bool init = false;
+  int calls = 0;    // calls recorded in the current window
+  int marks = 0;    // marks recorded in the current call
+  cudaEvent_t ev[kProfCalls][kStages + 1];
+};
+static StageProfiler g_prof;
+static std::mutex g_prof_mu;
+
+static void prof_mark(int i, cudaStream_t st) {
+  if (!g_prof.on) return;
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (!g_prof.init) {
+    for (auto& set : g_prof.ev)
+      for (auto& e : set) cudaEventCreate(&e);
+    g_prof.init = true;
+  }
+  if (g_prof.calls >= kProfCalls) return;
+  cudaEventRecord(g_prof.ev[g_prof.calls][i], st);
+  if (i == kStages) ++g_prof.calls;
+}
 
 int32_t* device_error_word() {
   int dev = 0;
@@ -237,10 +269,11 @@ size_t frank_moe_ffn_block_workspace_size(int dtype, int64_t T, int64_t H, int64
 
 int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, const void* w_up_p,
                         const void* w_gate_p, const void* w_down_p, int64_t T, int64_t E, int64_t k, int64_t H,
-                        int64_t F, int normalize, void* y, float* route_w, int32_t* route_ids, void* workspace,
+                        int64_t F, int normalize, int y_dtype, void* y, float* route_w, int32_t* route_ids, void* workspace,
                         size_t ws_bytes, void* stream) {
   FRANK_TRY(check_dtype(dtype, "moe_ffn_block"));
   FRANK_TRY(check_dtype(wr_dtype, "moe_ffn_block"));
+  FRANK_TRY(check_dtype(y_dtype, "moe_ffn_block"));
   FRANK_CHECK_ARG(E >= 1 && E <= 256, "moe_ffn_block: n_expert=%lld outside [1, 256]", (long long)E);
   FRANK_CHECK_ARG(k >= 1 && k <= E && k <= 32, "moe_ffn_block: n_expert_used=%lld outside [1, min(E, 32)]",
                   (long long)k);
@@ -263,26 +296,35 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
   moe_layout(dtype, T, H, F, E, k, workspace, ws_bytes, &L);
   float* w = route_w ? route_w : L.w;
   int32_t* ids = route_ids ? route_ids : L.ids;
+  prof_mark(0, st);
   // 1. router + softmax + top-k (+ renorm)          moe_ffn_block.mlir:54-128
   FRANK_TRY(launch_router_topk(dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, st));
+  prof_mark(1, st);
   // 2. stable expert permutation                    mul_mat_id.mlir:51-61
   FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, nullptr, L.perm_ws, L.perm_bytes, st));
   FRANK_TRY(launch_sorted_weights(w, L.sorted_slots, n, L.wsorted, st));
+  prof_mark(2, st);
   // 3. expert-sorted activation rows (replicate + permute, :130-144, mul_mat_id.mlir:64-84)
   FRANK_TRY(launch_gather_rows(dtype, x, L.sorted_slots, n, T, H, L.xs, st));
+  prof_mark(3, st);
   if (dtype == FRANK_F32) {
     // 4. h = gate(x) * silu(up(x))                   :146-156
     FRANK_TRY(launch_grouped_gemm_f32(2, (const float*)L.xs, (const float*)w_gate_p, (const float*)w_up_p, L.offsets,
                                       E, n, F, H, nullptr, (float*)L.hs, st));
+    prof_mark(4, st);
     // 5. d = down(h) * w                             :158-177
     FRANK_TRY(launch_grouped_gemm_f32(1, (const float*)L.hs, (const float*)w_down_p, nullptr, L.offsets, E, n, H, F,
                                       L.wsorted, L.ds, st));
   } else {
     FRANK_TRY(launch_tc_grouped_gemm(0, L.xs, w_gate_p, w_up_p, L.offsets, E, n, F, H, nullptr, L.hs, st));
+    prof_mark(4, st);
     FRANK_TRY(launch_tc_grouped_gemm(1, L.hs, w_down_p, nullptr, L.offsets, E, n, H, F, L.wsorted, L.ds, st));
   }
+  prof_mark(5, st);
   // 6. y[t] = sum_j d[slot j of t]                   :179-206
-  return launch_combine(dtype, L.ds, L.slot_pos, T, k, H, y, st);
+  FRANK_TRY(launch_combine(y_dtype, L.ds, L.slot_pos, T, k, H, y, st));
+  prof_mark(6, st);
+  return FRANK_OK;
 }
 
 int frank_read_device_error(int32_t* out, void* stream) {
@@ -297,6 +339,35 @@ int frank_read_device_error(int32_t* out, void* stream) {
   FRANK_CUDA_TRY(cudaMemsetAsync(p, 0, sizeof(v), st));
   FRANK_CUDA_TRY(cudaStreamSynchronize(st));
   if (out) *out = v;
+  return FRANK_OK;
+}
+
+uint64_t frank_launch_count(void) { return g_launches.load(); }
+
+int frank_profile_stages(int enable) {
+  g_prof.on = enable != 0;
+  return FRANK_OK;
+}
+
+int frank_profile_read(float* stage_ms, int max_stages, int* n_stages) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
+  if (!g_prof.init || g_prof.calls == 0) {
+    set_error("profile_read: no complete profiled call recorded");
+    return FRANK_EINVAL;
+  }
+  const int n = max_stages < kStages ? max_stages : kStages;
+  FRANK_CUDA_TRY(cudaEventSynchronize(g_prof.ev[g_prof.calls - 1][kStages]));
+  for (int i = 0; i < n; ++i) {
+    double acc = 0.0;
+    for (int c = 0; c < g_prof.calls; ++c) {
+      float ms = 0.f;
+      FRANK_CUDA_TRY(cudaEventElapsedTime(&ms, g_prof.ev[c][i], g_prof.ev[c][i + 1]));
+      acc += ms;
+    }
+    stage_ms[i] = (float)(acc / g_prof.calls);
+  }
+  if (n_stages) *n_stages = g_prof.calls;
+  g_prof.calls = 0;
   return FRANK_OK;
 }
 

@@ -66,7 +66,12 @@ class MulMatIdConfig:
 
 C2 = MulMatIdConfig("c2_mul_mat_id", T=4096, n_in=4096, n_out=14336, E=8, k=2)
 
-BLOCK_CONFIGS = {c.name: c for c in (C1, C3, C4, c5(1), c5(8), c5(32), c5(64))}
+# Mixtral-shaped block with 2 experts and T=4096 (every token uses both):
+# the same per-expert GEMM shapes as C3 (M = 4096 rows, N = 2 x 14336,
+# K = 4096) in about 1.5 GB, for ncu captures that replay kernels.
+C3_PROFILE = BlockConfig("c3_profile_2experts", T=4096, H=4096, F=14336, E=2, k=2, normalize=False, dtype="bf16")
+
+BLOCK_CONFIGS = {c.name: c for c in (C1, C3, C4, c5(1), c5(8), c5(32), c5(64), C3_PROFILE)}
 
 
 def zipf_log_bias(E: int, s: float, seed: int) -> np.ndarray:

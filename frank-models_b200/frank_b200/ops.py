@@ -207,14 +207,20 @@ class MoEFFNBlock:
 
     Mirrors @moe_ffn_components.moe_ffn_block (moe_ffn_block.mlir:34-209):
     the weights are given in the reference layouts (router [E, H], up/gate
-    [F, H, E], down [H, F, E]) and packed at construction.
+    [F, H, E], down [H, F, E]) and packed at construction.  ``dtype`` is the
+    compute dtype (bf16: tcgen05, fp32: FFMA); ``out_dtype`` the dtype of y
+    (default fp32, the reference's output type).
     """
 
     def __init__(self, gate_inp_w, up_exps_w, gate_exps_w, down_exps_w, n_expert: int, n_expert_used: int,
-                 normalize_weights: bool, dtype: torch.dtype = torch.bfloat16):
+                 normalize_weights: bool, dtype: torch.dtype = torch.bfloat16,
+                 out_dtype: torch.dtype = torch.float32):
         if dtype not in _DT:
             raise TypeError(f"MoEFFNBlock: unsupported compute dtype {dtype}")
+        if out_dtype not in _DT:
+            raise TypeError(f"MoEFFNBlock: unsupported output dtype {out_dtype}")
         self.dtype = dtype
+        self.out_dtype = out_dtype
         self.E = int(n_expert)
         self.k = int(n_expert_used)
         self.normalize = bool(normalize_weights)
@@ -245,13 +251,16 @@ class MoEFFNBlock:
             raise ValueError(f"moe_ffn_block: input must be {self.dtype} [T, {self.H}], got {x.dtype} "
                              f"{tuple(x.shape)}")
         T = x.shape[0]
-        y = out if out is not None else torch.empty((T, self.H), dtype=self.dtype, device=x.device)
+        if out is not None and (out.dtype != self.out_dtype or tuple(out.shape) != (T, self.H)
+                                or not out.is_contiguous()):
+            raise ValueError(f"moe_ffn_block: out must be contiguous {self.out_dtype} [{T}, {self.H}]")
+        y = out if out is not None else torch.empty((T, self.H), dtype=self.out_dtype, device=x.device)
         rw = torch.empty((self.k, T), dtype=torch.float32, device=x.device) if return_routing else None
         rid = torch.empty((self.k, T), dtype=torch.int32, device=x.device) if return_routing else None
         ws = self._workspace(T, x.device)
         _lib.check(_lib.load().frank_moe_ffn_block(
             _DT[self.dtype], _ptr(x), _dt(self.wr), _ptr(self.wr), _ptr(self.w_up), _ptr(self.w_gate),
-            _ptr(self.w_down), T, self.E, self.k, self.H, self.F, int(self.normalize), _ptr(y), _ptr(rw), _ptr(rid),
+            _ptr(self.w_down), T, self.E, self.k, self.H, self.F, int(self.normalize), _DT[self.out_dtype], _ptr(y), _ptr(rw), _ptr(rid),
             _ptr(ws), ws.numel(), _stream()))
         if return_routing:
             return y, rw, rid
@@ -265,3 +274,26 @@ def read_device_error() -> int:
     v = ctypes.c_int32(0)
     _lib.check(_lib.load().frank_read_device_error(ctypes.byref(v), _stream()))
     return v.value
+
+
+STAGE_NAMES = ("route", "permute", "gather", "gate_up_gemm", "down_gemm", "combine")
+
+
+def launch_count() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(_lib.load().frank_launch_count())
+
+
+def profile_stages(enable: bool) -> None:
+    """Record CUDA events around each stage of moe_ffn_block (measurement only)."""
+    _lib.check(_lib.load().frank_profile_stages(int(bool(enable))))
+
+
+def profile_read() -> dict:
+    """Stage durations (ms) of the most recent profiled moe_ffn_block call."""
+    import ctypes
+
+    buf = (ctypes.c_float * len(STAGE_NAMES))()
+    n = ctypes.c_int(0)
+    _lib.check(_lib.load().frank_profile_read(buf, len(STAGE_NAMES), ctypes.byref(n)))
+    return {name: float(buf[i]) for i, name in enumerate(STAGE_NAMES)}

@@ -136,9 +136,11 @@ int frank_mul_mat_id(int dtype, const void* w_eoi, const void* input,
  * (moe_ffn_block.mlir:34-209, oracles/moe.py:51-132):
  *   route -> permute -> h = gate(x) * silu(up(x)) -> d = down(h) * w
  *   -> y[t] = sum_j d[slot j of t]  (j = 0..k-1 in order).
- *   dtype FRANK_F32 : x fp32 [T,H], packed weights fp32, y fp32 (FFMA path)
- *   dtype FRANK_BF16: x bf16 [T,H], packed weights bf16, y bf16 (tcgen05
- *                     path, fp32 accumulation)
+ *   dtype FRANK_F32 : x fp32 [T,H], packed weights fp32 (FFMA path)
+ *   dtype FRANK_BF16: x bf16 [T,H], packed weights bf16 (tcgen05 path,
+ *                     fp32 accumulation, h = swiglu(..) held in bf16)
+ * y [T,H] has y_dtype: FRANK_F32 (the reference's output type,
+ * moe_ffn_block.mlir:45) or FRANK_BF16.
  * wr [E, H] is fp32 or bf16 (wr_dtype).  Packed weights:
  *   w_up_p, w_gate_p [E, F, H]; w_down_p [E, H, F]  (frank_prepack_experts)
  * Optional outputs (may be NULL): route_w [k,T] fp32, route_ids [k,T] int32.
@@ -148,7 +150,7 @@ size_t frank_moe_ffn_block_workspace_size(int dtype, int64_t T, int64_t H,
 int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr,
                         const void* w_up_p, const void* w_gate_p,
                         const void* w_down_p, int64_t T, int64_t E, int64_t k,
-                        int64_t H, int64_t F, int normalize, void* y,
+                        int64_t H, int64_t F, int normalize, int y_dtype, void* y,
                         float* route_w, int32_t* route_ids, void* workspace,
                         size_t ws_bytes, void* stream);
 
@@ -158,6 +160,23 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr,
  * it; synchronises the stream.
  */
 int frank_read_device_error(int32_t* out, void* stream);
+
+/* Number of kernels this library has launched in this process. */
+uint64_t frank_launch_count(void);
+
+/*
+ * Stage timing for measurement tools.  While enabled, frank_moe_ffn_block
+ * records a CUDA event on the caller's stream before its first stage and
+ * after each stage:  0 route (router + softmax + top-k), 1 permute,
+ * 2 gather of expert-sorted rows, 3 gate/up GEMM + swiglu, 4 down GEMM,
+ * 5 combine.  Up to 64 calls are recorded per window.  frank_profile_read
+ * waits for the last recorded call, writes up to max_stages mean durations
+ * in milliseconds over the window's calls, stores the number of calls in
+ * *n_stages and starts a new window.  Events belong to the device current at
+ * the first enabled call.  Measurement only; off by default.
+ */
+int frank_profile_stages(int enable);
+int frank_profile_read(float* stage_ms, int max_stages, int* n_stages);
 
 #ifdef __cplusplus
 }

@@ -64,6 +64,6 @@ def test_calls_without_device_work(lib):
     assert st == _lib.EINVAL and b"E=" in L.frank_last_error()
     st = L.frank_swiglu(7, None, None, None, 4, None)
     assert st == _lib.EINVAL
-    st = L.frank_moe_ffn_block(1, None, 0, None, None, None, None, 4, 8, 9, 64, 64, 0, None, None, None, None, 0,
-                               None)
+    st = L.frank_moe_ffn_block(1, None, 0, None, None, None, None, 4, 8, 9, 64, 64, 0, 0, None, None, None, None,
+                               0, None)
     assert st == _lib.EINVAL and b"n_expert_used" in L.frank_last_error()
