@@ -12,7 +12,8 @@ namespace frank {
 // ---- kernels implemented in the other translation units ----
 int launch_softmax_topk(const float*, int64_t, int64_t, int64_t, int, float*, int32_t*, cudaStream_t);
 int launch_router_topk(int, const void*, int, const void*, int64_t, int64_t, int64_t, int64_t, int, float*, int32_t*,
-                       cudaStream_t);
+                       float*, cudaStream_t);
+size_t router_logits_bytes(int64_t, int64_t);
 size_t permute_workspace_size(int64_t, int64_t);
 int launch_permute(const int32_t*, int64_t, int64_t, int32_t*, int32_t*, int32_t*, int32_t*, void*, size_t,
                    cudaStream_t);
@@ -116,6 +117,7 @@ struct MoeWs {
   void* xs;
   void* hs;
   float* ds;
+  float* logits;
   void* perm_ws;
   size_t perm_bytes;
 };
@@ -136,6 +138,7 @@ static size_t moe_layout(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, 
   l.xs = c.take<char>(n * H * esz);
   l.hs = c.take<char>(n * F * esz);
   l.ds = c.take<float>(n * H);
+  l.logits = c.take<float>(router_logits_bytes(T, E) / sizeof(float));
   l.perm_bytes = permute_workspace_size(n, E);
   l.perm_ws = c.take<char>(l.perm_bytes);
   if (L) *L = l;
@@ -211,7 +214,8 @@ int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, 
   FRANK_CHECK_ARG(E >= 1 && E <= 256, "router_topk: E=%lld outside [1, 256]", (long long)E);
   FRANK_CHECK_ARG(k >= 1 && k <= E && k <= 32, "router_topk: k=%lld outside [1, min(E, 32)]", (long long)k);
   FRANK_CHECK_ARG(T >= 0 && H >= 1, "router_topk: bad T=%lld / H=%lld", (long long)T, (long long)H);
-  return launch_router_topk(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, weights, ids, as_stream(stream));
+  return launch_router_topk(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, weights, ids, nullptr,
+                            as_stream(stream));
 }
 
 size_t frank_permute_workspace_size(int64_t n_slots, int64_t E) { return permute_workspace_size(n_slots, E); }
@@ -298,7 +302,7 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
   int32_t* ids = route_ids ? route_ids : L.ids;
   prof_mark(0, st);
   // 1. router + softmax + top-k (+ renorm)          moe_ffn_block.mlir:54-128
-  FRANK_TRY(launch_router_topk(dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, st));
+  FRANK_TRY(launch_router_topk(dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, L.logits, st));
   prof_mark(1, st);
   // 2. stable expert permutation                    mul_mat_id.mlir:51-61
   FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, nullptr, L.perm_ws, L.perm_bytes, st));

@@ -151,6 +151,109 @@ router_topk_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t 
   }
 }
 
+// Vector router: logits for EC experts of every token.  The block stages
+// wr[e0:e0+EC, :] (fp32) in shared memory once; each warp then takes groups
+// of kTPW tokens, each lane reading 8-element (16-byte for bf16) slices of
+// the token rows, accumulating kTPW x EC partial dot products in registers,
+// and reducing them across the warp with butterfly shuffles.  When all E
+// experts fit in one pass (E <= EC) the warp goes straight on to softmax +
+// top-k; otherwise logits [E, T] go to a buffer for softmax_topk_kernel.
+constexpr int kTPW = 4;
+constexpr int kVecThreads = 512;
+
+template <class T>
+__device__ __forceinline__ void load8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, float (&v)[8]) {
+  float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <class TX, class TW, int EC>
+__global__ void __launch_bounds__(kVecThreads)
+router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int H, int E, int k, int normalize,
+                  float* __restrict__ logits, float* __restrict__ w, int32_t* __restrict__ ids) {
+  extern __shared__ float sw[];                          // [EC][H] fp32
+  __shared__ float lg[kVecThreads / 32][kTPW][EC];
+  const int e0 = blockIdx.y * EC;
+  const int ec = min(EC, E - e0);
+  for (int i = threadIdx.x; i < EC * H; i += kVecThreads) {
+    int e = i / H, h = i - e * H;
+    sw[i] = (e < ec) ? load_as_f32(wr, (int64_t)(e0 + e) * H + h) : 0.f;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t groups = (T + kTPW - 1) / kTPW;
+  const bool fused = (E <= EC);
+  for (int64_t g = (int64_t)blockIdx.x * (kVecThreads / 32) + warp; g < groups;
+       g += (int64_t)gridDim.x * (kVecThreads / 32)) {
+    const int64_t t0 = g * kTPW;
+    float acc[kTPW][EC];
+#pragma unroll
+    for (int a = 0; a < kTPW; ++a)
+#pragma unroll
+      for (int e = 0; e < EC; ++e) acc[a][e] = 0.f;
+    for (int h = lane * 8; h < H; h += 256) {
+      float xv[kTPW][8];
+#pragma unroll
+      for (int a = 0; a < kTPW; ++a) {
+        if (t0 + a < T) load8(x + (t0 + a) * H + h, xv[a]);
+        else
+#pragma unroll
+          for (int i = 0; i < 8; ++i) xv[a][i] = 0.f;
+      }
+#pragma unroll
+      for (int e = 0; e < EC; ++e) {
+        const float4 w0 = *reinterpret_cast<const float4*>(sw + e * H + h);
+        const float4 w1 = *reinterpret_cast<const float4*>(sw + e * H + h + 4);
+        const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int a = 0; a < kTPW; ++a)
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[a][e] = fmaf(wv[i], xv[a][i], acc[a][e]);
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < kTPW; ++a)
+#pragma unroll
+      for (int e = 0; e < EC; ++e) {
+        float v = acc[a][e];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+        acc[a][e] = v;
+      }
+    if (fused) {
+      if (lane == 0)
+#pragma unroll
+        for (int a = 0; a < kTPW; ++a)
+#pragma unroll
+          for (int e = 0; e < EC; ++e) lg[warp][a][e] = acc[a][e];
+      __syncwarp();
+      for (int a = 0; a < kTPW; ++a)
+        if (t0 + a < T) warp_softmax_topk(lg[warp][a], E, k, normalize, w, ids, T, t0 + a);
+      __syncwarp();
+    } else if (lane < kTPW) {
+#pragma unroll
+      for (int a = 0; a < kTPW; ++a)
+        if (a == lane && t0 + a < T)
+#pragma unroll
+          for (int e = 0; e < EC; ++e)
+            if (e < ec) logits[(int64_t)(e0 + e) * T + t0 + a] = acc[a][e];
+    }
+  }
+}
+
 // ---------------------------------------------------------------- permute --
 // Three passes, no atomics:
 //  A) per chunk of kChunk slots: stable local rank of each slot among the
@@ -281,9 +384,8 @@ int launch_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k, in
   return FRANK_OK;
 }
 
-int launch_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H,
-                       int64_t E, int64_t k, int normalize, float* w, int32_t* ids, cudaStream_t st) {
-  if (T == 0) return FRANK_OK;
+static int launch_router_legacy(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H,
+                                int64_t E, int64_t k, int normalize, float* w, int32_t* ids, cudaStream_t st) {
   size_t smem = sizeof(float) * (kRouterTok * (kRouterHc + 1) + E * (kRouterHc + 1) + kRouterTok * E);
   dim3 grid((unsigned)((T + kRouterTok - 1) / kRouterTok));
 #define FRANK_ROUTER_CASE(TX, TW)                                                                 \
@@ -300,6 +402,57 @@ int launch_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr,
 #undef FRANK_ROUTER_CASE
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
+}
+
+template <class TX, class TW, int EC>
+static int launch_router_vec_t(const void* x, const void* wr, int64_t T, int64_t H, int64_t E, int64_t k,
+                               int normalize, float* logits, float* w, int32_t* ids, cudaStream_t st) {
+  auto kern = router_vec_kernel<TX, TW, EC>;
+  const size_t smem = (size_t)EC * H * sizeof(float);
+  FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  FRANK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kVecThreads, smem));
+  const int64_t passes = (E + EC - 1) / EC;
+  const int64_t groups = (T + kTPW - 1) / kTPW;
+  int64_t gx = (groups + kVecThreads / 32 - 1) / (kVecThreads / 32);
+  int64_t cap = (int64_t)num_sms() * (per_sm > 0 ? per_sm : 1);
+  cap = (cap + passes - 1) / passes;
+  if (gx > cap) gx = cap;
+  dim3 grid((unsigned)(gx < 1 ? 1 : gx), (unsigned)passes);
+  kern<<<grid, kVecThreads, smem, st>>>((const TX*)x, (const TW*)wr, T, (int)H, (int)E, (int)k, normalize, logits, w,
+                                        ids);
+  FRANK_LAUNCH_CHECK();
+  if (passes > 1) FRANK_TRY(launch_softmax_topk(logits, T, E, k, normalize, w, ids, st));
+  return FRANK_OK;
+}
+
+template <class TX, class TW>
+static int launch_router_vec(const void* x, const void* wr, int64_t T, int64_t H, int64_t E, int64_t k, int normalize,
+                             float* logits, float* w, int32_t* ids, cudaStream_t st) {
+  const int64_t budget = 160 * 1024;
+  if (8 * H * 4 <= budget) return launch_router_vec_t<TX, TW, 8>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+  if (4 * H * 4 <= budget) return launch_router_vec_t<TX, TW, 4>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+  if (2 * H * 4 <= budget) return launch_router_vec_t<TX, TW, 2>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+  return launch_router_vec_t<TX, TW, 1>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+}
+
+size_t router_logits_bytes(int64_t T, int64_t E) { return E <= 8 ? 0 : (size_t)T * E * sizeof(float); }
+
+// logits: fp32 scratch of router_logits_bytes(T, E) bytes (unused when E <= 8).
+int launch_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H,
+                       int64_t E, int64_t k, int normalize, float* w, int32_t* ids, float* logits, cudaStream_t st) {
+  if (T == 0) return FRANK_OK;
+  const size_t esz = x_dtype == FRANK_F32 ? 4 : 2;
+  const bool vec_ok = (H % 8 == 0) && ((uintptr_t)x % 16 == 0) && (H * 4 * 1 <= 160 * 1024) &&
+                      (E <= 8 || logits != nullptr) && (H * esz) % 16 == 0;
+  if (!vec_ok) return launch_router_legacy(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, st);
+  if (x_dtype == FRANK_F32 && wr_dtype == FRANK_F32)
+    return launch_router_vec<float, float>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+  if (x_dtype == FRANK_F32)
+    return launch_router_vec<float, __nv_bfloat16>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+  if (wr_dtype == FRANK_F32)
+    return launch_router_vec<__nv_bfloat16, float>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+  return launch_router_vec<__nv_bfloat16, __nv_bfloat16>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
 }
 
 size_t permute_workspace_size(int64_t n, int64_t E) {
