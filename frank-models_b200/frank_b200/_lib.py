@@ -39,6 +39,7 @@ SIGNATURES = {
                                    _c_vp, _c_vp, _c_vp]),
     "frank_permute_workspace_size": (_c_size, [_c_i64, _c_i64]),
     "frank_permute": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_size, _c_vp]),
+    "frank_permute_noalloc": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),
     "frank_prepack_experts": (_c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
     "frank_mul_mat_id_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
     "frank_mul_mat_id": (_c_int, [_c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp,

@@ -108,6 +108,26 @@ int frank_permute(const int32_t* ids, int64_t n_slots, int64_t E,
                   void* stream);
 
 /*
+ * frank_permute without a workspace argument, for callers that cannot
+ * allocate device memory (a host framework that owns the device memory
+ * pool, an FFI binding that cannot keep a CUDA workspace alive, or a loop
+ * where allocating is not allowed).  No counterpart in the reference: it is
+ * an addition of this library.  Same inputs, outputs and results as
+ * frank_permute; the scratch is a fixed library-owned device array of
+ * FRANK_PERMUTE_NOALLOC_SCRATCH_BYTES, held by every GPU that loads the
+ * library until exit.  Returns FRANK_EINVAL when
+ * frank_permute_workspace_size(n_slots, E) exceeds it (1 MiB covers, e.g.,
+ * 65536 slots with any E <= 1024).  The first call on a device looks up the
+ * array's device address and should come before any stream capture.  All
+ * calls share the array: calls that overlap on the GPU race and must be
+ * serialised by the caller.  Allocates nothing.
+ */
+#define FRANK_PERMUTE_NOALLOC_SCRATCH_BYTES (1u << 20)
+int frank_permute_noalloc(const int32_t* ids, int64_t n_slots, int64_t E,
+                          int32_t* sorted_slots, int32_t* offsets,
+                          int32_t* slot_pos, int32_t* err_flag, void* stream);
+
+/*
  * One-time weight prepack: [O, I, E] (expert innermost, in_dtype) ->
  * [E, O, I] (out_dtype).  Replaces the per-call transpose of
  * mul_mat_id.mlir:38-48.  FRANK_F32 -> FRANK_F32 or FRANK_BF16;
