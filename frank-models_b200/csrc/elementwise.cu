@@ -152,6 +152,48 @@ __global__ void sorted_weights_kernel(const float* __restrict__ w, const int32_t
   if (r < n) ws[r] = w[sorted_slots[r]];
 }
 
+// --------------------------------------------------- row segment copy ----
+// dst rows [dst_start[s], +len[s]) = src rows [src_start[s], +len[s]) for
+// every segment s; seg_prefix[nseg+1] is the exclusive prefix of len.  One
+// warp per destination row (16-byte vectors); the warp finds its segment by
+// binary search.  Used by the expert-parallel layer to turn
+// source-rank-major received rows into expert-major order and back.
+__global__ void copy_row_segments_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst,
+                                         const int64_t* __restrict__ src_start, const int64_t* __restrict__ dst_start,
+                                         const int64_t* __restrict__ seg_prefix, int nseg, int64_t vec_per_row) {
+  const int64_t total = seg_prefix[nseg];
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5); r < total;
+       r += (int64_t)gridDim.x * (blockDim.x / 32)) {
+    int lo = 0, hi = nseg;
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (seg_prefix[mid] <= r) lo = mid; else hi = mid;
+    }
+    const int64_t i = r - seg_prefix[lo];
+    const uint4* s = src + (src_start[lo] + i) * vec_per_row;
+    uint4* d = dst + (dst_start[lo] + i) * vec_per_row;
+    for (int64_t v = lane; v < vec_per_row; v += 32) d[v] = s[v];
+  }
+}
+
+__global__ void copy_row_segments_u32_kernel(const uint32_t* __restrict__ src, uint32_t* __restrict__ dst,
+                                             const int64_t* __restrict__ src_start,
+                                             const int64_t* __restrict__ dst_start,
+                                             const int64_t* __restrict__ seg_prefix, int nseg, int64_t words) {
+  const int64_t total = seg_prefix[nseg] * words;
+  for (int64_t q = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = q / words, wd = q - r * words;
+    int lo = 0, hi = nseg;
+    while (hi - lo > 1) {
+      int mid = (lo + hi) >> 1;
+      if (seg_prefix[mid] <= r) lo = mid; else hi = mid;
+    }
+    const int64_t i = r - seg_prefix[lo];
+    dst[(dst_start[lo] + i) * words + wd] = src[(src_start[lo] + i) * words + wd];
+  }
+}
+
 unsigned grid_1d(int64_t n, int threads) {
   int64_t b = (n + threads - 1) / threads;
   int64_t cap = (int64_t)frank::num_sms() * 16;
@@ -272,6 +314,29 @@ int launch_combine(int dtype, const float* d, const int32_t* slot_pos, int64_t T
     }
     FRANK_LAUNCH_CHECK();
   }
+  return FRANK_OK;
+}
+
+int launch_copy_row_segments(const void* src, void* dst, const int64_t* src_start, const int64_t* dst_start,
+                             const int64_t* seg_prefix, int64_t nseg, int64_t total_rows, int64_t row_bytes,
+                             cudaStream_t st) {
+  if (total_rows == 0 || nseg == 0) return FRANK_OK;
+  if (row_bytes % 4 != 0) {
+    set_error("copy_row_segments: row_bytes=%lld is not a multiple of 4", (long long)row_bytes);
+    return FRANK_EINVAL;
+  }
+  const int64_t cap = (int64_t)num_sms() * 16;
+  if (row_bytes % 16 == 0 && (uintptr_t)src % 16 == 0 && (uintptr_t)dst % 16 == 0) {
+    int64_t blocks = (total_rows + 7) / 8;
+    copy_row_segments_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, st>>>(
+        (const uint4*)src, (uint4*)dst, src_start, dst_start, seg_prefix, (int)nseg, row_bytes / 16);
+  } else {
+    int64_t words = row_bytes / 4;
+    int64_t blocks = (total_rows * words + 255) / 256;
+    copy_row_segments_u32_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, st>>>(
+        (const uint32_t*)src, (uint32_t*)dst, src_start, dst_start, seg_prefix, (int)nseg, words);
+  }
+  FRANK_LAUNCH_CHECK();
   return FRANK_OK;
 }
 

@@ -24,6 +24,8 @@ int launch_gather_cols(int, const void*, const int32_t*, int64_t, int64_t, void*
 int launch_scatter_out(const float*, const int32_t*, int64_t, int64_t, float*, cudaStream_t);
 int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
 int launch_sorted_weights(const float*, const int32_t*, int64_t, float*, cudaStream_t);
+int launch_copy_row_segments(const void*, void*, const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t,
+                             int64_t, cudaStream_t);
 int launch_grouped_gemm_f32(int, const float*, const float*, const float*, const int32_t*, int64_t, int64_t, int64_t,
                             int64_t, const float*, float*, cudaStream_t);
 int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int32_t*, int64_t, int64_t, int64_t,
@@ -207,14 +209,16 @@ int frank_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k, int
   return launch_softmax_topk(logits, T, E, k, normalize, weights, ids, as_stream(stream));
 }
 
+size_t frank_router_scratch_bytes(int64_t T, int64_t E) { return router_logits_bytes(T, E); }
+
 int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H, int64_t E,
-                      int64_t k, int normalize, float* weights, int32_t* ids, void* stream) {
+                      int64_t k, int normalize, float* weights, int32_t* ids, float* logits_scratch, void* stream) {
   FRANK_TRY(check_dtype(x_dtype, "router_topk"));
   FRANK_TRY(check_dtype(wr_dtype, "router_topk"));
   FRANK_CHECK_ARG(E >= 1 && E <= 256, "router_topk: E=%lld outside [1, 256]", (long long)E);
   FRANK_CHECK_ARG(k >= 1 && k <= E && k <= 32, "router_topk: k=%lld outside [1, min(E, 32)]", (long long)k);
   FRANK_CHECK_ARG(T >= 0 && H >= 1, "router_topk: bad T=%lld / H=%lld", (long long)T, (long long)H);
-  return launch_router_topk(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, weights, ids, nullptr,
+  return launch_router_topk(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, weights, ids, logits_scratch,
                             as_stream(stream));
 }
 
@@ -329,6 +333,60 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
   FRANK_TRY(launch_combine(y_dtype, L.ds, L.slot_pos, T, k, H, y, st));
   prof_mark(6, st);
   return FRANK_OK;
+}
+
+int frank_gather_rows(int dtype, const void* x, const int32_t* sorted_slots, int64_t rows, int64_t T, int64_t H,
+                      void* xs, void* stream) {
+  FRANK_TRY(check_dtype(dtype, "gather_rows"));
+  FRANK_CHECK_ARG(rows >= 0 && T >= 1 && H >= 1, "gather_rows: bad rows/T/H");
+  return launch_gather_rows(dtype, x, sorted_slots, rows, T, H, xs, as_stream(stream));
+}
+
+int frank_gather_weights(const float* w, const int32_t* sorted_slots, int64_t n, float* w_sorted, void* stream) {
+  FRANK_CHECK_ARG(n >= 0, "gather_weights: n < 0");
+  return launch_sorted_weights(w, sorted_slots, n, w_sorted, as_stream(stream));
+}
+
+size_t frank_expert_ffn_workspace_size(int dtype, int64_t rows, int64_t F) {
+  return align_up((size_t)rows * F * (dtype == FRANK_F32 ? 4 : 2), 256) + 256;
+}
+
+int frank_expert_ffn(int dtype, const void* xs, const float* w_rows, const int32_t* offsets, int64_t E, int64_t rows,
+                     int64_t H, int64_t F, const void* w_up_p, const void* w_gate_p, const void* w_down_p, float* d,
+                     void* workspace, size_t ws_bytes, void* stream) {
+  FRANK_TRY(check_dtype(dtype, "expert_ffn"));
+  FRANK_CHECK_ARG(E >= 1 && rows >= 0 && H >= 1 && F >= 1, "expert_ffn: bad shape");
+  if (rows == 0) return FRANK_OK;
+  if (ws_bytes < frank_expert_ffn_workspace_size(dtype, rows, F)) {
+    set_error("expert_ffn: workspace %zu < %zu bytes", ws_bytes, frank_expert_ffn_workspace_size(dtype, rows, F));
+    return FRANK_ENOSPC;
+  }
+  cudaStream_t st = as_stream(stream);
+  if (dtype == FRANK_F32) {
+    FRANK_TRY(launch_grouped_gemm_f32(2, (const float*)xs, (const float*)w_gate_p, (const float*)w_up_p, offsets, E,
+                                      rows, F, H, nullptr, (float*)workspace, st));
+    return launch_grouped_gemm_f32(1, (const float*)workspace, (const float*)w_down_p, nullptr, offsets, E, rows, H,
+                                   F, w_rows, d, st);
+  }
+  FRANK_TRY(check_tc_shapes(rows, F, H, E));
+  FRANK_TRY(check_tc_shapes(rows, H, F, E));
+  FRANK_TRY(launch_tc_grouped_gemm(0, xs, w_gate_p, w_up_p, offsets, E, rows, F, H, nullptr, workspace, st));
+  return launch_tc_grouped_gemm(1, workspace, w_down_p, nullptr, offsets, E, rows, H, F, w_rows, d, st);
+}
+
+int frank_combine(const float* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H, int y_dtype, void* y,
+                  void* stream) {
+  FRANK_TRY(check_dtype(y_dtype, "combine"));
+  FRANK_CHECK_ARG(T >= 0 && k >= 1 && H >= 1, "combine: bad shape");
+  return launch_combine(y_dtype, d, slot_pos, T, k, H, y, as_stream(stream));
+}
+
+int frank_copy_row_segments(const void* src, void* dst, const int64_t* src_start, const int64_t* dst_start,
+                            const int64_t* seg_prefix, int64_t nseg, int64_t total_rows, int64_t row_bytes,
+                            void* stream) {
+  FRANK_CHECK_ARG(nseg >= 0 && total_rows >= 0 && row_bytes > 0, "copy_row_segments: bad arguments");
+  return launch_copy_row_segments(src, dst, src_start, dst_start, seg_prefix, nseg, total_rows, row_bytes,
+                                  as_stream(stream));
 }
 
 int frank_read_device_error(int32_t* out, void* stream) {

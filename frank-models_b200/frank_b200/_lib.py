@@ -35,8 +35,9 @@ SIGNATURES = {
     "frank_num_sms": (_c_int, []),
     "frank_swiglu": (_c_int, [_c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp]),
     "frank_softmax_topk": (_c_int, [_c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_vp]),
+    "frank_router_scratch_bytes": (_c_size, [_c_i64, _c_i64]),
     "frank_router_topk": (_c_int, [_c_int, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
-                                   _c_vp, _c_vp, _c_vp]),
+                                   _c_vp, _c_vp, _c_vp, _c_vp]),
     "frank_permute_workspace_size": (_c_size, [_c_i64, _c_i64]),
     "frank_permute": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_size, _c_vp]),
     "frank_permute_noalloc": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp]),
@@ -47,6 +48,13 @@ SIGNATURES = {
     "frank_moe_ffn_block_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
     "frank_moe_ffn_block": (_c_int, [_c_int, _c_vp, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64,
                                      _c_i64, _c_i64, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_size, _c_vp]),
+    "frank_gather_rows": (_c_int, [_c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp]),
+    "frank_gather_weights": (_c_int, [_c_vp, _c_vp, _c_i64, _c_vp, _c_vp]),
+    "frank_expert_ffn_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64]),
+    "frank_expert_ffn": (_c_int, [_c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp,
+                                  _c_vp, _c_vp, _c_size, _c_vp]),
+    "frank_combine": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
+    "frank_copy_row_segments": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),
     "frank_read_device_error": (_c_int, [_c_vp, _c_vp]),
     "frank_launch_count": (ctypes.c_uint64, []),
     "frank_profile_stages": (_c_int, [_c_int]),

@@ -77,8 +77,11 @@ def router_topk(x: torch.Tensor, wr: torch.Tensor, k: int, normalize: bool):
         raise ValueError(f"router_topk: wr {tuple(wr.shape)} does not match n_embd={H}")
     w = torch.empty((k, T), dtype=torch.float32, device=x.device)
     ids = torch.empty((k, T), dtype=torch.int32, device=x.device)
-    _lib.check(_lib.load().frank_router_topk(_dt(x), _ptr(x), _dt(wr), _ptr(wr), T, H, E, k, int(bool(normalize)),
-                                             _ptr(w), _ptr(ids), _stream()))
+    lib = _lib.load()
+    nbytes = lib.frank_router_scratch_bytes(T, E)
+    scratch = torch.empty(nbytes // 4, dtype=torch.float32, device=x.device) if nbytes else None
+    _lib.check(lib.frank_router_topk(_dt(x), _ptr(x), _dt(wr), _ptr(wr), T, H, E, k, int(bool(normalize)),
+                                     _ptr(w), _ptr(ids), _ptr(scratch), _stream()))
     return w, ids
 
 
@@ -297,3 +300,52 @@ def profile_read() -> dict:
     n = ctypes.c_int(0)
     _lib.check(_lib.load().frank_profile_read(buf, len(STAGE_NAMES), ctypes.byref(n)))
     return {name: float(buf[i]) for i, name in enumerate(STAGE_NAMES)}
+
+
+def gather_rows(x: torch.Tensor, sorted_slots: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """xs[r] = x[sorted_slots[r] % T] for expert-sorted slots."""
+    T, H = x.shape
+    n = sorted_slots.numel()
+    xs = out if out is not None else torch.empty((n, H), dtype=x.dtype, device=x.device)
+    _lib.check(_lib.load().frank_gather_rows(_dt(x), _ptr(x), _ptr(sorted_slots), n, T, H, _ptr(xs), _stream()))
+    return xs
+
+
+def gather_weights(w: torch.Tensor, sorted_slots: torch.Tensor) -> torch.Tensor:
+    out = torch.empty(sorted_slots.numel(), dtype=torch.float32, device=w.device)
+    _lib.check(_lib.load().frank_gather_weights(_ptr(w), _ptr(sorted_slots), sorted_slots.numel(), _ptr(out),
+                                                _stream()))
+    return out
+
+
+def expert_ffn(xs: torch.Tensor, w_rows: torch.Tensor, offsets: torch.Tensor, w_up_p: torch.Tensor,
+               w_gate_p: torch.Tensor, w_down_p: torch.Tensor, out: torch.Tensor | None = None,
+               workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Grouped gate/up + swiglu + down x row weight over expert-sorted rows -> fp32 [rows, H]."""
+    rows, H = xs.shape
+    E, F, _ = w_up_p.shape
+    lib = _lib.load()
+    d = out if out is not None else torch.empty((rows, H), dtype=torch.float32, device=xs.device)
+    need = lib.frank_expert_ffn_workspace_size(_dt(xs), rows, F)
+    if workspace is None or workspace.numel() < need:
+        workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=xs.device)
+    _lib.check(lib.frank_expert_ffn(_dt(xs), _ptr(xs), _ptr(w_rows), _ptr(offsets), E, rows, H, F, _ptr(w_up_p),
+                                    _ptr(w_gate_p), _ptr(w_down_p), _ptr(d), _ptr(workspace), workspace.numel(),
+                                    _stream()))
+    return d
+
+
+def combine(d: torch.Tensor, slot_pos: torch.Tensor, T: int, k: int, out: torch.Tensor) -> torch.Tensor:
+    """y[t] = sum_j d[slot_pos[j*T + t]] (j in order)."""
+    H = d.shape[1]
+    _lib.check(_lib.load().frank_combine(_ptr(d), _ptr(slot_pos), T, k, H, _dt(out), _ptr(out), _stream()))
+    return out
+
+
+def copy_row_segments(src: torch.Tensor, dst: torch.Tensor, src_start: torch.Tensor, dst_start: torch.Tensor,
+                      seg_prefix: torch.Tensor, total_rows: int) -> None:
+    """dst rows [dst_start[s], +len_s) = src rows [src_start[s], +len_s) (int64 device tables)."""
+    row_bytes = src[0].numel() * src.element_size() if src.dim() > 1 else src.element_size()
+    _lib.check(_lib.load().frank_copy_row_segments(_ptr(src), _ptr(dst), _ptr(src_start), _ptr(dst_start),
+                                                   _ptr(seg_prefix), src_start.numel(), total_rows, row_bytes,
+                                                   _stream()))

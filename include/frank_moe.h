@@ -85,10 +85,15 @@ int frank_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k,
  * Router: logits = wr @ x.T in fp32, then frank_softmax_topk's rule
  * (moe_ffn_block.mlir:54-128, oracles/moe.py:87-105).
  * x_dtype / wr_dtype: FRANK_F32 or FRANK_BF16.  E <= 256, 1 <= k <= min(E, 32).
+ * logits_scratch: fp32 device scratch of frank_router_scratch_bytes(T, E)
+ * bytes (0 when E <= 8); with NULL and E > 8 a slower kernel that needs no
+ * scratch is used.
  */
+size_t frank_router_scratch_bytes(int64_t T, int64_t E);
 int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr,
                       int64_t T, int64_t H, int64_t E, int64_t k, int normalize,
-                      float* weights, int32_t* ids, void* stream);
+                      float* weights, int32_t* ids, float* logits_scratch,
+                      void* stream);
 
 /*
  * Atomic-free, stable expert permutation of the flattened slots
@@ -173,6 +178,42 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr,
                         int64_t H, int64_t F, int normalize, int y_dtype, void* y,
                         float* route_w, int32_t* route_ids, void* workspace,
                         size_t ws_bytes, void* stream);
+
+/*
+ * Building blocks of moe_ffn_block, exported for the expert-parallel layer
+ * (which runs the stages with NCCL exchanges in between):
+ *
+ * frank_gather_rows: xs[r, :] = x[sorted_slots[r] % T, :] (the replicate +
+ *   permute of moe_ffn_block.mlir:130-144 / mul_mat_id.mlir:64-84).
+ * frank_gather_weights: w_sorted[r] = w[sorted_slots[r]].
+ * frank_expert_ffn: for expert-sorted rows xs [rows, H] with expert row
+ *   offsets [E+1] and per-row gate weights: d = (gate(xs) * silu(up(xs)))
+ *   @ down^T * w_rows, fp32 [rows, H] (moe_ffn_block.mlir:146-177).
+ *   Workspace: frank_expert_ffn_workspace_size(dtype, rows, F).
+ * frank_combine: y[t] = sum_{j<k} d[slot_pos[j*T + t]] in order j
+ *   (moe_ffn_block.mlir:179-206); y_dtype FRANK_F32 or FRANK_BF16.
+ * frank_copy_row_segments: dst rows [dst_start[s], +len) = src rows
+ *   [src_start[s], +len) for nseg segments; seg_prefix [nseg+1] is the
+ *   exclusive prefix of the lengths (device int64 arrays); row_bytes % 4 == 0.
+ */
+int frank_gather_rows(int dtype, const void* x, const int32_t* sorted_slots,
+                      int64_t rows, int64_t T, int64_t H, void* xs,
+                      void* stream);
+int frank_gather_weights(const float* w, const int32_t* sorted_slots,
+                         int64_t n, float* w_sorted, void* stream);
+size_t frank_expert_ffn_workspace_size(int dtype, int64_t rows, int64_t F);
+int frank_expert_ffn(int dtype, const void* xs, const float* w_rows,
+                     const int32_t* offsets, int64_t E, int64_t rows,
+                     int64_t H, int64_t F, const void* w_up_p,
+                     const void* w_gate_p, const void* w_down_p, float* d,
+                     void* workspace, size_t ws_bytes, void* stream);
+int frank_combine(const float* d, const int32_t* slot_pos, int64_t T,
+                  int64_t k, int64_t H, int y_dtype, void* y, void* stream);
+int frank_copy_row_segments(const void* src, void* dst,
+                            const int64_t* src_start, const int64_t* dst_start,
+                            const int64_t* seg_prefix, int64_t nseg,
+                            int64_t total_rows, int64_t row_bytes,
+                            void* stream);
 
 /*
  * Device error word written by bounded waits inside the persistent GEMM

@@ -1,0 +1,76 @@
+"""Expert parallelism on real GPUs (NCCL): every rank's output must equal the
+single-GPU block on the same tokens bit for bit.  Needs >= 2 visible GPUs;
+ranks are child processes, one per GPU."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, cfg, q):
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev)
+    try:
+        from frank_b200 import configs, ep, ops
+
+        wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, dev, seed=0)
+        x = configs.block_x_torch(cfg, dev, seed=10 + rank)
+        El = cfg.E // world
+        sl = slice(rank * El, (rank + 1) * El)
+        moe = ep.ExpertParallelMoE(wr, wu[sl].contiguous(), wg[sl].contiguous(), wd[sl].contiguous(), cfg.E, cfg.k,
+                                   cfg.normalize)
+        y = moe(x)
+        y2 = moe(x)
+        single = ops.MoEFFNBlock(wr, ops.PackedExperts(wu), ops.PackedExperts(wg), ops.PackedExperts(wd), cfg.E,
+                                 cfg.k, cfg.normalize)
+        ref = single(x)
+        torch.cuda.synchronize()
+        q.put((rank, bool(torch.equal(y, ref)), bool(torch.equal(y, y2)),
+               float((y - ref).abs().max().item()), ops.read_device_error()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+@pytest.mark.parametrize("cfg_name", ["bf16_fg_ep", "bf16_c3like_ep"])
+def test_ep_equals_single_gpu(cfg_name):
+    from frank_b200 import configs
+
+    cfg = {
+        "bf16_fg_ep": configs.BlockConfig("bf16_fg_ep", T=1000, H=2048, F=768, E=128, k=8, normalize=False,
+                                          dtype="bf16", zipf=1.2),
+        "bf16_c3like_ep": configs.BlockConfig("bf16_c3like_ep", T=2048, H=1024, F=2048, E=8, k=2, normalize=True,
+                                              dtype="bf16"),
+    }[cfg_name]
+    world = min(torch.cuda.device_count(), 8)
+    while cfg.E % world:
+        world //= 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for rank, equal, det, err, dev_err in sorted(q.get(timeout=10) for _ in range(world)):
+        assert equal, f"rank {rank}: max |ep - single| = {err}"
+        assert det and dev_err == 0
