@@ -10,11 +10,12 @@ tokens; a step is
  2. stable expert permutation: because the experts of a rank are
     contiguous, expert-sorted rows are already grouped by destination rank
  3. all-to-all of the per-(rank, local expert) row counts   (NCCL)
- 4. all-to-all-v of the bf16 token rows and their gate weights (NCCL)
- 5. reorder the received rows from source-rank-major to expert-major
-    (segment copy kernel), run the local experts' grouped GEMMs
- 6. reorder back, reverse all-to-all-v of the fp32 output rows (NCCL)
- 7. combine the k rows of every local token in slot order (local kernel)
+ 4. grouped NCCL send/recv of the bf16 token rows and their gate weights,
+    one chunk per (peer, local expert), each received straight into its
+    expert-major position, then the local experts' grouped GEMMs
+ 5. the fp32 output rows go back chunk for chunk (NCCL send/recv) into the
+    sender's expert-sorted order
+ 6. combine the k rows of every local token in slot order (local kernel)
 
 Each token row is processed by exactly the same kernels with the same
 accumulation order as on one GPU, so the result equals the single-GPU
@@ -102,16 +103,6 @@ class CudaPrims:
     def gather(self, x, w, sorted_slots):
         return self.ops.gather_rows(x, sorted_slots), self.ops.gather_weights(w.reshape(-1), sorted_slots)
 
-    def reorder(self, src, dst, seg: Segments, reverse: bool):
-        total = int(seg.length.sum())
-        if total == 0:
-            return
-        dev = src.device
-        a = torch.from_numpy(seg.dst_start if reverse else seg.src_start).to(dev, non_blocking=True)
-        b = torch.from_numpy(seg.src_start if reverse else seg.dst_start).to(dev, non_blocking=True)
-        pre = torch.from_numpy(seg.prefix).to(dev, non_blocking=True)
-        self.ops.copy_row_segments(src, dst, a, b, pre, total)
-
     def expert_ffn(self, xs, w_rows, offsets, w_up, w_gate, w_down, out):
         return self.ops.expert_ffn(xs, w_rows, offsets, w_up, w_gate, w_down, out=out)
 
@@ -158,9 +149,29 @@ class ExpertParallelMoE:
         torch.cuda.empty_cache()
         return cls(wr, wu, wg, wd, cfg.E, cfg.k, cfg.normalize, group=group)
 
-    def _all_to_all(self, out, inp, out_splits, in_splits):
-        dist.all_to_all_single(out, inp, [int(v) for v in out_splits], [int(v) for v in in_splits],
-                               group=self.group)
+    def _exchange(self, send_buf, recv_buf, send_chunks, recv_chunks):
+        """Grouped point-to-point exchange of row chunks.  send_chunks[p] /
+        recv_chunks[p] list (start, length) row ranges for peer p, in the
+        same (local expert) order on both sides; zero-length chunks are
+        skipped on both sides alike.  The rank's own chunks are copied
+        locally."""
+        ops = []
+        for p in range(self.P):
+            if p == self.rank:
+                for (s0, n), (d0, m) in zip(send_chunks[p], recv_chunks[p]):
+                    if n:
+                        recv_buf[d0:d0 + m].copy_(send_buf[s0:s0 + n])
+                continue
+            peer = dist.get_global_rank(self.group, p) if self.group is not None else p
+            for s0, n in send_chunks[p]:
+                if n:
+                    ops.append(dist.P2POp(dist.isend, send_buf[s0:s0 + n], peer, self.group))
+            for d0, m in recv_chunks[p]:
+                if m:
+                    ops.append(dist.P2POp(dist.irecv, recv_buf[d0:d0 + m], peer, self.group))
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         T, H = x.shape
@@ -175,28 +186,29 @@ class ExpertParallelMoE:
         dist.all_to_all_single(recv_cnt_t, cnt.contiguous(), group=self.group)
         both = torch.stack([cnt, recv_cnt_t]).cpu().numpy()  # the one host sync per step
         send_cnt, recv_cnt = both[0], both[1]
-        send_splits, recv_splits, seg, local_off = plan_exchange(send_cnt, recv_cnt)
+        _, recv_splits, seg, local_off = plan_exchange(send_cnt, recv_cnt)
         self.last_plan = (send_cnt, recv_cnt)
         R = int(recv_splits.sum())
         n = xs.shape[0]
-        # dispatch rows + gate weights
-        recv_x = torch.empty((R, H), dtype=xs.dtype, device=dev)
-        recv_w = torch.empty((R,), dtype=torch.float32, device=dev)
-        self._all_to_all(recv_x, xs, recv_splits, send_splits)
-        self._all_to_all(recv_w, ws, recv_splits, send_splits)
-        # source-major -> expert-major, local experts, and back
-        xl = torch.empty_like(recv_x)
-        wl = torch.empty_like(recv_w)
-        pr.reorder(recv_x, xl, seg, reverse=False)
-        pr.reorder(recv_w, wl, seg, reverse=False)
+        # my expert-sorted rows for (p, e) are contiguous at the global expert offset
+        send_start = np.zeros(self.P * self.El + 1, dtype=np.int64)
+        np.cumsum(send_cnt.reshape(-1), out=send_start[1:])
+        send_chunks = [[(int(send_start[p * self.El + e]), int(send_cnt[p, e])) for e in range(self.El)]
+                       for p in range(self.P)]
+        # received rows land directly in expert-major order
+        dst = seg.dst_start.reshape(self.P, self.El)
+        recv_chunks = [[(int(dst[p, e]), int(recv_cnt[p, e])) for e in range(self.El)] for p in range(self.P)]
+        xl = torch.empty((R, H), dtype=xs.dtype, device=dev)
+        wl = torch.empty((R,), dtype=torch.float32, device=dev)
+        self._exchange(xs, xl, send_chunks, recv_chunks)
+        self._exchange(ws, wl, send_chunks, recv_chunks)
         dl = torch.empty((R, H), dtype=torch.float32, device=dev)
         offs = torch.from_numpy(local_off.astype(np.int32)).to(dev, non_blocking=True)
         if R:
             pr.expert_ffn(xl, wl, offs, self.w_up, self.w_gate, self.w_down, dl)
-        d_src = torch.empty_like(dl)
-        pr.reorder(dl, d_src, seg, reverse=True)
+        # results go back chunk for chunk into this rank's expert-sorted order
         ret = torch.empty((n, H), dtype=torch.float32, device=dev)
-        self._all_to_all(ret, d_src, send_splits, recv_splits)
+        self._exchange(dl, ret, recv_chunks, send_chunks)
         y = out if out is not None else torch.empty((T, H), dtype=self.out_dtype, device=dev)
         pr.combine(ret, slot_pos, T, self.k, y)
         return y

@@ -1,6 +1,6 @@
 """Expert-parallel host logic on CPU ranks (gloo, world size 2 and 4).
 
-The exchange plan, splits, segment reorders and the order of the combine are
+The exchange plan, the per-(peer, expert) chunk exchange and the combine order are
 the product code (frank_b200/ep.py); the device primitives are replaced by
 NumPy stand-ins built from the oracle, so no GPU is involved.  Every rank's
 output must equal the single-device oracle on that rank's tokens.
@@ -33,11 +33,6 @@ class NumpyPrims:
         T = x.shape[0]
         s = sorted_slots.numpy()
         return x[torch.from_numpy(s % T)].clone(), w.reshape(-1)[sorted_slots.long()].clone()
-
-    def reorder(self, src, dst, seg, reverse):
-        a, b = (seg.dst_start, seg.src_start) if reverse else (seg.src_start, seg.dst_start)
-        for s0, d0, n in zip(a, b, seg.length):
-            dst[d0:d0 + n] = src[s0:s0 + n]
 
     def expert_ffn(self, xs, w_rows, offsets, w_up, w_gate, w_down, out):
         off = offsets.numpy()
