@@ -218,6 +218,7 @@ def run_frank(args, cfg):
         runner = ep.ExpertParallelMoE.synthetic(cfg, rank, world, dev, seed=0)
         block_call = runner.__call__
     else:
+        runner = None
         dist = None
         wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, dev, seed=0)
         block = ops.MoEFFNBlock(wr, ops.PackedExperts(wu), ops.PackedExperts(wg), ops.PackedExperts(wd), cfg.E,
@@ -246,6 +247,8 @@ def run_frank(args, cfg):
 
     # ---- value: inputs resident in HBM -------------------------------------
     ops.profile_stages(True)
+    if runner is not None:
+        runner.profile = True
     l0 = ops.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clk:
@@ -258,6 +261,12 @@ def run_frank(args, cfg):
     launches = ops.launch_count() - l0
     ops.profile_stages(False)
     stage_ms = ops.profile_read() if world == 1 else {}
+    ep_info = None
+    if runner is not None:
+        runner.profile = False
+        mine = {"rank": rank, "phase_ms": runner.phase_ms(), "rows_received": int(runner.last_plan[1].sum())}
+        ep_info = [None] * world
+        dist.all_gather_object(ep_info, mine)
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
     value = cfg.T * world / (ms / 1e3)
 
@@ -309,6 +318,8 @@ def run_frank(args, cfg):
         }
         line["stage_ms"] = stage_ms
         line["block_frac_of_peak"] = line["tflops"] / peak
+    if ep_info:
+        line["ep_ranks"] = ep_info
     line["e2e"] = e2e
     line["gpu_launches"] = int(launches)
     line["clocks"] = clk.summary()

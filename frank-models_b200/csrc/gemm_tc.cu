@@ -44,6 +44,7 @@ constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KiB
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
 constexpr int kMaxExperts = 1024;
+constexpr int kMaxPeers = 8;
 
 enum Mode { SWIGLU = 0, SCALE = 1, PLAIN = 2 };
 
@@ -57,6 +58,11 @@ struct Params {
   int64_t ldo;
   const float* wrow;       // SCALE: per sorted row weight
   int32_t* err;            // device error word
+  // SCALE with a row map: row r goes to peer_out[row_rank[r]] + row_pos[r] * ldo
+  // (another GPU's buffer reached over NVLink) instead of out + r * ldo.
+  const int32_t* row_rank;
+  const int32_t* row_pos;
+  float* peer_out[kMaxPeers];
 };
 
 // ------------------------------------------------------------ PTX glue --
@@ -339,6 +345,8 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
         }
       } else {
         float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+        if (MODE == SCALE && p.row_rank != nullptr && valid)
+          out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
         const float s = (MODE == SCALE && valid) ? p.wrow[row] : 1.f;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
@@ -358,6 +366,9 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(a));
     }
+    // rows stored into other GPUs' memory must be visible to them once this
+    // kernel has completed
+    if (MODE == SCALE && p.row_rank != nullptr) __threadfence_system();
   }
 
   tc_fence_before();
@@ -452,7 +463,8 @@ int check_tc_shapes(int64_t rows, int64_t N, int64_t K, int64_t E) {
 // mode: 0 SWIGLU (B = gate, B2 = up, out bf16 [rows, N]), 1 SCALE, 2 PLAIN
 // (out fp32 [rows, N]).  A: bf16 [rows, K]; B/B2: bf16 [E, N, K].
 int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B2, const int32_t* offsets, int64_t E,
-                           int64_t rows, int64_t N, int64_t K, const float* wrow, void* out, cudaStream_t st) {
+                           int64_t rows, int64_t N, int64_t K, const float* wrow, void* out, cudaStream_t st,
+                           const int32_t* row_rank, const int32_t* row_pos, float* const* peer_out, int n_peers) {
   if (rows == 0) return FRANK_OK;
   FRANK_TRY(check_tc_shapes(rows, N, K, E));
   if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)(B2 ? B2 : B) | (uintptr_t)out) % 16 != 0) {
@@ -474,6 +486,13 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
   p.ldo = N;
   p.wrow = wrow;
   p.err = device_error_word();
+  p.row_rank = row_rank;
+  p.row_pos = row_pos;
+  for (int i = 0; i < kMaxPeers; ++i) p.peer_out[i] = (peer_out && i < n_peers) ? peer_out[i] : nullptr;
+  if (row_rank && (mode != SCALE || !row_pos || !peer_out || n_peers < 1 || n_peers > kMaxPeers)) {
+    set_error("tc_grouped_gemm: a row map needs SCALE mode, row_pos and 1..%d peer buffers", kMaxPeers);
+    return FRANK_EINVAL;
+  }
   size_t smem = smem_bytes((int)E);
   dim3 grid(num_sms()), block(THREADS);
   switch (mode) {

@@ -119,7 +119,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, wr, w_up_local, w_gate_local, w_down_local, n_expert: int, n_expert_used: int,
-                 normalize_weights: bool, group=None, prims=None, out_dtype=torch.float32):
+                 normalize_weights: bool, group=None, prims=None, out_dtype=torch.float32, mode: str | None = None):
         self.group = group
         self.P = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -135,6 +135,17 @@ class ExpertParallelMoE:
         self.prims = prims if prims is not None else CudaPrims()
         self.out_dtype = out_dtype
         self.last_plan = None
+        self.profile = False       # record CUDA events between the phases of each call
+        self._marks = []
+        # "p2p": rows move by P2P stores into symmetric (peer-mapped) buffers from
+        # the dispatch kernel and the down-GEMM epilogue; "nccl": grouped NCCL
+        # send/recv of row chunks (also the path the CPU tests drive).
+        if mode is None:
+            mode = "p2p" if (prims is None and w_up_local.is_cuda and self.P <= 8) else "nccl"
+        if mode not in ("p2p", "nccl"):
+            raise ValueError(f"mode must be 'p2p' or 'nccl', got {mode!r}")
+        self.mode = mode
+        self._symm = None
 
     @classmethod
     def synthetic(cls, cfg, rank, world, device, seed=0, group=None):
@@ -173,15 +184,134 @@ class ExpertParallelMoE:
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
 
+    # phase boundaries (nccl mode / p2p mode):
+    #   route+permute(+gather) | counts (+plan) | dispatch (+barrier) | expert GEMMs
+    #   | return (p2p: barrier only, the rows went back from the GEMM epilogue) | combine
+    PHASES = ("route_permute", "counts_plan", "dispatch", "expert_ffn", "return", "combine")
+
+    def _mark(self):
+        if self.profile:
+            e = torch.cuda.Event(enable_timing=True)
+            e.record()
+            self._marks[-1].append(e)
+
+    def phase_ms(self) -> dict:
+        """Mean per-phase milliseconds over the profiled calls since the last read."""
+        torch.cuda.synchronize()
+        acc = np.zeros(len(self.PHASES))
+        calls = [m for m in self._marks if len(m) == len(self.PHASES) + 1]
+        for m in calls:
+            acc += [m[i].elapsed_time(m[i + 1]) for i in range(len(self.PHASES))]
+        self._marks = []
+        return dict(zip(self.PHASES, (acc / max(len(calls), 1)).tolist()))
+
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if self.mode == "p2p":
+            return self._call_p2p(x, out)
+        return self._call_nccl(x, out)
+
+    # ------------------------------------------------------------ p2p mode --
+    def _symmetric(self, T: int, dev):
+        """Symmetric receive / return buffers sized for T tokens per rank (every
+        rank calls with the same T; the dispatch kernel refuses rows beyond the
+        capacity):
+        recv_x [P*k*T, H] bf16, recv_w [P*k*T] fp32, ret [k*T, H] fp32, and the
+        peer addresses of every rank's copy.  Allocated collectively."""
+        if self._symm is not None and self._symm["T"] >= T:
+            return self._symm
+        import torch.distributed._symmetric_memory as symm_mem
+
+        H, k, P = self.H, self.k, self.P
+        cap, n = P * k * T, k * T
+
+        def al(b):
+            return (b + 255) // 256 * 256
+
+        sizes = [al(cap * H * 2), al(cap * 4), al(n * H * 4)]
+        base = [0, sizes[0], sizes[0] + sizes[1]]
+        self._symm = None
+        torch.cuda.synchronize()
+        buf = symm_mem.empty(sum(sizes), dtype=torch.uint8, device=dev)
+        grp = self.group if self.group is not None else dist.group.WORLD
+        hdl = symm_mem.rendezvous(buf, group=grp.group_name)
+        ptrs = [int(p) for p in hdl.buffer_ptrs]
+        import ctypes
+
+        arr = lambda vals: (ctypes.c_void_p * self.P)(*vals)  # noqa: E731
+        self._symm = {
+            "T": T, "buf": buf, "hdl": hdl, "cap": cap,
+            "recv_x": buf[base[0]:base[0] + cap * H * 2].view(torch.bfloat16).view(cap, H),
+            "recv_w": buf[base[1]:base[1] + cap * 4].view(torch.float32),
+            "ret": buf[base[2]:base[2] + n * H * 4].view(torch.float32).view(n, H),
+            "peer_x": arr([q + base[0] for q in ptrs]),
+            "peer_w": arr([q + base[1] for q in ptrs]),
+            "peer_ret": arr([q + base[2] for q in ptrs]),
+            "dst_base": torch.empty(self.E, dtype=torch.int32, device=dev),
+            "local_off": torch.empty(self.El + 1, dtype=torch.int32, device=dev),
+            "row_rank": torch.empty(cap, dtype=torch.int32, device=dev),
+            "row_pos": torch.empty(cap, dtype=torch.int32, device=dev),
+            "counts": torch.empty((self.P, self.E), dtype=torch.int32, device=dev),
+            "flag": torch.zeros(1, dtype=torch.int32, device=dev),
+            "hs": torch.empty(max(cap * self.F * 2 + 256, 1), dtype=torch.uint8, device=dev),
+        }
+        return self._symm
+
+    def _barrier(self, flag):
+        # stream-ordered: every rank's preceding kernels (and their stores into
+        # peer memory) have completed when this collective completes
+        dist.all_reduce(flag, group=self.group)
+
+    def _call_p2p(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        from . import _lib, ops
+
+        T, H = x.shape
+        dev = x.device
+        lib = _lib.load()
+        st = torch.cuda.current_stream().cuda_stream
+        S = self._symmetric(T, dev)
+        if self.profile:
+            self._marks.append([])
+        self._mark()
+        w, ids = ops.router_topk(x, self.wr, self.k, self.normalize)
+        sorted_slots, offsets, slot_pos, _ = ops.permute(ids, self.E)
+        cnt = (offsets[1:] - offsets[:-1]).contiguous()
+        self._mark()
+        dist.all_gather_into_tensor(S["counts"], cnt, group=self.group)
+        _lib.check(lib.frank_ep_plan(S["counts"].data_ptr(), self.P, self.El, self.rank, S["dst_base"].data_ptr(),
+                                     S["local_off"].data_ptr(), S["row_rank"].data_ptr(), S["row_pos"].data_ptr(),
+                                     S["cap"], st))
+        self._mark()
+        _lib.check(lib.frank_ep_dispatch(x.data_ptr(), T, H, w.data_ptr(), sorted_slots.data_ptr(),
+                                         offsets.data_ptr(), self.E, self.El, self.k * T, S["dst_base"].data_ptr(),
+                                         S["peer_x"], S["peer_w"], self.P, S["cap"], st))
+        self._barrier(S["flag"])
+        self._mark()
+        _lib.check(lib.frank_expert_ffn_scatter(
+            S["recv_x"].data_ptr(), S["recv_w"].data_ptr(), S["local_off"].data_ptr(), self.El, S["cap"], H, self.F,
+            self.w_up.data_ptr(), self.w_gate.data_ptr(), self.w_down.data_ptr(), S["row_rank"].data_ptr(),
+            S["row_pos"].data_ptr(), S["peer_ret"], self.P, S["hs"].data_ptr(), S["hs"].numel(), st))
+        self._mark()
+        self._barrier(S["flag"])
+        self._mark()
+        y = out if out is not None else torch.empty((T, H), dtype=self.out_dtype, device=dev)
+        ops.combine(S["ret"], slot_pos, T, self.k, y)
+        self._mark()
+        return y
+
+    # ----------------------------------------------------------- nccl mode --
+    def _call_nccl(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         T, H = x.shape
         dev = x.device
         pr = self.prims
+        if self.profile:
+            self._marks.append([])
+        self._mark()
         w, ids = pr.route(x, self.wr, self.k, self.normalize)
         sorted_slots, offsets, slot_pos = pr.permute(ids, self.E)
         xs, ws = pr.gather(x, w, sorted_slots)
         # per-(destination rank, its local expert) counts
         cnt = (offsets[1:] - offsets[:-1]).to(torch.int64).reshape(self.P, self.El)
+        self._mark()
         recv_cnt_t = torch.empty_like(cnt)
         dist.all_to_all_single(recv_cnt_t, cnt.contiguous(), group=self.group)
         both = torch.stack([cnt, recv_cnt_t]).cpu().numpy()  # the one host sync per step
@@ -200,15 +330,20 @@ class ExpertParallelMoE:
         recv_chunks = [[(int(dst[p, e]), int(recv_cnt[p, e])) for e in range(self.El)] for p in range(self.P)]
         xl = torch.empty((R, H), dtype=xs.dtype, device=dev)
         wl = torch.empty((R,), dtype=torch.float32, device=dev)
+        self._mark()
         self._exchange(xs, xl, send_chunks, recv_chunks)
         self._exchange(ws, wl, send_chunks, recv_chunks)
         dl = torch.empty((R, H), dtype=torch.float32, device=dev)
         offs = torch.from_numpy(local_off.astype(np.int32)).to(dev, non_blocking=True)
+        self._mark()
         if R:
             pr.expert_ffn(xl, wl, offs, self.w_up, self.w_gate, self.w_down, dl)
         # results go back chunk for chunk into this rank's expert-sorted order
         ret = torch.empty((n, H), dtype=torch.float32, device=dev)
+        self._mark()
         self._exchange(dl, ret, recv_chunks, send_chunks)
+        self._mark()
         y = out if out is not None else torch.empty((T, H), dtype=self.out_dtype, device=dev)
         pr.combine(ret, slot_pos, T, self.k, y)
+        self._mark()
         return y

@@ -216,6 +216,47 @@ int frank_copy_row_segments(const void* src, void* dst,
                             void* stream);
 
 /*
+ * Expert-parallel exchange over NVLink peer memory (no counterpart in the
+ * reference, which runs on one device).  E experts are split evenly over P
+ * ranks (El = E / P each, contiguous).  counts_all [P][E] int32 holds every
+ * rank's per-expert row counts (all-gathered by the caller).
+ *
+ * frank_ep_plan: dst_base [E] = first row of this rank's chunk for expert g
+ *   in the owning rank's expert-major receive buffer; local_offsets [El+1] =
+ *   this rank's expert row offsets; row_rank / row_pos [capacity] = for each
+ *   received row, the source rank and its row in that rank's expert-sorted
+ *   order (filled for the rows actually received, below `capacity`).
+ * frank_ep_dispatch: for this rank's n_slots expert-sorted slots, copies the
+ *   bf16 token row x[sorted_slots[r] % T] and gate weight w[sorted_slots[r]]
+ *   into peer_x[p] / peer_w[p] (device addresses of every rank's receive
+ *   buffers of `capacity` rows, P <= 8) at the planned rows.  A planned row
+ *   outside [0, capacity) is skipped and FRANK_EINVAL is recorded in the
+ *   device error word (frank_read_device_error).
+ * frank_expert_ffn_scatter: frank_expert_ffn (bf16) whose fp32 output row r
+ *   is stored at peer_out[row_rank[r]] + row_pos[r] * H, i.e. straight into
+ *   the return buffer of the rank the row came from.
+ * Stores to other GPUs complete with the kernels; the caller orders the
+ *   ranks' steps (e.g. an NCCL collective on the same stream) before a rank
+ *   reads what its peers wrote.  No kernel here waits on another GPU.
+ */
+int frank_ep_plan(const int32_t* counts_all, int P, int El, int rank,
+                  int32_t* dst_base, int32_t* local_offsets, int32_t* row_rank,
+                  int32_t* row_pos, int64_t capacity, void* stream);
+int frank_ep_dispatch(const void* x, int64_t T, int64_t H, const float* w,
+                      const int32_t* sorted_slots, const int32_t* offsets,
+                      int64_t E, int64_t El, int64_t n_slots,
+                      const int32_t* dst_base, void* const* peer_x,
+                      float* const* peer_w, int P, int64_t capacity,
+                      void* stream);
+int frank_expert_ffn_scatter(const void* xs, const float* w_rows,
+                             const int32_t* offsets, int64_t E, int64_t rows,
+                             int64_t H, int64_t F, const void* w_up_p,
+                             const void* w_gate_p, const void* w_down_p,
+                             const int32_t* row_rank, const int32_t* row_pos,
+                             void* const* peer_out, int n_peers,
+                             void* workspace, size_t ws_bytes, void* stream);
+
+/*
  * Device error word written by bounded waits inside the persistent GEMM
  * kernels (0 = none).  frank_read_device_error copies it to *out and resets
  * it; synchronises the stream.

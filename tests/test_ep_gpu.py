@@ -20,7 +20,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, cfg, q):
+def _worker(rank, world, port, cfg, mode, q):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -35,7 +35,7 @@ def _worker(rank, world, port, cfg, q):
         El = cfg.E // world
         sl = slice(rank * El, (rank + 1) * El)
         moe = ep.ExpertParallelMoE(wr, wu[sl].contiguous(), wg[sl].contiguous(), wd[sl].contiguous(), cfg.E, cfg.k,
-                                   cfg.normalize)
+                                   cfg.normalize, mode=mode)
         y = moe(x)
         y2 = moe(x)
         single = ops.MoEFFNBlock(wr, ops.PackedExperts(wu), ops.PackedExperts(wg), ops.PackedExperts(wd), cfg.E,
@@ -49,8 +49,9 @@ def _worker(rank, world, port, cfg, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
 @pytest.mark.parametrize("cfg_name", ["bf16_fg_ep", "bf16_c3like_ep"])
-def test_ep_equals_single_gpu(cfg_name):
+def test_ep_equals_single_gpu(cfg_name, mode):
     from frank_b200 import configs
 
     cfg = {
@@ -65,7 +66,7 @@ def test_ep_equals_single_gpu(cfg_name):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, mode, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
