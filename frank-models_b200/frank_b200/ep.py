@@ -219,6 +219,10 @@ class ExpertParallelMoE:
         peer addresses of every rank's copy.  Allocated collectively."""
         if self._symm is not None and self._symm["T"] >= T:
             return self._symm
+        import os
+
+        # plain peer mappings only: no multicast object is bound to these buffers
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem
 
         H, k, P = self.H, self.k, self.P
