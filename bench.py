@@ -264,7 +264,7 @@ def run_frank(args, cfg):
     ep_info = None
     if runner is not None:
         runner.profile = False
-        mine = {"rank": rank, "phase_ms": runner.phase_ms(), "rows_received": int(runner.last_plan[1].sum())}
+        mine = {"rank": rank, "phase_ms": runner.phase_ms(), "rows_received": runner.rows_received(), "mode": runner.mode}
         ep_info = [None] * world
         dist.all_gather_object(ep_info, mine)
     ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps

@@ -195,6 +195,12 @@ class ExpertParallelMoE:
             e.record()
             self._marks[-1].append(e)
 
+    def rows_received(self) -> int:
+        """Rows this rank's experts processed in the most recent call (synchronises)."""
+        if self.mode == "p2p" and self._symm is not None:
+            return int(self._symm["local_off"][-1].item())
+        return int(self.last_plan[1].sum()) if self.last_plan is not None else 0
+
     def phase_ms(self) -> dict:
         """Mean per-phase milliseconds over the profiled calls since the last read."""
         torch.cuda.synchronize()
