@@ -249,13 +249,24 @@ def run_frank(args, cfg):
     ops.profile_stages(True)
     if runner is not None:
         runner.profile = True
+    # Decode-sized steps touch less than the 126 MB L2 (T=1 reads ~75 MB of
+    # weights): flush L2 between steps (a 256 MiB write, outside the timed
+    # spans) and time every step on its own.
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if cfg.T <= 64 else None
     l0 = ops.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)] if flush is not None else []
     with ClockSampler(local) as clk:
         barrier()
         ev0.record(stream)
-        for _ in range(args.steps):
+        for i in range(args.steps):
+            if flush is not None:
+                flush.zero_()
+                step_ev[i][0].record(stream)
             block_call(x, out=y)
+            if flush is not None:
+                step_ev[i][1].record(stream)
         ev1.record(stream)
         barrier()
     launches = ops.launch_count() - l0
@@ -267,8 +278,15 @@ def run_frank(args, cfg):
         mine = {"rank": rank, "phase_ms": runner.phase_ms(), "rows_received": runner.rows_received(), "mode": runner.mode}
         ep_info = [None] * world
         dist.all_gather_object(ep_info, mine)
-    ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
+    if flush is not None:
+        ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in step_ev)) / args.steps
+    else:
+        ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
     value = cfg.T * world / (ms / 1e3)
+    n_distinct = None
+    if world == 1:
+        _, _, rid = block(x, return_routing=True)
+        n_distinct = int(torch.unique(rid).numel())
 
     # ---- e2e: host x in, host y out, through the public API ---------------
     x_host = x.cpu().pin_memory()
@@ -305,7 +323,26 @@ def run_frank(args, cfg):
         "config": config_dict(cfg, world),
         "tflops": cfg.flops * world / (ms / 1e3) / 1e12,
     }
-    if stage_ms:
+    if flush is not None:
+        line["config"]["l2"] = "L2 flushed (256 MiB write) before every timed step; steps timed individually"
+    if stage_ms and cfg.T <= 64:
+        # decode: weight streaming, HBM-bound.  Algorithmic bytes of the gate/up
+        # GEMM = distinct experts x 2 matrices x F x H bf16 + rows read + h written.
+        rows = cfg.k * cfg.T
+        gu_bytes = n_distinct * 2 * cfg.F * cfg.H * 2 + rows * cfg.H * 2 + rows * cfg.F * 2
+        blk_bytes = (n_distinct * 3 * cfg.F * cfg.H * 2 + cfg.E * cfg.H * 4 + cfg.T * cfg.H * 2 + cfg.T * cfg.H * 4)
+        gu_ms = stage_ms["gate_up_gemm"]
+        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+        peak = float(pk["hbm_gbs"])
+        line["roofline"] = {
+            "kernel": "tc_grouped_gemm<SWIGLU> (gate/up GEMM + swiglu)", "bound": "hbm", "achieved": achieved,
+            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{pk_kind} hbm_gbs",
+            "traffic": None, "bytes_per_launch": gu_bytes, "ms_per_launch": gu_ms, "distinct_experts": n_distinct,
+        }
+        line["stage_ms"] = stage_ms
+        line["block_hbm_gbs"] = blk_bytes / (ms / 1e3) / 1e9
+        line["block_frac_of_hbm"] = line["block_hbm_gbs"] / peak
+    elif stage_ms:
         gu_flops = 4.0 * cfg.k * cfg.T * cfg.H * cfg.F
         gu_ms = stage_ms["gate_up_gemm"]
         achieved = gu_flops / (gu_ms / 1e3) / 1e12
@@ -329,6 +366,49 @@ def run_frank(args, cfg):
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_mul_mat_id(args, cfg):
+    """mul_mat_id alone (bf16 in, fp32 accumulate and output), one GPU."""
+    import numpy as np
+    import torch
+
+    from frank_b200 import ops
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    w = torch.empty((cfg.E, cfg.n_out, cfg.n_in), dtype=torch.float32, device=dev).normal_(0, 0.02, generator=g)
+    wp = ops.PackedExperts(w.bfloat16())
+    del w
+    x = torch.empty((cfg.n_in, 1, cfg.T), dtype=torch.float32, device=dev).normal_(0, 1, generator=g)
+    inp = x.expand(cfg.n_in, cfg.k, cfg.T).contiguous().bfloat16()
+    rng = np.random.default_rng(0)
+    ids = torch.from_numpy(np.stack([rng.permutation(cfg.E)[: cfg.k] for _ in range(cfg.T)], axis=1)
+                           .astype(np.int32)).to(dev)
+    for _ in range(args.warmup):
+        ops.mul_mat_id(wp, inp, ids, check_ids=False)
+    torch.cuda.synchronize()
+    l0 = ops.launch_count()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(0) as clk:
+        ev0.record()
+        for _ in range(args.steps):
+            ops.mul_mat_id(wp, inp, ids, check_ids=False)
+        ev1.record()
+        torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1) / args.steps
+    pk, pk_kind = peaks()
+    tf = cfg.flops / (ms / 1e3) / 1e12
+    line = {"metric": "mul_mat_id tokens/s", "value": cfg.T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": cfg.name, "n_tokens": cfg.T, "n_in": cfg.n_in, "n_out": cfg.n_out,
+                       "n_expert": cfg.E, "n_expert_used": cfg.k, "output": "fp32 [n_out, k, T]"},
+            "tflops": tf, "frac_of_sustained_bf16": tf / float(pk["bf16_tflops_sustained"]),
+            "gpu_launches": int(ops.launch_count() - l0), "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
 
 
 def cpu_baseline_from_device(cfg, x, block):
@@ -360,6 +440,12 @@ def main():
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     from frank_b200 import configs
 
+    if args.config == configs.C2.name:
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference arm covers moe_ffn_block configs"}))
+            return
+        run_mul_mat_id(args, configs.C2)
+        return
     cfg = configs.BLOCK_CONFIGS[args.config]
     if args.impl == "reference":
         run_reference(args, cfg)
