@@ -57,6 +57,7 @@ constexpr int kStages = 6;
 constexpr int kProfCalls = 64;
 struct StageProfiler {
   bool on = false;
+  bool fixed = false;  // graph-capture mode: always the first event set, kept across reads
   bool init = false;
   int calls = 0;    // calls recorded in the current window
   int marks = 0;    // marks recorded in the current call
@@ -72,6 +73,11 @@ static void prof_mark(int i, cudaStream_t st) {
     for (auto& set : g_prof.ev)
       for (auto& e : set) cudaEventCreate(&e);
     g_prof.init = true;
+  }
+  if (g_prof.fixed) {
+    cudaEventRecord(g_prof.ev[0][i], st);
+    if (i == kStages) g_prof.calls = 1;
+    return;
   }
   if (g_prof.calls >= kProfCalls) return;
   cudaEventRecord(g_prof.ev[g_prof.calls][i], st);
@@ -428,7 +434,10 @@ int frank_read_device_error(int32_t* out, void* stream) {
 uint64_t frank_launch_count(void) { return g_launches.load(); }
 
 int frank_profile_stages(int enable) {
+  std::lock_guard<std::mutex> lk(g_prof_mu);
   g_prof.on = enable != 0;
+  g_prof.fixed = enable == 2;
+  if (enable) g_prof.calls = 0;
   return FRANK_OK;
 }
 
@@ -450,7 +459,7 @@ int frank_profile_read(float* stage_ms, int max_stages, int* n_stages) {
     stage_ms[i] = (float)(acc / g_prof.calls);
   }
   if (n_stages) *n_stages = g_prof.calls;
-  g_prof.calls = 0;
+  if (!g_prof.fixed) g_prof.calls = 0;
   return FRANK_OK;
 }
 

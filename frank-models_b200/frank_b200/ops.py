@@ -270,6 +270,42 @@ class MoEFFNBlock:
         return y
 
 
+class GraphedMoEFFN:
+    """A :class:`MoEFFNBlock` call for a fixed token count captured once in a
+    CUDA graph (the small, launch-bound decode steps).  ``x`` and ``y`` are the
+    graph's static input and output buffers: copy tokens into ``x``, call
+    :meth:`replay`, read ``y``.  The block's workspace is held for the life of
+    this object."""
+
+    def __init__(self, block: "MoEFFNBlock", T: int, device=None):
+        device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.block = block
+        self.x = torch.zeros((T, block.H), dtype=block.dtype, device=device)
+        self.y = torch.empty((T, block.H), dtype=block.out_dtype, device=device)
+        block._workspace(T, device)
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            block(self.x, out=self.y)  # warm-up outside capture (attributes, tensor maps)
+        torch.cuda.current_stream(device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=side):
+            block(self.x, out=self.y)
+        torch.cuda.current_stream(device).wait_stream(side)
+
+    def replay(self) -> torch.Tensor:
+        self.graph.replay()
+        return self.y
+
+    def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        self.x.copy_(x, non_blocking=True)
+        self.graph.replay()
+        if out is not None:
+            out.copy_(self.y, non_blocking=True)
+            return out
+        return self.y
+
+
 def read_device_error() -> int:
     """Return and clear the device error word of bounded in-kernel waits."""
     import ctypes
@@ -287,9 +323,10 @@ def launch_count() -> int:
     return int(_lib.load().frank_launch_count())
 
 
-def profile_stages(enable: bool) -> None:
-    """Record CUDA events around each stage of moe_ffn_block (measurement only)."""
-    _lib.check(_lib.load().frank_profile_stages(int(bool(enable))))
+def profile_stages(enable) -> None:
+    """Record CUDA events around each stage of moe_ffn_block (measurement only).
+    enable=2: graph-capture form (one event set, re-recorded by every replay)."""
+    _lib.check(_lib.load().frank_profile_stages(2 if enable == 2 else int(bool(enable))))
 
 
 def profile_read() -> dict:

@@ -276,6 +276,9 @@ uint64_t frank_launch_count(void);
  * in milliseconds over the window's calls, stores the number of calls in
  * *n_stages and starts a new window.  Events belong to the device current at
  * the first enabled call.  Measurement only; off by default.
+ * enable = 2 is the graph-capture form: every call records into the same
+ * single event set (so a captured graph re-records it on each replay) and
+ * reading does not clear it.
  */
 int frank_profile_stages(int enable);
 int frank_profile_read(float* stage_ms, int max_stages, int* n_stages);
