@@ -75,7 +75,8 @@ static void prof_mark(int i, cudaStream_t st) {
     g_prof.init = true;
   }
   if (g_prof.fixed) {
-    cudaEventRecord(g_prof.ev[0][i], st);
+    // external record nodes: a captured graph records the event on each replay
+    cudaEventRecordWithFlags(g_prof.ev[0][i], st, cudaEventRecordExternal);
     if (i == kStages) g_prof.calls = 1;
     return;
   }
