@@ -76,7 +76,12 @@ static void prof_mark(int i, cudaStream_t st) {
   }
   if (g_prof.fixed) {
     // external record nodes: a captured graph records the event on each replay
-    cudaEventRecordWithFlags(g_prof.ev[0][i], st, cudaEventRecordExternal);
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaStreamIsCapturing(st, &cs);
+    if (cs == cudaStreamCaptureStatusActive)
+      cudaEventRecordWithFlags(g_prof.ev[0][i], st, cudaEventRecordExternal);
+    else
+      cudaEventRecord(g_prof.ev[0][i], st);
     if (i == kStages) g_prof.calls = 1;
     return;
   }
