@@ -442,8 +442,10 @@ uint64_t frank_launch_count(void) { return g_launches.load(); }
 int frank_profile_stages(int enable) {
   std::lock_guard<std::mutex> lk(g_prof_mu);
   g_prof.on = enable != 0;
-  g_prof.fixed = enable == 2;
-  if (enable) g_prof.calls = 0;
+  if (enable) {  // disabling keeps the mode so recorded events can still be read
+    g_prof.fixed = enable == 2;
+    g_prof.calls = 0;
+  }
   return FRANK_OK;
 }
 
