@@ -1,0 +1,410 @@
+// Decode-sized MoE FFN block (a few tokens per step): three launches,
+// weight-streaming on CUDA cores.
+//
+// With T <= 64 tokens an expert receives a handful of rows, so the block is
+// bound by reading the active experts' weights from HBM (3 x H x F bf16 per
+// active expert) -- tensor cores would idle on 128-row tiles.  The three
+// kernels:
+//   decode_route_kernel    router logits (one warp per (expert, 8 tokens)),
+//                          then the last block to finish runs softmax +
+//                          top-k + renorm for every token and the stable
+//                          expert permutation (moe_ffn_block.mlir:54-128,
+//                          mul_mat_id.mlir:51-53);
+//   decode_gateup_kernel   one block per (expert, 32 rows of F): streams the
+//                          gate and up rows once, dots them with the
+//                          expert's token rows (gathered straight from x),
+//                          writes h = gate * silu(up) (swiglu.mlir:37-47);
+//   decode_down_kernel     one block per 8 rows of H: every warp streams the
+//                          down rows of its experts, scales by the gate
+//                          weight, and the block sums the k slots of every
+//                          token in slot order (moe_ffn_block.mlir:158-206)
+//                          -- the combine is fused, deterministic, no atomics.
+// The only atomic is the completion ticket of the route kernel; it resets
+// itself, and the launcher zeroes it at every call.
+#include "common.cuh"
+#include "topk.cuh"
+
+namespace {
+
+using namespace frank_topk;
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kRouteTok = 8;    // tokens per route warp item
+constexpr int kMaxSlots = 2048; // k * T handled by the decode path
+constexpr int kRC = 8;          // token rows per pass over an expert's weights
+constexpr int kFRows = 4;       // gate/up rows (each of gate and up) per warp
+constexpr int kHRows = 8;       // down rows per block
+
+__device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+
+template <class TW>
+__device__ __forceinline__ void load8_w(const TW* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void load8_w<float>(const float* p, float (&v)[8]) {
+  float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8_w<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
+  bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(p)), v);
+}
+
+struct DecodeWs {
+  float* logits;        // [E, T]
+  unsigned* ticket;     // completion counter of the route kernel
+  float* w;             // [k, T] gate weights
+  int32_t* ids;         // [k, T]
+  int32_t* sorted_slots;
+  int32_t* offsets;     // [E + 1]
+  int32_t* slot_pos;
+  float* wsorted;
+  __nv_bfloat16* hs;    // [k*T, F]
+};
+
+// ----------------------------------------------------------------- route --
+template <class TW>
+__global__ void __launch_bounds__(kThreads)
+decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr, int T, int H, int E, int k,
+                    int normalize, DecodeWs ws) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tchunks = (T + kRouteTok - 1) / kRouteTok;
+  const int item = blockIdx.x * kWarps + warp;
+  if (item < E * tchunks) {
+    const int e = item / tchunks, t0 = (item - e * tchunks) * kRouteTok;
+    float acc[kRouteTok];
+#pragma unroll
+    for (int a = 0; a < kRouteTok; ++a) acc[a] = 0.f;
+    for (int h = lane * 8; h < H; h += 256) {
+      float wv[8];
+      load8_w(wr + (int64_t)e * H + h, wv);
+#pragma unroll
+      for (int a = 0; a < kRouteTok; ++a) {
+        if (t0 + a < T) {
+          float xv[8];
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)(t0 + a) * H + h)), xv);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[a] = fmaf(wv[i], xv[i], acc[a]);
+        }
+      }
+    }
+#pragma unroll
+    for (int a = 0; a < kRouteTok; ++a) {
+      float v = acc[a];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      if (lane == 0 && t0 + a < T) ws.logits[(int64_t)e * T + t0 + a] = v;
+    }
+  }
+  // ---- the last block: softmax + top-k for every token, then the permutation
+  __shared__ unsigned s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) s_last = (atomicAdd(ws.ticket, 1u) == gridDim.x - 1);
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  __shared__ float lg[kWarps][kMaxE];
+  for (int t = warp; t < T; t += kWarps) {
+    for (int e = lane; e < E; e += 32) lg[warp][e] = ws.logits[(int64_t)e * T + t];
+    __syncwarp();
+    warp_softmax_topk(lg[warp], E, k, normalize, ws.w, ws.ids, T, t);
+    __syncwarp();
+  }
+  __syncthreads();
+  // stable counting sort of the n = k*T flat slots by expert (same order as
+  // argsort(ids.reshape(-1), stable)); one block, warp-level ranks
+  __shared__ int32_t running[kMaxE + 1];
+  __shared__ int32_t warp_cnt[kWarps][kMaxE];
+  __shared__ int32_t rank[kMaxSlots];
+  const int n = k * T;
+  for (int e = threadIdx.x; e < E; e += kThreads) {
+    running[e] = 0;
+    for (int w2 = 0; w2 < kWarps; ++w2) warp_cnt[w2][e] = 0;
+  }
+  __syncthreads();
+  for (int base = 0; base < n; base += kThreads) {
+    const int s = base + threadIdx.x;
+    const int e = s < n ? ws.ids[s] : -1;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int rank_w = __popc(peers & ((1u << lane) - 1u));
+    const int leader = __ffs(peers) - 1;
+    if (e >= 0 && lane == leader) warp_cnt[warp][e] = __popc(peers);
+    __syncthreads();
+    int pos = 0;
+    bool last = false;
+    if (e >= 0) {
+      int before = 0;
+      for (int w2 = 0; w2 < warp; ++w2) before += warp_cnt[w2][e];
+      pos = running[e] + before + rank_w;
+      rank[s] = pos;
+      last = (lane == 31 - __clz(peers));
+      for (int w2 = warp + 1; w2 < kWarps && last; ++w2)
+        if (warp_cnt[w2][e] != 0) last = false;
+    }
+    __syncthreads();
+    if (last) running[e] = pos + 1;
+    if (e >= 0 && lane == leader) warp_cnt[warp][e] = 0;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {  // exclusive scan of the counts (E <= 256)
+    int32_t acc = 0;
+    for (int e = 0; e < E; ++e) {
+      const int32_t c = running[e];
+      ws.offsets[e] = acc;
+      running[e] = acc;
+      acc += c;
+    }
+    ws.offsets[E] = acc;
+    *ws.ticket = 0;  // ready for the next call
+  }
+  __syncthreads();
+  for (int s = threadIdx.x; s < n; s += kThreads) {
+    const int32_t pos = running[ws.ids[s]] + rank[s];
+    ws.sorted_slots[pos] = s;
+    ws.slot_pos[s] = pos;
+    ws.wsorted[pos] = ws.w[s];
+  }
+}
+
+// --------------------------------------------------------------- gate/up --
+// Block (f-chunk, expert e): kWarps warps x kFRows rows of gate and of up.
+// The expert's token rows (<= kRC per pass) are staged in shared memory as
+// bf16; each lane streams 16-byte slices of its 2*kFRows weight rows.
+__global__ void __launch_bounds__(kThreads)
+decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
+                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, DecodeWs ws) {
+  extern __shared__ uint4 xsm[];  // [kRC][H/8]
+  const int e = blockIdx.y;
+  const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
+  if (cnt == 0) return;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int f0 = (blockIdx.x * kWarps + warp) * kFRows;
+  const int hv = H / 8;
+  const __nv_bfloat16* wg = w_gate + (int64_t)e * F * H;
+  const __nv_bfloat16* wu = w_up + (int64_t)e * F * H;
+  for (int c0 = 0; c0 < cnt; c0 += kRC) {
+    const int rc = min(kRC, cnt - c0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
+      const int r = i / hv, v = i - r * hv;
+      const int t = ws.sorted_slots[r0 + c0 + r] % T;
+      xsm[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
+    }
+    __syncthreads();
+    if (f0 >= F) continue;
+    float ag[kFRows][kRC], au[kFRows][kRC];
+#pragma unroll
+    for (int j = 0; j < kFRows; ++j)
+#pragma unroll
+      for (int r = 0; r < kRC; ++r) ag[j][r] = au[j][r] = 0.f;
+    for (int v = lane; v < hv; v += 32) {
+      float gv[kFRows][8], uv[kFRows][8];
+#pragma unroll
+      for (int j = 0; j < kFRows; ++j) {
+        const int f = min(f0 + j, F - 1);
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wg + (int64_t)f * H) + v), gv[j]);
+        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wu + (int64_t)f * H) + v), uv[j]);
+      }
+#pragma unroll
+      for (int r = 0; r < kRC; ++r) {
+        if (r < rc) {
+          float xv[8];
+          bf16x8_to_f32(xsm[r * hv + v], xv);
+#pragma unroll
+          for (int j = 0; j < kFRows; ++j)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              ag[j][r] = fmaf(gv[j][i], xv[i], ag[j][r]);
+              au[j][r] = fmaf(uv[j][i], xv[i], au[j][r]);
+            }
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kFRows; ++j)
+#pragma unroll
+      for (int r = 0; r < kRC; ++r) {
+        float g = ag[j][r], u = au[j][r];
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+          g += __shfl_xor_sync(0xffffffffu, g, o);
+          u += __shfl_xor_sync(0xffffffffu, u, o);
+        }
+        if (lane == j * kRC + r && r < rc && f0 + j < F)
+          ws.hs[(int64_t)(r0 + c0 + r) * F + f0 + j] = __float2bfloat16_rn(g * silu_ref(u));
+      }
+  }
+}
+
+// ------------------------------------------------------- down + combine --
+// Block = kHRows output columns of H for every token.  Warp w takes experts
+// w, w + kWarps, ...; for each it streams the kHRows down rows of that expert
+// and dots them with the expert's h rows; d * gate weight goes to shared
+// memory, then the block sums the k slots of every token in slot order.
+template <class TY>
+__global__ void __launch_bounds__(kThreads)
+decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, TY* __restrict__ y,
+                   DecodeWs ws) {
+  extern __shared__ float dsm[];  // [n][kHRows]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int h0 = blockIdx.x * kHRows;
+  const int fv = F / 8;
+  for (int e = warp; e < E; e += kWarps) {
+    const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
+    if (cnt == 0) continue;
+    const __nv_bfloat16* wd = w_down + (int64_t)e * H * F;
+    for (int c0 = 0; c0 < cnt; c0 += kRC) {
+      const int rc = min(kRC, cnt - c0);
+      float acc[kHRows][kRC];
+#pragma unroll
+      for (int j = 0; j < kHRows; ++j)
+#pragma unroll
+        for (int r = 0; r < kRC; ++r) acc[j][r] = 0.f;
+      for (int v = lane; v < fv; v += 32) {
+        float wv[kHRows][8];
+#pragma unroll
+        for (int j = 0; j < kHRows; ++j)
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v), wv[j]);
+#pragma unroll
+        for (int r = 0; r < kRC; ++r) {
+          if (r < rc) {
+            float hv8[8];
+            bf16x8_to_f32(reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0 + r) * F)[v], hv8);
+#pragma unroll
+            for (int j = 0; j < kHRows; ++j)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[j][r] = fmaf(wv[j][i], hv8[i], acc[j][r]);
+          }
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < kHRows; ++j)
+#pragma unroll
+        for (int r = 0; r < kRC; ++r) {
+          float v = acc[j][r];
+#pragma unroll
+          for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+          if (lane == (j * kRC + r) % 32 && r < rc) {
+            const int row = r0 + c0 + r;
+            dsm[row * kHRows + j] = v * ws.wsorted[row];
+          }
+        }
+    }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < T * kHRows; i += kThreads) {
+    const int t = i / kHRows, j = i - t * kHRows;
+    if (h0 + j >= H) continue;
+    float acc = 0.f;
+    for (int s = 0; s < k; ++s) acc += dsm[ws.slot_pos[s * T + t] * kHRows + j];
+    y[(int64_t)t * H + h0 + j] = from_f32<TY>(acc);
+  }
+}
+
+}  // namespace
+
+namespace frank {
+
+bool decode_path_ok(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
+  return dtype == FRANK_BF16 && T >= 1 && T <= 64 && k * T <= kMaxSlots && E <= kMaxE && H % 8 == 0 && F % 8 == 0 &&
+         H <= 8192 && F % kHRows == 0 && H % kHRows == 0;
+}
+
+size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
+  Carve c(nullptr, 0);
+  const int64_t n = k * T;
+  c.take<float>(E * T);
+  c.take<unsigned>(1);
+  c.take<float>(n);
+  c.take<int32_t>(n);
+  c.take<int32_t>(n);
+  c.take<int32_t>(E + 1);
+  c.take<int32_t>(n);
+  c.take<float>(n);
+  c.take<__nv_bfloat16>(n * F);
+  return align_up(c.used, 256);
+}
+
+// Writes route_w / route_ids when non-null (copies of the internal buffers).
+int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void* w_up_p, const void* w_gate_p,
+                        const void* w_down_p, int64_t T, int64_t E, int64_t k, int64_t H, int64_t F, int normalize,
+                        int y_dtype, void* y, float* route_w, int32_t* route_ids, void* workspace, size_t ws_bytes,
+                        cudaStream_t st, void (*mark)(int, cudaStream_t)) {
+  if (ws_bytes < decode_workspace_size(T, H, F, E, k)) {
+    set_error("decode block: workspace %zu < %zu", ws_bytes, decode_workspace_size(T, H, F, E, k));
+    return FRANK_ENOSPC;
+  }
+  if ((uintptr_t)x % 16 || (uintptr_t)w_up_p % 16 || (uintptr_t)w_gate_p % 16 || (uintptr_t)w_down_p % 16 ||
+      (uintptr_t)wr % 16) {
+    set_error("decode block: inputs must be 16-byte aligned");
+    return FRANK_EINVAL;
+  }
+  const int64_t n = k * T;
+  Carve c(workspace, ws_bytes);
+  DecodeWs ws;
+  ws.logits = c.take<float>(E * T);
+  ws.ticket = c.take<unsigned>(1);
+  ws.w = c.take<float>(n);
+  ws.ids = c.take<int32_t>(n);
+  ws.sorted_slots = c.take<int32_t>(n);
+  ws.offsets = c.take<int32_t>(E + 1);
+  ws.slot_pos = c.take<int32_t>(n);
+  ws.wsorted = c.take<float>(n);
+  ws.hs = c.take<__nv_bfloat16>(n * F);
+  mark(0, st);
+  FRANK_CUDA_TRY(cudaMemsetAsync(ws.ticket, 0, sizeof(unsigned), st));
+  const int64_t items = E * ((T + kRouteTok - 1) / kRouteTok);
+  const unsigned rblocks = (unsigned)((items + kWarps - 1) / kWarps);
+  if (wr_dtype == FRANK_F32)
+    decode_route_kernel<float><<<rblocks, kThreads, 0, st>>>((const __nv_bfloat16*)x, (const float*)wr, (int)T,
+                                                             (int)H, (int)E, (int)k, normalize, ws);
+  else
+    decode_route_kernel<__nv_bfloat16><<<rblocks, kThreads, 0, st>>>(
+        (const __nv_bfloat16*)x, (const __nv_bfloat16*)wr, (int)T, (int)H, (int)E, (int)k, normalize, ws);
+  FRANK_LAUNCH_CHECK();
+  mark(1, st);
+  mark(2, st);
+  mark(3, st);
+  {
+    const size_t smem = (size_t)kRC * H * 2;
+    FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    dim3 grid((unsigned)((F + kWarps * kFRows - 1) / (kWarps * kFRows)), (unsigned)E);
+    decode_gateup_kernel<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
+                                                       (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, ws);
+    FRANK_LAUNCH_CHECK();
+  }
+  mark(4, st);
+  {
+    const size_t smem = (size_t)n * kHRows * sizeof(float);
+    dim3 grid((unsigned)(H / kHRows));
+    if (y_dtype == FRANK_F32) {
+      FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          (int)smem));
+      decode_down_kernel<float><<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)w_down_p, (int)T, (int)H, (int)F,
+                                                              (int)E, (int)k, (float*)y, ws);
+    } else {
+      FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel<__nv_bfloat16>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      decode_down_kernel<__nv_bfloat16><<<grid, kThreads, smem, st>>>(
+          (const __nv_bfloat16*)w_down_p, (int)T, (int)H, (int)F, (int)E, (int)k, (__nv_bfloat16*)y, ws);
+    }
+    FRANK_LAUNCH_CHECK();
+  }
+  mark(5, st);
+  mark(6, st);
+  if (route_w) FRANK_CUDA_TRY(cudaMemcpyAsync(route_w, ws.w, n * sizeof(float), cudaMemcpyDeviceToDevice, st));
+  if (route_ids)
+    FRANK_CUDA_TRY(cudaMemcpyAsync(route_ids, ws.ids, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
+  return FRANK_OK;
+}
+
+}  // namespace frank

@@ -32,6 +32,11 @@ int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int
                            int64_t, const float*, void*, cudaStream_t, const int32_t* row_rank = nullptr,
                            const int32_t* row_pos = nullptr, float* const* peer_out = nullptr, int n_peers = 0);
 int check_tc_shapes(int64_t, int64_t, int64_t, int64_t);
+bool decode_path_ok(int, int64_t, int64_t, int64_t, int64_t, int64_t);
+size_t decode_workspace_size(int64_t, int64_t, int64_t, int64_t, int64_t);
+int launch_decode_block(const void*, int, const void*, const void*, const void*, const void*, int64_t, int64_t,
+                        int64_t, int64_t, int64_t, int, int, void*, float*, int32_t*, void*, size_t, cudaStream_t,
+                        void (*)(int, cudaStream_t));
 
 // ---- error state ----
 static thread_local std::string g_err;
@@ -285,6 +290,7 @@ int frank_mul_mat_id(int dtype, const void* w_eoi, const void* input, const int3
 }
 
 size_t frank_moe_ffn_block_workspace_size(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
+  if (decode_path_ok(dtype, T, H, F, E, k)) return decode_workspace_size(T, H, F, E, k);
   return moe_layout(dtype, T, H, F, E, k, nullptr, 0, nullptr);
 }
 
@@ -307,6 +313,11 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
     FRANK_TRY(check_tc_shapes(n, F, H, E));
     FRANK_TRY(check_tc_shapes(n, H, F, E));
     FRANK_CHECK_ARG(H % 4 == 0, "moe_ffn_block bf16: n_embd %% 4 != 0");
+  }
+  if (decode_path_ok(dtype, T, H, F, E, k)) {
+    // a few tokens: weight-streaming decode kernels (csrc/decode.cu)
+    return launch_decode_block(x, wr_dtype, wr, w_up_p, w_gate_p, w_down_p, T, E, k, H, F, normalize, y_dtype, y,
+                               route_w, route_ids, workspace, ws_bytes, st, prof_mark);
   }
   size_t need = moe_layout(dtype, T, H, F, E, k, nullptr, 0, nullptr);
   if (ws_bytes < need) {

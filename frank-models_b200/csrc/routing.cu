@@ -8,75 +8,14 @@
 //   renormalisation      moe_ffn_block.mlir:91-128, oracles/moe.py:103-105
 //   slot flattening      components/moe/mul_mat_id.mlir:51-53 (s = j*T + t)
 #include "common.cuh"
+#include "topk.cuh"
 
 namespace {
+using namespace frank_topk;
 
-constexpr int kMaxE = 256;        // experts handled by the router
-constexpr int kMaxK = 32;         // top-k bound
 constexpr int kRouterTok = 32;    // tokens per router block
 constexpr int kRouterHc = 32;     // H chunk staged in shared memory
 constexpr int kRouterThreads = 256;
-
-// One warp: softmax over E logits held in shared memory (stride 1), then k
-// rounds of arg-max.  Ties resolve to the lowest expert index.  Lane l owns
-// experts l, l+32, ...
-__device__ void warp_softmax_topk(const float* lg, int E, int k, int normalize,
-                                  float* w_out, int32_t* id_out, int64_t T, int64_t t) {
-  const int lane = threadIdx.x & 31;
-  constexpr int kPer = kMaxE / 32;
-  float p[kPer];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    int e = lane + 32 * i;
-    p[i] = (e < E) ? lg[e] : -INFINITY;
-    mx = fmaxf(mx, p[i]);
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-  float sum = 0.f;
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    int e = lane + 32 * i;
-    p[i] = (e < E) ? expf(p[i] - mx) : 0.f;
-    sum += p[i];
-  }
-#pragma unroll
-  for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    int e = lane + 32 * i;
-    p[i] = (e < E) ? p[i] / sum : -1.f;  // probabilities are >= 0; -1 marks "absent"
-  }
-  float chosen[kMaxK];
-  float wsum = 0.f;
-  for (int j = 0; j < k; ++j) {
-    // lane-local best (lowest index on ties: scan ascending, strict >)
-    float bv = -2.f;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int i = 0; i < kPer; ++i) {
-      if (p[i] > bv) { bv = p[i]; bi = lane + 32 * i; }
-    }
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    // remove the winner from its owner lane
-#pragma unroll
-    for (int i = 0; i < kPer; ++i)
-      if (lane + 32 * i == bi) p[i] = -2.f;
-    chosen[j] = bv;
-    wsum += bv;  // ascending j, as numpy's sum over a short axis
-    if (lane == 0) id_out[(int64_t)j * T + t] = bi;
-  }
-  if (lane == 0) {
-    for (int j = 0; j < k; ++j)
-      w_out[(int64_t)j * T + t] = normalize ? chosen[j] / wsum : chosen[j];
-  }
-}
 
 __global__ void softmax_topk_kernel(const float* __restrict__ logits, int64_t T, int E, int k,
                                     int normalize, float* __restrict__ w, int32_t* __restrict__ ids) {
