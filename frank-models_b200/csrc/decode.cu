@@ -1,24 +1,23 @@
-// Decode-sized MoE FFN block (a few tokens per step): three launches,
+// Decode-sized MoE FFN block (a few tokens per step): four launches,
 // weight-streaming on CUDA cores.
 //
 // With T <= 64 tokens an expert receives a handful of rows, so the block is
 // bound by reading the active experts' weights from HBM (3 x H x F bf16 per
-// active expert) -- tensor cores would idle on 128-row tiles.  The three
-// kernels:
-//   decode_route_kernel    router logits (one warp per (expert, 8 tokens)),
-//                          then the last block to finish runs softmax +
-//                          top-k + renorm for every token and the stable
-//                          expert permutation (moe_ffn_block.mlir:54-128,
-//                          mul_mat_id.mlir:51-53);
-//   decode_gateup_kernel   one block per (expert, 32 rows of F): streams the
-//                          gate and up rows once, dots them with the
-//                          expert's token rows (gathered straight from x),
-//                          writes h = gate * silu(up) (swiglu.mlir:37-47);
-//   decode_down_kernel     one block per 8 rows of H: every warp streams the
-//                          down rows of its experts, scales by the gate
-//                          weight, and the block sums the k slots of every
-//                          token in slot order (moe_ffn_block.mlir:158-206)
-//                          -- the combine is fused, deterministic, no atomics.
+// active expert) -- tensor cores would idle on 128-row tiles.  The kernels:
+//   decode_route_kernel    router logits (one warp per (expert, 8 tokens));
+//                          the last block to finish runs softmax + top-k +
+//                          renorm for every token, the stable expert
+//                          permutation and the list of active experts
+//                          (moe_ffn_block.mlir:54-128, mul_mat_id.mlir:51-53);
+//   decode_gateup_kernel   persistent blocks over (active expert, 8 rows of F):
+//                          one gate row and one up row per warp streamed once
+//                          and dotted with the expert's token rows (gathered
+//                          straight from x), h = gate * silu(up)
+//                          (swiglu.mlir:37-47);
+//   decode_down_kernel     persistent blocks over (active expert, 32 rows of
+//                          H): d = down(h) * gate weight, fp32;
+//   combine_kernel         y[t] = sum of the k slots of t in slot order
+//                          (moe_ffn_block.mlir:179-206), deterministic.
 // The only atomic is the completion ticket of the route kernel; it resets
 // itself, and the launcher zeroes it at every call.
 #include "common.cuh"
@@ -33,8 +32,6 @@ constexpr int kWarps = kThreads / 32;
 constexpr int kRouteTok = 8;    // tokens per route warp item
 constexpr int kMaxSlots = 2048; // k * T handled by the decode path
 constexpr int kRC = 8;          // token rows per pass over an expert's weights
-constexpr int kFRows = 4;       // gate/up rows (each of gate and up) per warp
-constexpr int kHRows = 8;       // down rows per block
 
 __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
   const uint32_t w[4] = {u.x, u.y, u.z, u.w};
@@ -68,6 +65,9 @@ struct DecodeWs {
   int32_t* slot_pos;
   float* wsorted;
   __nv_bfloat16* hs;    // [k*T, F]
+  int32_t* active;      // experts with at least one row, ascending
+  int32_t* nactive;
+  float* d;             // [k*T, H] down output x gate weight
 };
 
 // ----------------------------------------------------------------- route --
@@ -164,6 +164,10 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
       acc += c;
     }
     ws.offsets[E] = acc;
+    int na = 0;
+    for (int e = 0; e < E; ++e)
+      if (ws.offsets[e + 1] > ws.offsets[e]) ws.active[na++] = e;
+    *ws.nactive = na;
     *ws.ticket = 0;  // ready for the next call
   }
   __syncthreads();
@@ -176,137 +180,132 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
 }
 
 // --------------------------------------------------------------- gate/up --
-// Block (f-chunk, expert e): kWarps warps x kFRows rows of gate and of up.
-// The expert's token rows (<= kRC per pass) are staged in shared memory as
-// bf16; each lane streams 16-byte slices of its 2*kFRows weight rows.
+// Persistent blocks over items (active expert, 8 rows of F).  The block
+// stages the expert's token rows (<= kRC per pass, gathered from x) in shared
+// memory; warp w streams gate row f0+w and up row f0+w (16-byte slices) and
+// dots them with every staged row.
+constexpr int kGUF = kWarps;  // F rows per item (one per warp)
+
 __global__ void __launch_bounds__(kThreads)
 decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, DecodeWs ws) {
   extern __shared__ uint4 xsm[];  // [kRC][H/8]
-  const int e = blockIdx.y;
-  const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
-  if (cnt == 0) return;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int f0 = (blockIdx.x * kWarps + warp) * kFRows;
   const int hv = H / 8;
-  const __nv_bfloat16* wg = w_gate + (int64_t)e * F * H;
-  const __nv_bfloat16* wu = w_up + (int64_t)e * F * H;
-  for (int c0 = 0; c0 < cnt; c0 += kRC) {
-    const int rc = min(kRC, cnt - c0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
-      const int r = i / hv, v = i - r * hv;
-      const int t = ws.sorted_slots[r0 + c0 + r] % T;
-      xsm[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
-    }
-    __syncthreads();
-    if (f0 >= F) continue;
-    float ag[kFRows][kRC], au[kFRows][kRC];
-#pragma unroll
-    for (int j = 0; j < kFRows; ++j)
-#pragma unroll
-      for (int r = 0; r < kRC; ++r) ag[j][r] = au[j][r] = 0.f;
-    for (int v = lane; v < hv; v += 32) {
-      float gv[kFRows][8], uv[kFRows][8];
-#pragma unroll
-      for (int j = 0; j < kFRows; ++j) {
-        const int f = min(f0 + j, F - 1);
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wg + (int64_t)f * H) + v), gv[j]);
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wu + (int64_t)f * H) + v), uv[j]);
+  const int nfc = (F + kGUF - 1) / kGUF;
+  const int items = *ws.nactive * nfc;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int e = ws.active[item / nfc];
+    const int f = (item % nfc) * kGUF + warp;
+    const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
+    const uint4* wg = reinterpret_cast<const uint4*>(w_gate + ((int64_t)e * F + min(f, F - 1)) * H);
+    const uint4* wu = reinterpret_cast<const uint4*>(w_up + ((int64_t)e * F + min(f, F - 1)) * H);
+    for (int c0 = 0; c0 < cnt; c0 += kRC) {
+      const int rc = min(kRC, cnt - c0);
+      __syncthreads();
+      for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
+        const int r = i / hv, v = i - r * hv;
+        const int t = ws.sorted_slots[r0 + c0 + r] % T;
+        xsm[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
       }
+      __syncthreads();
+      float ag[kRC], au[kRC];
 #pragma unroll
-      for (int r = 0; r < kRC; ++r) {
-        if (r < rc) {
-          float xv[8];
-          bf16x8_to_f32(xsm[r * hv + v], xv);
+      for (int r = 0; r < kRC; ++r) ag[r] = au[r] = 0.f;
+#pragma unroll 4
+      for (int v = lane; v < hv; v += 32) {
+        float gv[8], uv[8];
+        bf16x8_to_f32(__ldg(wg + v), gv);
+        bf16x8_to_f32(__ldg(wu + v), uv);
 #pragma unroll
-          for (int j = 0; j < kFRows; ++j)
+        for (int r = 0; r < kRC; ++r) {
+          if (r < rc) {
+            float xv[8];
+            bf16x8_to_f32(xsm[r * hv + v], xv);
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-              ag[j][r] = fmaf(gv[j][i], xv[i], ag[j][r]);
-              au[j][r] = fmaf(uv[j][i], xv[i], au[j][r]);
+              ag[r] = fmaf(gv[i], xv[i], ag[r]);
+              au[r] = fmaf(uv[i], xv[i], au[r]);
             }
+          }
         }
       }
-    }
-#pragma unroll
-    for (int j = 0; j < kFRows; ++j)
 #pragma unroll
       for (int r = 0; r < kRC; ++r) {
-        float g = ag[j][r], u = au[j][r];
+        float g = ag[r], u = au[r];
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
           g += __shfl_xor_sync(0xffffffffu, g, o);
           u += __shfl_xor_sync(0xffffffffu, u, o);
         }
-        if (lane == j * kRC + r && r < rc && f0 + j < F)
-          ws.hs[(int64_t)(r0 + c0 + r) * F + f0 + j] = __float2bfloat16_rn(g * silu_ref(u));
+        if (lane == r && r < rc && f < F)
+          ws.hs[(int64_t)(r0 + c0 + r) * F + f] = __float2bfloat16_rn(g * silu_ref(u));
       }
+    }
   }
 }
 
-// ------------------------------------------------------- down + combine --
-// Block = kHRows output columns of H for every token.  Warp w takes experts
-// w, w + kWarps, ...; for each it streams the kHRows down rows of that expert
-// and dots them with the expert's h rows; d * gate weight goes to shared
-// memory, then the block sums the k slots of every token in slot order.
-template <class TY>
+// ------------------------------------------------------------------ down --
+// Persistent blocks over items (active expert, 32 rows of H): the expert's h
+// rows are staged in shared memory; warp w streams down rows h0+4w..h0+4w+3.
+// d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
+constexpr int kDH = 4;                  // down rows per warp
+constexpr int kDItem = kDH * kWarps;    // down rows per item
+
 __global__ void __launch_bounds__(kThreads)
-decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, TY* __restrict__ y,
-                   DecodeWs ws) {
-  extern __shared__ float dsm[];  // [n][kHRows]
+decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, DecodeWs ws) {
+  extern __shared__ uint4 hsm[];  // [kRC][F/8]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int h0 = blockIdx.x * kHRows;
   const int fv = F / 8;
-  for (int e = warp; e < E; e += kWarps) {
+  const int nhc = (H + kDItem - 1) / kDItem;
+  const int items = *ws.nactive * nhc;
+  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+    const int e = ws.active[item / nhc];
+    const int h0 = (item % nhc) * kDItem + warp * kDH;
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
-    if (cnt == 0) continue;
     const __nv_bfloat16* wd = w_down + (int64_t)e * H * F;
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
-      float acc[kHRows][kRC];
+      __syncthreads();
+      for (int i = threadIdx.x; i < rc * fv; i += kThreads)
+        hsm[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
+      __syncthreads();
+      float acc[kDH][kRC];
 #pragma unroll
-      for (int j = 0; j < kHRows; ++j)
+      for (int j = 0; j < kDH; ++j)
 #pragma unroll
         for (int r = 0; r < kRC; ++r) acc[j][r] = 0.f;
+#pragma unroll 2
       for (int v = lane; v < fv; v += 32) {
-        float wv[kHRows][8];
+        float wv[kDH][8];
 #pragma unroll
-        for (int j = 0; j < kHRows; ++j)
+        for (int j = 0; j < kDH; ++j)
           bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v), wv[j]);
 #pragma unroll
         for (int r = 0; r < kRC; ++r) {
           if (r < rc) {
             float hv8[8];
-            bf16x8_to_f32(reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0 + r) * F)[v], hv8);
+            bf16x8_to_f32(hsm[r * fv + v], hv8);
 #pragma unroll
-            for (int j = 0; j < kHRows; ++j)
+            for (int j = 0; j < kDH; ++j)
 #pragma unroll
               for (int i = 0; i < 8; ++i) acc[j][r] = fmaf(wv[j][i], hv8[i], acc[j][r]);
           }
         }
       }
 #pragma unroll
-      for (int j = 0; j < kHRows; ++j)
+      for (int j = 0; j < kDH; ++j)
 #pragma unroll
         for (int r = 0; r < kRC; ++r) {
           float v = acc[j][r];
 #pragma unroll
           for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == (j * kRC + r) % 32 && r < rc) {
+          if (lane == j * kRC + r && r < rc && h0 + j < H) {
             const int row = r0 + c0 + r;
-            dsm[row * kHRows + j] = v * ws.wsorted[row];
+            ws.d[(int64_t)row * H + h0 + j] = v * ws.wsorted[row];
           }
         }
     }
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < T * kHRows; i += kThreads) {
-    const int t = i / kHRows, j = i - t * kHRows;
-    if (h0 + j >= H) continue;
-    float acc = 0.f;
-    for (int s = 0; s < k; ++s) acc += dsm[ws.slot_pos[s * T + t] * kHRows + j];
-    y[(int64_t)t * H + h0 + j] = from_f32<TY>(acc);
   }
 }
 
@@ -314,9 +313,11 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int T, int H, int F
 
 namespace frank {
 
+int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
+
 bool decode_path_ok(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
   return dtype == FRANK_BF16 && T >= 1 && T <= 64 && k * T <= kMaxSlots && E <= kMaxE && H % 8 == 0 && F % 8 == 0 &&
-         H <= 8192 && F % kHRows == 0 && H % kHRows == 0;
+         H <= 8192 && F <= 8192;
 }
 
 size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
@@ -331,6 +332,9 @@ size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t
   c.take<int32_t>(n);
   c.take<float>(n);
   c.take<__nv_bfloat16>(n * F);
+  c.take<int32_t>(E);
+  c.take<int32_t>(1);
+  c.take<float>(n * H);
   return align_up(c.used, 256);
 }
 
@@ -360,6 +364,9 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.slot_pos = c.take<int32_t>(n);
   ws.wsorted = c.take<float>(n);
   ws.hs = c.take<__nv_bfloat16>(n * F);
+  ws.active = c.take<int32_t>(E);
+  ws.nactive = c.take<int32_t>(1);
+  ws.d = c.take<float>(n * H);
   mark(0, st);
   FRANK_CUDA_TRY(cudaMemsetAsync(ws.ticket, 0, sizeof(unsigned), st));
   const int64_t items = E * ((T + kRouteTok - 1) / kRouteTok);
@@ -374,32 +381,23 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   mark(1, st);
   mark(2, st);
   mark(3, st);
+  const int grid_p = num_sms() * 4;
   {
     const size_t smem = (size_t)kRC * H * 2;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    dim3 grid((unsigned)((F + kWarps * kFRows - 1) / (kWarps * kFRows)), (unsigned)E);
-    decode_gateup_kernel<<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
-                                                       (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, ws);
+    decode_gateup_kernel<<<grid_p, kThreads, smem, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
+                                                         (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, ws);
     FRANK_LAUNCH_CHECK();
   }
   mark(4, st);
   {
-    const size_t smem = (size_t)n * kHRows * sizeof(float);
-    dim3 grid((unsigned)(H / kHRows));
-    if (y_dtype == FRANK_F32) {
-      FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          (int)smem));
-      decode_down_kernel<float><<<grid, kThreads, smem, st>>>((const __nv_bfloat16*)w_down_p, (int)T, (int)H, (int)F,
-                                                              (int)E, (int)k, (float*)y, ws);
-    } else {
-      FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel<__nv_bfloat16>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-      decode_down_kernel<__nv_bfloat16><<<grid, kThreads, smem, st>>>(
-          (const __nv_bfloat16*)w_down_p, (int)T, (int)H, (int)F, (int)E, (int)k, (__nv_bfloat16*)y, ws);
-    }
+    const size_t smem = (size_t)kRC * F * 2;
+    FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    decode_down_kernel<<<grid_p, kThreads, smem, st>>>((const __nv_bfloat16*)w_down_p, (int)H, (int)F, ws);
     FRANK_LAUNCH_CHECK();
   }
   mark(5, st);
+  FRANK_TRY(launch_combine(y_dtype, ws.d, ws.slot_pos, T, k, H, y, st));
   mark(6, st);
   if (route_w) FRANK_CUDA_TRY(cudaMemcpyAsync(route_w, ws.w, n * sizeof(float), cudaMemcpyDeviceToDevice, st));
   if (route_ids)
