@@ -75,6 +75,7 @@ template <class TW>
 __global__ void __launch_bounds__(kThreads)
 decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr, int T, int H, int E, int k,
                     int normalize, DecodeWs ws) {
+  asm volatile("griddepcontrol.launch_dependents;" :::);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tchunks = (T + kRouteTok - 1) / kRouteTok;
   const int item = blockIdx.x * kWarps + warp;
@@ -83,6 +84,7 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
     float acc[kRouteTok];
 #pragma unroll
     for (int a = 0; a < kRouteTok; ++a) acc[a] = 0.f;
+#pragma unroll 8
     for (int h = lane * 8; h < H; h += 256) {
       float wv[8];
       load8_w(wr + (int64_t)e * H + h, wv);
@@ -179,17 +181,26 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   }
 }
 
+// Programmatic dependent launch: a kernel's blocks may start while the
+// previous kernel of the stream finishes; they wait here for its results.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 // --------------------------------------------------------------- gate/up --
-// Persistent blocks over items (active expert, 8 rows of F).  The block
-// stages the expert's token rows (<= kRC per pass, gathered from x) in shared
-// memory; warp w streams gate row f0+w and up row f0+w (16-byte slices) and
-// dots them with every staged row.
+// Persistent blocks over items (active expert, 8 rows of F).  Warp w owns
+// gate row f and up row f (f = 8*chunk + w): all its 16-byte slices of a
+// round (kRV per lane) are requested before any is used, the expert's token
+// rows (<= kRC per pass, gathered from x) are staged in shared memory
+// meanwhile, then every slice is dotted with every staged row.
 constexpr int kGUF = kWarps;  // F rows per item (one per warp)
+constexpr int kRV = 8;        // 16-byte weight slices per lane per round and row
 
 __global__ void __launch_bounds__(kThreads)
 decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, DecodeWs ws) {
   extern __shared__ uint4 xsm[];  // [kRC][H/8]
+  wait_prior_grid();
+  allow_next_grid();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8;
   const int nfc = (F + kGUF - 1) / kGUF;
@@ -200,6 +211,18 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
     const uint4* wg = reinterpret_cast<const uint4*>(w_gate + ((int64_t)e * F + min(f, F - 1)) * H);
     const uint4* wu = reinterpret_cast<const uint4*>(w_up + ((int64_t)e * F + min(f, F - 1)) * H);
+    uint4 gq[kRV], uq[kRV];
+    auto fetch = [&](int v0) {
+#pragma unroll
+      for (int i = 0; i < kRV; ++i) {
+        const int v = v0 + lane + 32 * i;
+        if (v < hv) {
+          gq[i] = __ldg(wg + v);
+          uq[i] = __ldg(wu + v);
+        }
+      }
+    };
+    fetch(0);
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
       __syncthreads();
@@ -212,20 +235,26 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
       float ag[kRC], au[kRC];
 #pragma unroll
       for (int r = 0; r < kRC; ++r) ag[r] = au[r] = 0.f;
-#pragma unroll 4
-      for (int v = lane; v < hv; v += 32) {
-        float gv[8], uv[8];
-        bf16x8_to_f32(__ldg(wg + v), gv);
-        bf16x8_to_f32(__ldg(wu + v), uv);
+      for (int v0 = 0; v0 < hv; v0 += 32 * kRV) {
+        if (v0 != 0 || c0 != 0) fetch(v0);
 #pragma unroll
-        for (int r = 0; r < kRC; ++r) {
-          if (r < rc) {
-            float xv[8];
-            bf16x8_to_f32(xsm[r * hv + v], xv);
+        for (int i = 0; i < kRV; ++i) {
+          const int v = v0 + lane + 32 * i;
+          if (v < hv) {
+            float gv[8], uv[8];
+            bf16x8_to_f32(gq[i], gv);
+            bf16x8_to_f32(uq[i], uv);
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              ag[r] = fmaf(gv[i], xv[i], ag[r]);
-              au[r] = fmaf(uv[i], xv[i], au[r]);
+            for (int r = 0; r < kRC; ++r) {
+              if (r < rc) {
+                float xv[8];
+                bf16x8_to_f32(xsm[r * hv + v], xv);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                  ag[r] = fmaf(gv[q], xv[q], ag[r]);
+                  au[r] = fmaf(uv[q], xv[q], au[r]);
+                }
+              }
             }
           }
         }
@@ -246,15 +275,19 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 }
 
 // ------------------------------------------------------------------ down --
-// Persistent blocks over items (active expert, 32 rows of H): the expert's h
-// rows are staged in shared memory; warp w streams down rows h0+4w..h0+4w+3.
+// Persistent blocks over items (active expert, 32 rows of H): warp w streams
+// down rows h0..h0+3 (all slices of a round requested up front) while the
+// expert's h rows are staged in shared memory.
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
 constexpr int kDH = 4;                  // down rows per warp
 constexpr int kDItem = kDH * kWarps;    // down rows per item
+constexpr int kDV = 4;                  // slices per lane per round and row
 
 __global__ void __launch_bounds__(kThreads)
 decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, DecodeWs ws) {
   extern __shared__ uint4 hsm[];  // [kRC][F/8]
+  wait_prior_grid();
+  allow_next_grid();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fv = F / 8;
   const int nhc = (H + kDItem - 1) / kDItem;
@@ -264,6 +297,17 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, Decod
     const int h0 = (item % nhc) * kDItem + warp * kDH;
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
     const __nv_bfloat16* wd = w_down + (int64_t)e * H * F;
+    uint4 wq[kDH][kDV];
+    auto fetch = [&](int v0) {
+#pragma unroll
+      for (int j = 0; j < kDH; ++j)
+#pragma unroll
+        for (int i = 0; i < kDV; ++i) {
+          const int v = v0 + lane + 32 * i;
+          if (v < fv) wq[j][i] = __ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v);
+        }
+    };
+    fetch(0);
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
       __syncthreads();
@@ -275,21 +319,26 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, Decod
       for (int j = 0; j < kDH; ++j)
 #pragma unroll
         for (int r = 0; r < kRC; ++r) acc[j][r] = 0.f;
-#pragma unroll 2
-      for (int v = lane; v < fv; v += 32) {
-        float wv[kDH][8];
+      for (int v0 = 0; v0 < fv; v0 += 32 * kDV) {
+        if (v0 != 0 || c0 != 0) fetch(v0);
 #pragma unroll
-        for (int j = 0; j < kDH; ++j)
-          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v), wv[j]);
+        for (int i = 0; i < kDV; ++i) {
+          const int v = v0 + lane + 32 * i;
+          if (v < fv) {
 #pragma unroll
-        for (int r = 0; r < kRC; ++r) {
-          if (r < rc) {
-            float hv8[8];
-            bf16x8_to_f32(hsm[r * fv + v], hv8);
+            for (int r = 0; r < kRC; ++r) {
+              if (r < rc) {
+                float hv8[8];
+                bf16x8_to_f32(hsm[r * fv + v], hv8);
 #pragma unroll
-            for (int j = 0; j < kDH; ++j)
+                for (int j = 0; j < kDH; ++j) {
+                  float wv[8];
+                  bf16x8_to_f32(wq[j][i], wv);
 #pragma unroll
-              for (int i = 0; i < 8; ++i) acc[j][r] = fmaf(wv[j][i], hv8[i], acc[j][r]);
+                  for (int q = 0; q < 8; ++q) acc[j][r] = fmaf(wv[q], hv8[q], acc[j][r]);
+                }
+              }
+            }
           }
         }
       }
@@ -309,11 +358,40 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, Decod
   }
 }
 
+// --------------------------------------------------------------- combine --
+// y[t, h] = sum_{j<k} d[slot_pos[j*T + t], h] in slot order (deterministic).
+template <class TY>
+__global__ void __launch_bounds__(kThreads)
+decode_combine_kernel(int T, int H, int k, TY* __restrict__ y, DecodeWs ws) {
+  wait_prior_grid();
+  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < (int64_t)T * H;
+       i += (int64_t)gridDim.x * kThreads) {
+    const int t = (int)(i / H), h = (int)(i - (int64_t)t * H);
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc += ws.d[(int64_t)ws.slot_pos[j * T + t] * H + h];
+    y[i] = from_f32<TY>(acc);
+  }
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 }  // namespace
 
 namespace frank {
-
-int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
 
 bool decode_path_ok(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
   return dtype == FRANK_BF16 && T >= 1 && T <= 64 && k * T <= kMaxSlots && E <= kMaxE && H % 8 == 0 && F % 8 == 0 &&
@@ -381,23 +459,35 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   mark(1, st);
   mark(2, st);
   mark(3, st);
-  const int grid_p = num_sms() * 4;
+  const int grid_p = num_sms() * 2;
   {
     const size_t smem = (size_t)kRC * H * 2;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    decode_gateup_kernel<<<grid_p, kThreads, smem, st>>>((const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
-                                                         (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, ws);
+    FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kThreads), smem, st,
+                              (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
+                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(4, st);
   {
     const size_t smem = (size_t)kRC * F * 2;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    decode_down_kernel<<<grid_p, kThreads, smem, st>>>((const __nv_bfloat16*)w_down_p, (int)H, (int)F, ws);
+    FRANK_CUDA_TRY(launch_pdl(decode_down_kernel, dim3(grid_p), dim3(kThreads), smem, st,
+                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(5, st);
-  FRANK_TRY(launch_combine(y_dtype, ws.d, ws.slot_pos, T, k, H, y, st));
+  {
+    const int64_t tot = T * H;
+    const unsigned g = (unsigned)((tot + kThreads - 1) / kThreads);
+    if (y_dtype == FRANK_F32)
+      FRANK_CUDA_TRY(launch_pdl(decode_combine_kernel<float>, dim3(g), dim3(kThreads), 0, st, (int)T, (int)H,
+                                (int)k, (float*)y, ws));
+    else
+      FRANK_CUDA_TRY(launch_pdl(decode_combine_kernel<__nv_bfloat16>, dim3(g), dim3(kThreads), 0, st, (int)T,
+                                (int)H, (int)k, (__nv_bfloat16*)y, ws));
+    FRANK_LAUNCH_CHECK();
+  }
   mark(6, st);
   if (route_w) FRANK_CUDA_TRY(cudaMemcpyAsync(route_w, ws.w, n * sizeof(float), cudaMemcpyDeviceToDevice, st));
   if (route_ids)
