@@ -42,6 +42,20 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
   }
 }
 
+// Same as bf16x8_to_f32, but opaque to the optimiser so that the unpacking
+// stays next to its use (it must not be hoisted out of the per-row loops,
+// which would keep 64+ unpacked floats live per lane).
+__device__ __forceinline__ void bf16x8_unpack_here(uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint32_t lo, hi;
+    asm volatile("shl.b32 %0, %2, 16;\n\tand.b32 %1, %2, 0xffff0000;" : "=r"(lo), "=r"(hi) : "r"(w[i]));
+    v[2 * i] = __uint_as_float(lo);
+    v[2 * i + 1] = __uint_as_float(hi);
+  }
+}
+
 template <class TW>
 __device__ __forceinline__ void load8_w(const TW* p, float (&v)[8]);
 template <>
@@ -189,9 +203,11 @@ __device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol
 // --------------------------------------------------------------- gate/up --
 // Persistent blocks over items (active expert, 8 rows of F).  Warp w owns
 // gate row f and up row f (f = 8*chunk + w): all its 16-byte slices of a
-// round (kRV per lane) are requested before any is used, the expert's token
-// rows (<= kRC per pass, gathered from x) are staged in shared memory
-// meanwhile, then every slice is dotted with every staged row.
+// round (kRV per lane) are requested before any is used, while the expert's
+// token rows (<= kRC per pass, gathered from x) are staged in shared memory.
+// Rows are then taken one at a time (a short dynamic loop: an expert has
+// only a few rows at decode sizes), each dot product reduced across the warp
+// at once; partial sums of multi-round rows (H > 2048) live in shared memory.
 constexpr int kGUF = kWarps;  // F rows per item (one per warp)
 constexpr int kRV = 8;        // 16-byte weight slices per lane per round and row
 
@@ -199,6 +215,7 @@ __global__ void __launch_bounds__(kThreads)
 decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, DecodeWs ws) {
   extern __shared__ uint4 xsm[];  // [kRC][H/8]
+  __shared__ float part[kWarps][2][kRC];
   wait_prior_grid();
   allow_next_grid();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -211,20 +228,15 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
     const uint4* wg = reinterpret_cast<const uint4*>(w_gate + ((int64_t)e * F + min(f, F - 1)) * H);
     const uint4* wu = reinterpret_cast<const uint4*>(w_up + ((int64_t)e * F + min(f, F - 1)) * H);
-    uint4 gq[kRV], uq[kRV];
-    auto fetch = [&](int v0) {
-#pragma unroll
-      for (int i = 0; i < kRV; ++i) {
-        const int v = v0 + lane + 32 * i;
-        if (v < hv) {
-          gq[i] = __ldg(wg + v);
-          uq[i] = __ldg(wu + v);
-        }
-      }
-    };
-    fetch(0);
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
+      uint4 gq[kRV], uq[kRV];
+#pragma unroll
+      for (int i = 0; i < kRV; ++i) {
+        const int v = lane + 32 * i;
+        gq[i] = v < hv ? __ldg(wg + v) : make_uint4(0, 0, 0, 0);
+        uq[i] = v < hv ? __ldg(wu + v) : make_uint4(0, 0, 0, 0);
+      }
       __syncthreads();
       for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
         const int r = i / hv, v = i - r * hv;
@@ -232,43 +244,47 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
         xsm[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
       }
       __syncthreads();
-      float ag[kRC], au[kRC];
-#pragma unroll
-      for (int r = 0; r < kRC; ++r) ag[r] = au[r] = 0.f;
       for (int v0 = 0; v0 < hv; v0 += 32 * kRV) {
-        if (v0 != 0 || c0 != 0) fetch(v0);
+        if (v0 != 0) {
 #pragma unroll
-        for (int i = 0; i < kRV; ++i) {
-          const int v = v0 + lane + 32 * i;
-          if (v < hv) {
-            float gv[8], uv[8];
-            bf16x8_to_f32(gq[i], gv);
-            bf16x8_to_f32(uq[i], uv);
+          for (int i = 0; i < kRV; ++i) {
+            const int v = v0 + lane + 32 * i;
+            gq[i] = v < hv ? __ldg(wg + v) : make_uint4(0, 0, 0, 0);
+            uq[i] = v < hv ? __ldg(wu + v) : make_uint4(0, 0, 0, 0);
+          }
+        }
+        for (int r = 0; r < rc; ++r) {
+          float g = 0.f, u = 0.f;
 #pragma unroll
-            for (int r = 0; r < kRC; ++r) {
-              if (r < rc) {
-                float xv[8];
-                bf16x8_to_f32(xsm[r * hv + v], xv);
+          for (int i = 0; i < kRV; ++i) {
+            const int v = v0 + lane + 32 * i;
+            if (v < hv) {
+              float gv[8], uv[8], xv[8];
+              bf16x8_unpack_here(gq[i], gv);
+              bf16x8_unpack_here(uq[i], uv);
+              bf16x8_to_f32(xsm[r * hv + v], xv);
 #pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                  ag[r] = fmaf(gv[q], xv[q], ag[r]);
-                  au[r] = fmaf(uv[q], xv[q], au[r]);
-                }
+              for (int q = 0; q < 8; ++q) {
+                g = fmaf(gv[q], xv[q], g);
+                u = fmaf(uv[q], xv[q], u);
               }
             }
           }
+#pragma unroll
+          for (int o = 16; o; o >>= 1) {
+            g += __shfl_xor_sync(0xffffffffu, g, o);
+            u += __shfl_xor_sync(0xffffffffu, u, o);
+          }
+          if (lane == 0) {
+            part[warp][0][r] = (v0 == 0 ? 0.f : part[warp][0][r]) + g;
+            part[warp][1][r] = (v0 == 0 ? 0.f : part[warp][1][r]) + u;
+          }
         }
       }
-#pragma unroll
-      for (int r = 0; r < kRC; ++r) {
-        float g = ag[r], u = au[r];
-#pragma unroll
-        for (int o = 16; o; o >>= 1) {
-          g += __shfl_xor_sync(0xffffffffu, g, o);
-          u += __shfl_xor_sync(0xffffffffu, u, o);
-        }
-        if (lane == r && r < rc && f < F)
-          ws.hs[(int64_t)(r0 + c0 + r) * F + f] = __float2bfloat16_rn(g * silu_ref(u));
+      __syncwarp();
+      if (lane < rc && f < F) {
+        const float g = part[warp][0][lane], u = part[warp][1][lane];
+        ws.hs[(int64_t)(r0 + c0 + lane) * F + f] = __float2bfloat16_rn(g * silu_ref(u));
       }
     }
   }
@@ -277,7 +293,7 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 // ------------------------------------------------------------------ down --
 // Persistent blocks over items (active expert, 32 rows of H): warp w streams
 // down rows h0..h0+3 (all slices of a round requested up front) while the
-// expert's h rows are staged in shared memory.
+// expert's h rows are staged in shared memory; rows of h one at a time.
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
 constexpr int kDH = 4;                  // down rows per warp
 constexpr int kDItem = kDH * kWarps;    // down rows per item
@@ -286,6 +302,7 @@ constexpr int kDV = 4;                  // slices per lane per round and row
 __global__ void __launch_bounds__(kThreads)
 decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, DecodeWs ws) {
   extern __shared__ uint4 hsm[];  // [kRC][F/8]
+  __shared__ float part[kWarps][kDH][kRC];
   wait_prior_grid();
   allow_next_grid();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -297,63 +314,66 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, Decod
     const int h0 = (item % nhc) * kDItem + warp * kDH;
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
     const __nv_bfloat16* wd = w_down + (int64_t)e * H * F;
-    uint4 wq[kDH][kDV];
-    auto fetch = [&](int v0) {
+    for (int c0 = 0; c0 < cnt; c0 += kRC) {
+      const int rc = min(kRC, cnt - c0);
+      uint4 wq[kDH][kDV];
 #pragma unroll
       for (int j = 0; j < kDH; ++j)
 #pragma unroll
         for (int i = 0; i < kDV; ++i) {
-          const int v = v0 + lane + 32 * i;
-          if (v < fv) wq[j][i] = __ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v);
+          const int v = lane + 32 * i;
+          wq[j][i] = v < fv ? __ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v)
+                            : make_uint4(0, 0, 0, 0);
         }
-    };
-    fetch(0);
-    for (int c0 = 0; c0 < cnt; c0 += kRC) {
-      const int rc = min(kRC, cnt - c0);
       __syncthreads();
       for (int i = threadIdx.x; i < rc * fv; i += kThreads)
         hsm[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
       __syncthreads();
-      float acc[kDH][kRC];
-#pragma unroll
-      for (int j = 0; j < kDH; ++j)
-#pragma unroll
-        for (int r = 0; r < kRC; ++r) acc[j][r] = 0.f;
       for (int v0 = 0; v0 < fv; v0 += 32 * kDV) {
-        if (v0 != 0 || c0 != 0) fetch(v0);
+        if (v0 != 0) {
 #pragma unroll
-        for (int i = 0; i < kDV; ++i) {
-          const int v = v0 + lane + 32 * i;
-          if (v < fv) {
+          for (int j = 0; j < kDH; ++j)
 #pragma unroll
-            for (int r = 0; r < kRC; ++r) {
-              if (r < rc) {
-                float hv8[8];
-                bf16x8_to_f32(hsm[r * fv + v], hv8);
+            for (int i = 0; i < kDV; ++i) {
+              const int v = v0 + lane + 32 * i;
+              wq[j][i] = v < fv ? __ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v)
+                                : make_uint4(0, 0, 0, 0);
+            }
+        }
+        for (int r = 0; r < rc; ++r) {
+          float acc[kDH] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                for (int j = 0; j < kDH; ++j) {
-                  float wv[8];
-                  bf16x8_to_f32(wq[j][i], wv);
+          for (int i = 0; i < kDV; ++i) {
+            const int v = v0 + lane + 32 * i;
+            if (v < fv) {
+              float hv8[8];
+              bf16x8_to_f32(hsm[r * fv + v], hv8);
 #pragma unroll
-                  for (int q = 0; q < 8; ++q) acc[j][r] = fmaf(wv[q], hv8[q], acc[j][r]);
-                }
+              for (int j = 0; j < kDH; ++j) {
+                float wv[8];
+                bf16x8_unpack_here(wq[j][i], wv);
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[j] = fmaf(wv[q], hv8[q], acc[j]);
               }
             }
           }
-        }
-      }
 #pragma unroll
-      for (int j = 0; j < kDH; ++j)
+          for (int j = 0; j < kDH; ++j) {
+            float v = acc[j];
 #pragma unroll
-        for (int r = 0; r < kRC; ++r) {
-          float v = acc[j][r];
-#pragma unroll
-          for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          if (lane == j * kRC + r && r < rc && h0 + j < H) {
-            const int row = r0 + c0 + r;
-            ws.d[(int64_t)row * H + h0 + j] = v * ws.wsorted[row];
+            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+            if (lane == 0) part[warp][j][r] = (v0 == 0 ? 0.f : part[warp][j][r]) + v;
           }
         }
+      }
+      __syncwarp();
+      if (lane < kDH * kRC) {
+        const int j = lane / kRC, r = lane - j * kRC;
+        if (r < rc && h0 + j < H) {
+          const int row = r0 + c0 + r;
+          ws.d[(int64_t)row * H + h0 + j] = part[warp][j][r] * ws.wsorted[row];
+        }
+      }
     }
   }
 }
