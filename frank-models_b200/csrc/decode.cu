@@ -21,6 +21,7 @@
 // The only atomic is the completion ticket of the route kernel; it resets
 // itself, and the launcher zeroes it at every call.
 #include "common.cuh"
+#include "mbarrier.cuh"
 #include "topk.cuh"
 
 namespace {
@@ -82,6 +83,7 @@ struct DecodeWs {
   int32_t* active;      // experts with at least one row, ascending
   int32_t* nactive;
   float* d;             // [k*T, H] down output x gate weight
+  int32_t* err;         // device error word (bounded waits)
 };
 
 // ----------------------------------------------------------------- route --
@@ -171,20 +173,31 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
     if (e >= 0 && lane == leader) warp_cnt[warp][e] = 0;
     __syncthreads();
   }
-  if (threadIdx.x == 0) {  // exclusive scan of the counts (E <= 256)
-    int32_t acc = 0;
-    for (int e = 0; e < E; ++e) {
-      const int32_t c = running[e];
-      ws.offsets[e] = acc;
-      running[e] = acc;
-      acc += c;
+  if (warp == 0) {  // exclusive scan of the counts and the active-expert list (E <= 256)
+    int carry = 0, na = 0;
+    for (int base = 0; base < E; base += 32) {
+      const int e = base + lane;
+      const int c = e < E ? running[e] : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (e < E) {
+        ws.offsets[e] = carry + incl - c;
+        running[e] = carry + incl - c;
+      }
+      const unsigned act = __ballot_sync(0xffffffffu, c > 0);
+      if (c > 0) ws.active[na + __popc(act & ((1u << lane) - 1u))] = e;
+      na += __popc(act);
+      carry += __shfl_sync(0xffffffffu, incl, 31);
     }
-    ws.offsets[E] = acc;
-    int na = 0;
-    for (int e = 0; e < E; ++e)
-      if (ws.offsets[e + 1] > ws.offsets[e]) ws.active[na++] = e;
-    *ws.nactive = na;
-    *ws.ticket = 0;  // ready for the next call
+    if (lane == 0) {
+      ws.offsets[E] = carry;
+      *ws.nactive = na;
+      *ws.ticket = 0;  // ready for the next call
+    }
   }
   __syncthreads();
   for (int s = threadIdx.x; s < n; s += kThreads) {
@@ -200,74 +213,94 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
 __device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
-// --------------------------------------------------------------- gate/up --
-// Persistent blocks over items (active expert, 8 rows of F).  Warp w owns
-// gate row f and up row f (f = 8*chunk + w): all its 16-byte slices of a
-// round (kRV per lane) are requested before any is used, while the expert's
-// token rows (<= kRC per pass, gathered from x) are staged in shared memory.
-// Rows are then taken one at a time (a short dynamic loop: an expert has
-// only a few rows at decode sizes), each dot product reduced across the warp
-// at once; partial sums of multi-round rows (H > 2048) live in shared memory.
-constexpr int kGUF = kWarps;  // F rows per item (one per warp)
-constexpr int kRV = 8;        // 16-byte weight slices per lane per round and row
+// ----------------------------------------------- weight-streaming GEMVs --
+// Both GEMV kernels stream contiguous chunks of an expert's weight rows from
+// HBM into a ring of shared-memory stages with 1-D bulk copies
+// (cp.async.bulk, one mbarrier per stage), so that every SM keeps 100+ KB of
+// weights in flight; the token rows of the chunk's expert are staged next to
+// them and every warp dots whole rows out of shared memory.  Items are
+// (active expert, chunk of rows), spread over persistent blocks.
+using namespace frank_mbar;
 
+struct StreamSmem {
+  uint32_t stage0;   // shared address of stage 0
+  uint32_t stage_bytes;
+  int stages;
+};
+
+// gate/up: item = (active expert e, fr rows of F starting at f0): stage =
+// fr gate rows then fr up rows ([2][fr][H] bf16).  Warp w < fr computes row
+// f0 + w for each token row: h = gate . x * silu(up . x).
 __global__ void __launch_bounds__(kThreads)
 decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
-                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, DecodeWs ws) {
-  extern __shared__ uint4 xsm[];  // [kRC][H/8]
-  __shared__ float part[kWarps][2][kRC];
-  wait_prior_grid();
-  allow_next_grid();
+                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int fr, int stages,
+                     DecodeWs ws) {
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  __shared__ __align__(8) uint64_t full[4];
+  __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8;
-  const int nfc = (F + kGUF - 1) / kGUF;
+  const uint32_t stage_bytes = 2u * fr * H * 2;
+  uint8_t* stage_base = dsm_raw;
+  uint4* xs = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][hv]
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  wait_prior_grid();
+  allow_next_grid();
+  const int nfc = (F + fr - 1) / fr;
   const int items = *ws.nactive * nfc;
-  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+  const int mine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto issue = [&](int j) {
+    const int item = blockIdx.x + j * gridDim.x;
     const int e = ws.active[item / nfc];
-    const int f = (item % nfc) * kGUF + warp;
+    const int f0 = (item % nfc) * fr;
+    const int rows = min(fr, F - f0);
+    const uint32_t bytes = (uint32_t)rows * H * 2;
+    const int s = j % stages;
+    const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
+    const uint32_t bar = smem_u32(&full[s]);
+    mbar_expect_tx(bar, 2 * bytes);
+    bulk_load(dst, w_gate + ((int64_t)e * F + f0) * H, bytes, bar);
+    bulk_load(dst + (uint32_t)fr * H * 2, w_up + ((int64_t)e * F + f0) * H, bytes, bar);
+  };
+  if (threadIdx.x == 0)
+    for (int j = 0; j < stages && j < mine; ++j) issue(j);
+  for (int j = 0; j < mine; ++j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    const int e = ws.active[item / nfc];
+    const int f0 = (item % nfc) * fr;
+    const int rows = min(fr, F - f0);
+    const int s = j % stages;
+    if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, &s_abort, ws.err)) break;
+    const uint4* gsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
+    const uint4* usm = gsm + (size_t)fr * hv;
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
-    const uint4* wg = reinterpret_cast<const uint4*>(w_gate + ((int64_t)e * F + min(f, F - 1)) * H);
-    const uint4* wu = reinterpret_cast<const uint4*>(w_up + ((int64_t)e * F + min(f, F - 1)) * H);
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
-      uint4 gq[kRV], uq[kRV];
-#pragma unroll
-      for (int i = 0; i < kRV; ++i) {
-        const int v = lane + 32 * i;
-        gq[i] = v < hv ? __ldg(wg + v) : make_uint4(0, 0, 0, 0);
-        uq[i] = v < hv ? __ldg(wu + v) : make_uint4(0, 0, 0, 0);
-      }
-      __syncthreads();
       for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
         const int r = i / hv, v = i - r * hv;
         const int t = ws.sorted_slots[r0 + c0 + r] % T;
-        xsm[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
+        xs[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
       }
       __syncthreads();
-      for (int v0 = 0; v0 < hv; v0 += 32 * kRV) {
-        if (v0 != 0) {
-#pragma unroll
-          for (int i = 0; i < kRV; ++i) {
-            const int v = v0 + lane + 32 * i;
-            gq[i] = v < hv ? __ldg(wg + v) : make_uint4(0, 0, 0, 0);
-            uq[i] = v < hv ? __ldg(wu + v) : make_uint4(0, 0, 0, 0);
-          }
-        }
+      if (warp < rows) {
+        const uint4* gr = gsm + (size_t)warp * hv;
+        const uint4* ur = usm + (size_t)warp * hv;
         for (int r = 0; r < rc; ++r) {
           float g = 0.f, u = 0.f;
+          for (int v = lane; v < hv; v += 32) {
+            float gv[8], uv[8], xv[8];
+            bf16x8_to_f32(gr[v], gv);
+            bf16x8_to_f32(ur[v], uv);
+            bf16x8_to_f32(xs[r * hv + v], xv);
 #pragma unroll
-          for (int i = 0; i < kRV; ++i) {
-            const int v = v0 + lane + 32 * i;
-            if (v < hv) {
-              float gv[8], uv[8], xv[8];
-              bf16x8_unpack_here(gq[i], gv);
-              bf16x8_unpack_here(uq[i], uv);
-              bf16x8_to_f32(xsm[r * hv + v], xv);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                g = fmaf(gv[q], xv[q], g);
-                u = fmaf(uv[q], xv[q], u);
-              }
+            for (int q = 0; q < 8; ++q) {
+              g = fmaf(gv[q], xv[q], g);
+              u = fmaf(uv[q], xv[q], u);
             }
           }
 #pragma unroll
@@ -275,105 +308,92 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
             g += __shfl_xor_sync(0xffffffffu, g, o);
             u += __shfl_xor_sync(0xffffffffu, u, o);
           }
-          if (lane == 0) {
-            part[warp][0][r] = (v0 == 0 ? 0.f : part[warp][0][r]) + g;
-            part[warp][1][r] = (v0 == 0 ? 0.f : part[warp][1][r]) + u;
-          }
+          if (lane == 0) ws.hs[(int64_t)(r0 + c0 + r) * F + f0 + warp] = __float2bfloat16_rn(g * silu_ref(u));
         }
       }
-      __syncwarp();
-      if (lane < rc && f < F) {
-        const float g = part[warp][0][lane], u = part[warp][1][lane];
-        ws.hs[(int64_t)(r0 + c0 + lane) * F + f] = __float2bfloat16_rn(g * silu_ref(u));
-      }
+      __syncthreads();
+    }
+    if (threadIdx.x == 0 && j + stages < mine) {
+      fence_proxy_async_smem();  // generic reads of stage s precede the bulk copy that refills it
+      issue(j + stages);
     }
   }
 }
 
-// ------------------------------------------------------------------ down --
-// Persistent blocks over items (active expert, 32 rows of H): warp w streams
-// down rows h0..h0+3 (all slices of a round requested up front) while the
-// expert's h rows are staged in shared memory; rows of h one at a time.
+// down: item = (active expert e, hr rows of H starting at h0): stage =
+// [hr][F] bf16.  Warp w computes rows h0 + w, h0 + w + 8, ...:
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
-constexpr int kDH = 4;                  // down rows per warp
-constexpr int kDItem = kDH * kWarps;    // down rows per item
-constexpr int kDV = 4;                  // slices per lane per round and row
-
 __global__ void __launch_bounds__(kThreads)
-decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, DecodeWs ws) {
-  extern __shared__ uint4 hsm[];  // [kRC][F/8]
-  __shared__ float part[kWarps][kDH][kRC];
-  wait_prior_grid();
-  allow_next_grid();
+decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int hr, int stages, DecodeWs ws) {
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  __shared__ __align__(8) uint64_t full[4];
+  __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fv = F / 8;
-  const int nhc = (H + kDItem - 1) / kDItem;
+  const uint32_t stage_bytes = (uint32_t)hr * F * 2;
+  uint8_t* stage_base = dsm_raw;
+  uint4* hsm = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][fv]
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
+    s_abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  __syncthreads();
+  wait_prior_grid();
+  allow_next_grid();
+  const int nhc = (H + hr - 1) / hr;
   const int items = *ws.nactive * nhc;
-  for (int item = blockIdx.x; item < items; item += gridDim.x) {
+  const int mine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  auto issue = [&](int j) {
+    const int item = blockIdx.x + j * gridDim.x;
     const int e = ws.active[item / nhc];
-    const int h0 = (item % nhc) * kDItem + warp * kDH;
+    const int h0 = (item % nhc) * hr;
+    const uint32_t bytes = (uint32_t)min(hr, H - h0) * F * 2;
+    const int s = j % stages;
+    const uint32_t bar = smem_u32(&full[s]);
+    mbar_expect_tx(bar, bytes);
+    bulk_load(smem_u32(stage_base + (size_t)s * stage_bytes), w_down + ((int64_t)e * H + h0) * F, bytes, bar);
+  };
+  if (threadIdx.x == 0)
+    for (int j = 0; j < stages && j < mine; ++j) issue(j);
+  for (int j = 0; j < mine; ++j) {
+    const int item = blockIdx.x + j * gridDim.x;
+    const int e = ws.active[item / nhc];
+    const int h0 = (item % nhc) * hr;
+    const int rows = min(hr, H - h0);
+    const int s = j % stages;
+    if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, &s_abort, ws.err)) break;
+    const uint4* wsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
-    const __nv_bfloat16* wd = w_down + (int64_t)e * H * F;
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
-      uint4 wq[kDH][kDV];
-#pragma unroll
-      for (int j = 0; j < kDH; ++j)
-#pragma unroll
-        for (int i = 0; i < kDV; ++i) {
-          const int v = lane + 32 * i;
-          wq[j][i] = v < fv ? __ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v)
-                            : make_uint4(0, 0, 0, 0);
-        }
-      __syncthreads();
       for (int i = threadIdx.x; i < rc * fv; i += kThreads)
         hsm[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
       __syncthreads();
-      for (int v0 = 0; v0 < fv; v0 += 32 * kDV) {
-        if (v0 != 0) {
-#pragma unroll
-          for (int j = 0; j < kDH; ++j)
-#pragma unroll
-            for (int i = 0; i < kDV; ++i) {
-              const int v = v0 + lane + 32 * i;
-              wq[j][i] = v < fv ? __ldg(reinterpret_cast<const uint4*>(wd + (int64_t)min(h0 + j, H - 1) * F) + v)
-                                : make_uint4(0, 0, 0, 0);
-            }
-        }
+      for (int jr = warp; jr < rows; jr += kWarps) {
+        const uint4* wr = wsm + (size_t)jr * fv;
         for (int r = 0; r < rc; ++r) {
-          float acc[kDH] = {0.f, 0.f, 0.f, 0.f};
+          float acc = 0.f;
+          for (int v = lane; v < fv; v += 32) {
+            float wv[8], hv8[8];
+            bf16x8_to_f32(wr[v], wv);
+            bf16x8_to_f32(hsm[r * fv + v], hv8);
 #pragma unroll
-          for (int i = 0; i < kDV; ++i) {
-            const int v = v0 + lane + 32 * i;
-            if (v < fv) {
-              float hv8[8];
-              bf16x8_to_f32(hsm[r * fv + v], hv8);
-#pragma unroll
-              for (int j = 0; j < kDH; ++j) {
-                float wv[8];
-                bf16x8_unpack_here(wq[j][i], wv);
-#pragma unroll
-                for (int q = 0; q < 8; ++q) acc[j] = fmaf(wv[q], hv8[q], acc[j]);
-              }
-            }
+            for (int q = 0; q < 8; ++q) acc = fmaf(wv[q], hv8[q], acc);
           }
 #pragma unroll
-          for (int j = 0; j < kDH; ++j) {
-            float v = acc[j];
-#pragma unroll
-            for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-            if (lane == 0) part[warp][j][r] = (v0 == 0 ? 0.f : part[warp][j][r]) + v;
+          for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+          if (lane == 0) {
+            const int row = r0 + c0 + r;
+            ws.d[(int64_t)row * H + h0 + jr] = acc * ws.wsorted[row];
           }
         }
       }
-      __syncwarp();
-      if (lane < kDH * kRC) {
-        const int j = lane / kRC, r = lane - j * kRC;
-        if (r < rc && h0 + j < H) {
-          const int row = r0 + c0 + r;
-          ws.d[(int64_t)row * H + h0 + j] = part[warp][j][r] * ws.wsorted[row];
-        }
-      }
+      __syncthreads();
+    }
+    if (threadIdx.x == 0 && j + stages < mine) {
+      fence_proxy_async_smem();
+      issue(j + stages);
     }
   }
 }
@@ -415,7 +435,7 @@ namespace frank {
 
 bool decode_path_ok(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
   return dtype == FRANK_BF16 && T >= 1 && T <= 64 && k * T <= kMaxSlots && E <= kMaxE && H % 8 == 0 && F % 8 == 0 &&
-         H <= 8192 && F <= 8192;
+         H <= 4096 && F <= 8192 && k * T <= E;
 }
 
 size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
@@ -479,21 +499,39 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   mark(1, st);
   mark(2, st);
   mark(3, st);
-  const int grid_p = num_sms() * 2;
+  ws.err = device_error_word();
+  const int grid_p = num_sms();
+  const size_t kSmemMax = 227 * 1024;
   {
-    const size_t smem = (size_t)kRC * H * 2;
+    const int fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
+    const size_t stage = (size_t)2 * fr * H * 2, xs = (size_t)kRC * H * 2;
+    int stages = (int)((kSmemMax - xs - 1024) / stage);
+    stages = stages > 3 ? 3 : stages;
+    if (stages < 2) {
+      set_error("decode block: n_embd=%lld too large for the streaming kernel", (long long)H);
+      return FRANK_EINVAL;
+    }
+    const size_t smem = stages * stage + xs;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kThreads), smem, st,
                               (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
-                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, ws));
+                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, fr, stages, ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(4, st);
   {
-    const size_t smem = (size_t)kRC * F * 2;
+    const int hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
+    const size_t stage = (size_t)hr * F * 2, hs = (size_t)kRC * F * 2;
+    int stages = (int)((kSmemMax - hs - 1024) / stage);
+    stages = stages > 4 ? 4 : stages;
+    if (stages < 2) {
+      set_error("decode block: n_ff=%lld too large for the streaming kernel", (long long)F);
+      return FRANK_EINVAL;
+    }
+    const size_t smem = stages * stage + hs;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     FRANK_CUDA_TRY(launch_pdl(decode_down_kernel, dim3(grid_p), dim3(kThreads), smem, st,
-                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, ws));
+                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, hr, stages, ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(5, st);
