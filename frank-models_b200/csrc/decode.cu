@@ -240,9 +240,11 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8;
-  const uint32_t stage_bytes = 2u * fr * H * 2;
+  // stage: [2][fr][H] weights, then [kRC][H] token rows of the item's expert
+  const uint32_t wbytes = 2u * fr * H * 2;
+  const uint32_t stage_bytes = wbytes + (uint32_t)kRC * H * 2;
   uint8_t* stage_base = dsm_raw;
-  uint4* xs = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][hv]
+  uint4* xs = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][hv], rows beyond kRC
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
     s_abort = 0;
@@ -263,9 +265,14 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
     const int s = j % stages;
     const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
     const uint32_t bar = smem_u32(&full[s]);
-    mbar_expect_tx(bar, 2 * bytes);
+    const int r0 = ws.offsets[e];
+    const int rc = min(kRC, ws.offsets[e + 1] - r0);
+    const uint32_t xrow = (uint32_t)H * 2;
+    mbar_expect_tx(bar, 2 * bytes + rc * xrow);
     bulk_load(dst, w_gate + ((int64_t)e * F + f0) * H, bytes, bar);
     bulk_load(dst + (uint32_t)fr * H * 2, w_up + ((int64_t)e * F + f0) * H, bytes, bar);
+    for (int r = 0; r < rc; ++r)
+      bulk_load(dst + wbytes + r * xrow, x + (int64_t)(ws.sorted_slots[r0 + r] % T) * H, xrow, bar);
   };
   if (threadIdx.x == 0)
     for (int j = 0; j < stages && j < mine; ++j) issue(j);
@@ -281,12 +288,16 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
-      for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
-        const int r = i / hv, v = i - r * hv;
-        const int t = ws.sorted_slots[r0 + c0 + r] % T;
-        xs[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
+      const uint4* xr = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
+      if (c0 > 0) {  // more than kRC rows: later chunks are gathered by the block
+        for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
+          const int r = i / hv, v = i - r * hv;
+          const int t = ws.sorted_slots[r0 + c0 + r] % T;
+          xs[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
+        }
+        __syncthreads();
+        xr = xs;
       }
-      __syncthreads();
       if (warp < rows) {
         const uint4* gr = gsm + (size_t)warp * hv;
         const uint4* ur = usm + (size_t)warp * hv;
@@ -296,7 +307,7 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
             float gv[8], uv[8], xv[8];
             bf16x8_to_f32(gr[v], gv);
             bf16x8_to_f32(ur[v], uv);
-            bf16x8_to_f32(xs[r * hv + v], xv);
+            bf16x8_to_f32(xr[r * hv + v], xv);
 #pragma unroll
             for (int q = 0; q < 8; ++q) {
               g = fmaf(gv[q], xv[q], g);
@@ -330,9 +341,11 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int h
   __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fv = F / 8;
-  const uint32_t stage_bytes = (uint32_t)hr * F * 2;
+  // stage: [hr][F] weights, then [kRC][F] h rows of the item's expert
+  const uint32_t wbytes = (uint32_t)hr * F * 2;
+  const uint32_t stage_bytes = wbytes + (uint32_t)kRC * F * 2;
   uint8_t* stage_base = dsm_raw;
-  uint4* hsm = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][fv]
+  uint4* hsm = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][fv], rows beyond kRC
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
     s_abort = 0;
@@ -351,8 +364,13 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int h
     const uint32_t bytes = (uint32_t)min(hr, H - h0) * F * 2;
     const int s = j % stages;
     const uint32_t bar = smem_u32(&full[s]);
-    mbar_expect_tx(bar, bytes);
-    bulk_load(smem_u32(stage_base + (size_t)s * stage_bytes), w_down + ((int64_t)e * H + h0) * F, bytes, bar);
+    const int r0 = ws.offsets[e];
+    const int rc = min(kRC, ws.offsets[e + 1] - r0);
+    const uint32_t hbytes = (uint32_t)rc * F * 2;
+    const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
+    mbar_expect_tx(bar, bytes + hbytes);
+    bulk_load(dst, w_down + ((int64_t)e * H + h0) * F, bytes, bar);
+    bulk_load(dst + wbytes, ws.hs + (int64_t)r0 * F, hbytes, bar);
   };
   if (threadIdx.x == 0)
     for (int j = 0; j < stages && j < mine; ++j) issue(j);
@@ -367,9 +385,13 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int h
     const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
-      for (int i = threadIdx.x; i < rc * fv; i += kThreads)
-        hsm[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
-      __syncthreads();
+      const uint4* hr8 = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
+      if (c0 > 0) {
+        for (int i = threadIdx.x; i < rc * fv; i += kThreads)
+          hsm[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
+        __syncthreads();
+        hr8 = hsm;
+      }
       for (int jr = warp; jr < rows; jr += kWarps) {
         const uint4* wr = wsm + (size_t)jr * fv;
         for (int r = 0; r < rc; ++r) {
@@ -377,7 +399,7 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int h
           for (int v = lane; v < fv; v += 32) {
             float wv[8], hv8[8];
             bf16x8_to_f32(wr[v], wv);
-            bf16x8_to_f32(hsm[r * fv + v], hv8);
+            bf16x8_to_f32(hr8[r * fv + v], hv8);
 #pragma unroll
             for (int q = 0; q < 8; ++q) acc = fmaf(wv[q], hv8[q], acc);
           }
@@ -504,9 +526,9 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   const size_t kSmemMax = 227 * 1024;
   {
     const int fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
-    const size_t stage = (size_t)2 * fr * H * 2, xs = (size_t)kRC * H * 2;
+    const size_t xs = (size_t)kRC * H * 2, stage = (size_t)2 * fr * H * 2 + xs;
     int stages = (int)((kSmemMax - xs - 1024) / stage);
-    stages = stages > 3 ? 3 : stages;
+    stages = stages > 4 ? 4 : stages;
     if (stages < 2) {
       set_error("decode block: n_embd=%lld too large for the streaming kernel", (long long)H);
       return FRANK_EINVAL;
@@ -521,7 +543,7 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   mark(4, st);
   {
     const int hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
-    const size_t stage = (size_t)hr * F * 2, hs = (size_t)kRC * F * 2;
+    const size_t hs = (size_t)kRC * F * 2, stage = (size_t)hr * F * 2 + hs;
     int stages = (int)((kSmemMax - hs - 1024) / stage);
     stages = stages > 4 ? 4 : stages;
     if (stages < 2) {
