@@ -1,14 +1,14 @@
-// Decode-sized MoE FFN block (a few tokens per step): four launches,
+// Decode-sized MoE FFN block (a few tokens per step): five launches,
 // weight-streaming on CUDA cores.
 //
 // With T <= 64 tokens an expert receives a handful of rows, so the block is
 // bound by reading the active experts' weights from HBM (3 x H x F bf16 per
 // active expert) -- tensor cores would idle on 128-row tiles.  The kernels:
 //   decode_route_kernel    router logits (one warp per (expert, 8 tokens));
-//                          the last block to finish runs softmax + top-k +
-//                          renorm for every token, the stable expert
-//                          permutation and the list of active experts
-//                          (moe_ffn_block.mlir:54-128, mul_mat_id.mlir:51-53);
+//   decode_finalize_kernel one block: softmax + top-k + renorm for every
+//                          token, the stable expert permutation and the list
+//                          of active experts (moe_ffn_block.mlir:54-128,
+//                          mul_mat_id.mlir:51-53);
 //   decode_gateup_kernel   persistent blocks over (active expert, 8 rows of F):
 //                          one gate row and one up row per warp streamed once
 //                          and dotted with the expert's token rows (gathered
@@ -18,8 +18,7 @@
 //                          H): d = down(h) * gate weight, fp32;
 //   combine_kernel         y[t] = sum of the k slots of t in slot order
 //                          (moe_ffn_block.mlir:179-206), deterministic.
-// The only atomic is the completion ticket of the route kernel; it resets
-// itself, and the launcher zeroes it at every call.
+// Consecutive kernels use programmatic dependent launch; no atomics.
 #include "common.cuh"
 #include "mbarrier.cuh"
 #include "topk.cuh"
@@ -72,7 +71,6 @@ __device__ __forceinline__ void load8_w<__nv_bfloat16>(const __nv_bfloat16* p, f
 
 struct DecodeWs {
   float* logits;        // [E, T]
-  unsigned* ticket;     // completion counter of the route kernel
   float* w;             // [k, T] gate weights
   int32_t* ids;         // [k, T]
   int32_t* sorted_slots;
@@ -85,6 +83,11 @@ struct DecodeWs {
   float* d;             // [k*T, H] down output x gate weight
   int32_t* err;         // device error word (bounded waits)
 };
+
+// Programmatic dependent launch: a kernel's blocks may start while the
+// previous kernel of the stream finishes; they wait here for its results.
+__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // ----------------------------------------------------------------- route --
 template <class TW>
@@ -122,14 +125,16 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
       if (lane == 0 && t0 + a < T) ws.logits[(int64_t)e * T + t0 + a] = v;
     }
   }
-  // ---- the last block: softmax + top-k for every token, then the permutation
-  __shared__ unsigned s_last;
-  __threadfence();
-  __syncthreads();
-  if (threadIdx.x == 0) s_last = (atomicAdd(ws.ticket, 1u) == gridDim.x - 1);
-  __syncthreads();
-  if (!s_last) return;
-  __threadfence();
+}
+
+// One block: softmax + top-k + renorm for every token, the stable expert
+// permutation (same order as argsort(ids.reshape(-1), stable)) and the list of
+// active experts.
+__global__ void __launch_bounds__(kThreads)
+decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
+  wait_prior_grid();
+  allow_next_grid();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   __shared__ float lg[kWarps][kMaxE];
   for (int t = warp; t < T; t += kWarps) {
     for (int e = lane; e < E; e += 32) lg[warp][e] = ws.logits[(int64_t)e * T + t];
@@ -196,8 +201,7 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
     if (lane == 0) {
       ws.offsets[E] = carry;
       *ws.nactive = na;
-      *ws.ticket = 0;  // ready for the next call
-    }
+      }
   }
   __syncthreads();
   for (int s = threadIdx.x; s < n; s += kThreads) {
@@ -208,10 +212,6 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   }
 }
 
-// Programmatic dependent launch: a kernel's blocks may start while the
-// previous kernel of the stream finishes; they wait here for its results.
-__device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // ----------------------------------------------- weight-streaming GEMVs --
 // Both GEMV kernels stream contiguous chunks of an expert's weight rows from
@@ -233,9 +233,12 @@ struct StreamSmem {
 // f0 + w for each token row: h = gate . x * silu(up . x).
 __global__ void __launch_bounds__(kThreads)
 decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
-                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int fr, int stages,
+                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int stages,
                      DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
+  // routing metadata cached once per block so that refilling a stage needs no
+  // global round trips: expert offsets, active experts, token of each row
+  __shared__ int32_t sm_off[kMaxE + 1], sm_act[kMaxE], sm_tok[kMaxSlots];
   __shared__ __align__(8) uint64_t full[4];
   __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -244,59 +247,61 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   const uint32_t wbytes = 2u * fr * H * 2;
   const uint32_t stage_bytes = wbytes + (uint32_t)kRC * H * 2;
   uint8_t* stage_base = dsm_raw;
-  uint4* xs = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][hv], rows beyond kRC
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
   wait_prior_grid();
   allow_next_grid();
+  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = ws.offsets[i];
+  const int nact = *ws.nactive;
+  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = ws.active[i];
+  __syncthreads();
+  for (int i = threadIdx.x; i < sm_off[E]; i += kThreads) sm_tok[i] = ws.sorted_slots[i] % T;
+  __syncthreads();
   const int nfc = (F + fr - 1) / fr;
-  const int items = *ws.nactive * nfc;
+  const int items = nact * nfc;
   const int mine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   auto issue = [&](int j) {
     const int item = blockIdx.x + j * gridDim.x;
-    const int e = ws.active[item / nfc];
+    const int e = sm_act[item / nfc];
     const int f0 = (item % nfc) * fr;
     const int rows = min(fr, F - f0);
     const uint32_t bytes = (uint32_t)rows * H * 2;
     const int s = j % stages;
     const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
     const uint32_t bar = smem_u32(&full[s]);
-    const int r0 = ws.offsets[e];
-    const int rc = min(kRC, ws.offsets[e + 1] - r0);
+    const int r0 = sm_off[e];
+    const int rc = min(kRC, sm_off[e + 1] - r0);
     const uint32_t xrow = (uint32_t)H * 2;
     mbar_expect_tx(bar, 2 * bytes + rc * xrow);
     bulk_load(dst, w_gate + ((int64_t)e * F + f0) * H, bytes, bar);
     bulk_load(dst + (uint32_t)fr * H * 2, w_up + ((int64_t)e * F + f0) * H, bytes, bar);
     for (int r = 0; r < rc; ++r)
-      bulk_load(dst + wbytes + r * xrow, x + (int64_t)(ws.sorted_slots[r0 + r] % T) * H, xrow, bar);
+      bulk_load(dst + wbytes + r * xrow, x + (int64_t)sm_tok[r0 + r] * H, xrow, bar);
   };
   if (threadIdx.x == 0)
     for (int j = 0; j < stages && j < mine; ++j) issue(j);
   for (int j = 0; j < mine; ++j) {
     const int item = blockIdx.x + j * gridDim.x;
-    const int e = ws.active[item / nfc];
+    const int e = sm_act[item / nfc];
     const int f0 = (item % nfc) * fr;
     const int rows = min(fr, F - f0);
     const int s = j % stages;
     if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, &s_abort, ws.err)) break;
     const uint4* gsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
     const uint4* usm = gsm + (size_t)fr * hv;
-    const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
+    const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
-      const uint4* xr = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
-      if (c0 > 0) {  // more than kRC rows: later chunks are gathered by the block
+      uint4* xr = reinterpret_cast<uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
+      if (c0 > 0) {  // more than kRC rows: later chunks are gathered into the same area
         for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
           const int r = i / hv, v = i - r * hv;
-          const int t = ws.sorted_slots[r0 + c0 + r] % T;
-          xs[i] = reinterpret_cast<const uint4*>(x + (int64_t)t * H)[v];
+          xr[i] = reinterpret_cast<const uint4*>(x + (int64_t)sm_tok[r0 + c0 + r] * H)[v];
         }
         __syncthreads();
-        xr = xs;
       }
       if (warp < rows) {
         const uint4* gr = gsm + (size_t)warp * hv;
@@ -335,8 +340,9 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 // [hr][F] bf16.  Warp w computes rows h0 + w, h0 + w + 8, ...:
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
 __global__ void __launch_bounds__(kThreads)
-decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int hr, int stages, DecodeWs ws) {
+decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
+  __shared__ int32_t sm_off[kMaxE + 1], sm_act[kMaxE];
   __shared__ __align__(8) uint64_t full[4];
   __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -345,27 +351,29 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int h
   const uint32_t wbytes = (uint32_t)hr * F * 2;
   const uint32_t stage_bytes = wbytes + (uint32_t)kRC * F * 2;
   uint8_t* stage_base = dsm_raw;
-  uint4* hsm = reinterpret_cast<uint4*>(dsm_raw + (size_t)stages * stage_bytes);  // [kRC][fv], rows beyond kRC
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
     s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  __syncthreads();
   wait_prior_grid();
   allow_next_grid();
+  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = ws.offsets[i];
+  const int nact = *ws.nactive;
+  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = ws.active[i];
+  __syncthreads();
   const int nhc = (H + hr - 1) / hr;
-  const int items = *ws.nactive * nhc;
+  const int items = nact * nhc;
   const int mine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
   auto issue = [&](int j) {
     const int item = blockIdx.x + j * gridDim.x;
-    const int e = ws.active[item / nhc];
+    const int e = sm_act[item / nhc];
     const int h0 = (item % nhc) * hr;
     const uint32_t bytes = (uint32_t)min(hr, H - h0) * F * 2;
     const int s = j % stages;
     const uint32_t bar = smem_u32(&full[s]);
-    const int r0 = ws.offsets[e];
-    const int rc = min(kRC, ws.offsets[e + 1] - r0);
+    const int r0 = sm_off[e];
+    const int rc = min(kRC, sm_off[e + 1] - r0);
     const uint32_t hbytes = (uint32_t)rc * F * 2;
     const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
     mbar_expect_tx(bar, bytes + hbytes);
@@ -376,21 +384,20 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int h
     for (int j = 0; j < stages && j < mine; ++j) issue(j);
   for (int j = 0; j < mine; ++j) {
     const int item = blockIdx.x + j * gridDim.x;
-    const int e = ws.active[item / nhc];
+    const int e = sm_act[item / nhc];
     const int h0 = (item % nhc) * hr;
     const int rows = min(hr, H - h0);
     const int s = j % stages;
     if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, &s_abort, ws.err)) break;
     const uint4* wsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
-    const int r0 = ws.offsets[e], cnt = ws.offsets[e + 1] - r0;
+    const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
       const int rc = min(kRC, cnt - c0);
-      const uint4* hr8 = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
-      if (c0 > 0) {
+      uint4* hr8 = reinterpret_cast<uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
+      if (c0 > 0) {  // more than kRC rows: later chunks are loaded into the same area
         for (int i = threadIdx.x; i < rc * fv; i += kThreads)
-          hsm[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
+          hr8[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
         __syncthreads();
-        hr8 = hsm;
       }
       for (int jr = warp; jr < rows; jr += kWarps) {
         const uint4* wr = wsm + (size_t)jr * fv;
@@ -464,7 +471,6 @@ size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t
   Carve c(nullptr, 0);
   const int64_t n = k * T;
   c.take<float>(E * T);
-  c.take<unsigned>(1);
   c.take<float>(n);
   c.take<int32_t>(n);
   c.take<int32_t>(n);
@@ -496,7 +502,6 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   Carve c(workspace, ws_bytes);
   DecodeWs ws;
   ws.logits = c.take<float>(E * T);
-  ws.ticket = c.take<unsigned>(1);
   ws.w = c.take<float>(n);
   ws.ids = c.take<int32_t>(n);
   ws.sorted_slots = c.take<int32_t>(n);
@@ -508,7 +513,6 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.nactive = c.take<int32_t>(1);
   ws.d = c.take<float>(n * H);
   mark(0, st);
-  FRANK_CUDA_TRY(cudaMemsetAsync(ws.ticket, 0, sizeof(unsigned), st));
   const int64_t items = E * ((T + kRouteTok - 1) / kRouteTok);
   const unsigned rblocks = (unsigned)((items + kWarps - 1) / kWarps);
   if (wr_dtype == FRANK_F32)
@@ -518,6 +522,9 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
     decode_route_kernel<__nv_bfloat16><<<rblocks, kThreads, 0, st>>>(
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)wr, (int)T, (int)H, (int)E, (int)k, normalize, ws);
   FRANK_LAUNCH_CHECK();
+  FRANK_CUDA_TRY(launch_pdl(decode_finalize_kernel, dim3(1), dim3(kThreads), 0, st, (int)T, (int)E, (int)k,
+                            normalize, ws));
+  FRANK_LAUNCH_CHECK();
   mark(1, st);
   mark(2, st);
   mark(3, st);
@@ -526,34 +533,34 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   const size_t kSmemMax = 227 * 1024;
   {
     const int fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
-    const size_t xs = (size_t)kRC * H * 2, stage = (size_t)2 * fr * H * 2 + xs;
-    int stages = (int)((kSmemMax - xs - 1024) / stage);
+    const size_t stage = (size_t)2 * fr * H * 2 + (size_t)kRC * H * 2;
+    int stages = (int)((kSmemMax - 16 * 1024) / stage);
     stages = stages > 4 ? 4 : stages;
     if (stages < 2) {
       set_error("decode block: n_embd=%lld too large for the streaming kernel", (long long)H);
       return FRANK_EINVAL;
     }
-    const size_t smem = stages * stage + xs;
+    const size_t smem = stages * stage;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kThreads), smem, st,
                               (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
-                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, fr, stages, ws));
+                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, (int)E, fr, stages, ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(4, st);
   {
     const int hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
-    const size_t hs = (size_t)kRC * F * 2, stage = (size_t)hr * F * 2 + hs;
-    int stages = (int)((kSmemMax - hs - 1024) / stage);
+    const size_t stage = (size_t)hr * F * 2 + (size_t)kRC * F * 2;
+    int stages = (int)((kSmemMax - 4 * 1024) / stage);
     stages = stages > 4 ? 4 : stages;
     if (stages < 2) {
       set_error("decode block: n_ff=%lld too large for the streaming kernel", (long long)F);
       return FRANK_EINVAL;
     }
-    const size_t smem = stages * stage + hs;
+    const size_t smem = stages * stage;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     FRANK_CUDA_TRY(launch_pdl(decode_down_kernel, dim3(grid_p), dim3(kThreads), smem, st,
-                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, hr, stages, ws));
+                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, (int)E, hr, stages, ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(5, st);
