@@ -13,7 +13,7 @@ namespace frank {
 int launch_softmax_topk(const float*, int64_t, int64_t, int64_t, int, float*, int32_t*, cudaStream_t);
 int launch_router_topk(int, const void*, int, const void*, int64_t, int64_t, int64_t, int64_t, int, float*, int32_t*,
                        float*, cudaStream_t);
-size_t router_logits_bytes(int64_t, int64_t);
+size_t router_scratch_bytes(int, int64_t, int64_t, int64_t);
 size_t permute_workspace_size(int64_t, int64_t);
 int launch_permute(const int32_t*, int64_t, int64_t, int32_t*, int32_t*, int32_t*, int32_t*, void*, size_t,
                    cudaStream_t);
@@ -158,7 +158,7 @@ static size_t moe_layout(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, 
   l.xs = c.take<char>(n * H * esz);
   l.hs = c.take<char>(n * F * esz);
   l.ds = c.take<float>(n * H);
-  l.logits = c.take<float>(router_logits_bytes(T, E) / sizeof(float));
+  l.logits = c.take<float>(router_scratch_bytes(dtype, T, H, E) / sizeof(float) + 1);
   l.perm_bytes = permute_workspace_size(n, E);
   l.perm_ws = c.take<char>(l.perm_bytes);
   if (L) *L = l;
@@ -227,7 +227,9 @@ int frank_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k, int
   return launch_softmax_topk(logits, T, E, k, normalize, weights, ids, as_stream(stream));
 }
 
-size_t frank_router_scratch_bytes(int64_t T, int64_t E) { return router_logits_bytes(T, E); }
+size_t frank_router_scratch_bytes(int x_dtype, int64_t T, int64_t H, int64_t E) {
+  return router_scratch_bytes(x_dtype, T, H, E);
+}
 
 int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H, int64_t E,
                       int64_t k, int normalize, float* weights, int32_t* ids, float* logits_scratch, void* stream) {

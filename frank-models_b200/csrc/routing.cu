@@ -193,6 +193,46 @@ router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T
   }
 }
 
+// Tensor-core router for many experts.  wr (fp32) is split exactly into three
+// bf16 terms, hi = bf16(w), mid = bf16(w - hi), lo = bf16(w - hi - mid)
+// (hi + mid + lo carries all 24 bits of w), stacked as a [3E, H] matrix, so
+// logits = x.hi + x.mid + x.lo comes out of one bf16 GEMM with fp32
+// accumulation (x is bf16, hence exact in the products).  The three partial
+// dot products are added in fp32 before softmax + top-k.
+template <class TW>
+__global__ void router_split_kernel(const TW* __restrict__ wr, int E, int H, int64_t T,
+                                    __nv_bfloat16* __restrict__ wr3, int32_t* __restrict__ offs) {
+  const int64_t EH = (int64_t)E * H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < EH; i += (int64_t)gridDim.x * blockDim.x) {
+    const float w = load_as_f32(wr, i);
+    const __nv_bfloat16 hi = __float2bfloat16_rn(w);
+    const float r1 = w - __bfloat162float(hi);
+    const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+    const __nv_bfloat16 lo = __float2bfloat16_rn(r1 - __bfloat162float(mid));
+    wr3[i] = hi;
+    wr3[EH + i] = mid;
+    wr3[2 * EH + i] = lo;
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    offs[0] = 0;
+    offs[1] = (int32_t)T;
+  }
+}
+
+// One warp per token: logits[e] = (p[e] + p[E+e]) + p[2E+e] from the [T, 3E]
+// GEMM output, then softmax + top-k.
+__global__ void softmax_topk3_kernel(const float* __restrict__ l3, int64_t T, int E, int k, int normalize,
+                                     float* __restrict__ w, int32_t* __restrict__ ids) {
+  __shared__ float lg[8][kMaxE];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t t = (int64_t)blockIdx.x * 8 + warp;
+  if (t >= T) return;
+  const float* row = l3 + t * 3 * E;
+  for (int e = lane; e < E; e += 32) lg[warp][e] = (row[e] + row[E + e]) + row[2 * E + e];
+  __syncwarp();
+  warp_softmax_topk(lg[warp], E, k, normalize, w, ids, T, t);
+}
+
 // ---------------------------------------------------------------- permute --
 // Three passes, no atomics:
 //  A) per chunk of kChunk slots: stable local rank of each slot among the
@@ -375,12 +415,47 @@ static int launch_router_vec(const void* x, const void* wr, int64_t T, int64_t H
   return launch_router_vec_t<TX, TW, 1>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
 }
 
-size_t router_logits_bytes(int64_t T, int64_t E) { return E <= 8 ? 0 : (size_t)T * E * sizeof(float); }
+int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int32_t*, int64_t, int64_t, int64_t,
+                           int64_t, const float*, void*, cudaStream_t, const int32_t*, const int32_t*, float* const*,
+                           int);
 
-// logits: fp32 scratch of router_logits_bytes(T, E) bytes (unused when E <= 8).
+static bool router_tc_ok(int x_dtype, int64_t T, int64_t H, int64_t E) {
+  return x_dtype == FRANK_BF16 && E >= 16 && E % 16 == 0 && E <= kMaxE && H % 8 == 0 && T >= 128;
+}
+
+size_t router_scratch_bytes(int x_dtype, int64_t T, int64_t H, int64_t E) {
+  if (router_tc_ok(x_dtype, T, H, E))
+    return align_up((size_t)T * 3 * E * 4, 256) + align_up((size_t)3 * E * H * 2, 256) + 256;
+  return E <= 8 ? 0 : (size_t)T * E * sizeof(float);
+}
+
+static int launch_router_tc(const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H, int64_t E, int64_t k,
+                            int normalize, float* w, int32_t* ids, void* scratch, cudaStream_t st) {
+  Carve c(scratch, router_scratch_bytes(FRANK_BF16, T, H, E));
+  float* l3 = c.take<float>(T * 3 * E);
+  __nv_bfloat16* wr3 = c.take<__nv_bfloat16>(3 * E * H);
+  int32_t* offs = c.take<int32_t>(2);
+  const int64_t EH = E * H;
+  const unsigned blocks = (unsigned)((EH + 255) / 256 < 1024 ? (EH + 255) / 256 : 1024);
+  if (wr_dtype == FRANK_F32)
+    router_split_kernel<float><<<blocks, 256, 0, st>>>((const float*)wr, (int)E, (int)H, T, wr3, offs);
+  else
+    router_split_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)wr, (int)E, (int)H, T, wr3,
+                                                                offs);
+  FRANK_LAUNCH_CHECK();
+  FRANK_TRY(launch_tc_grouped_gemm(2, x, wr3, nullptr, offs, 1, T, 3 * E, H, nullptr, l3, st, nullptr, nullptr,
+                                   nullptr, 0));
+  softmax_topk3_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(l3, T, (int)E, (int)k, normalize, w, ids);
+  FRANK_LAUNCH_CHECK();
+  return FRANK_OK;
+}
+
+// logits: scratch of router_scratch_bytes(x_dtype, T, H, E) bytes (may be null: slower kernels).
 int launch_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H,
                        int64_t E, int64_t k, int normalize, float* w, int32_t* ids, float* logits, cudaStream_t st) {
   if (T == 0) return FRANK_OK;
+  if (logits != nullptr && router_tc_ok(x_dtype, T, H, E) && (uintptr_t)x % 16 == 0)
+    return launch_router_tc(x, wr_dtype, wr, T, H, E, k, normalize, w, ids, logits, st);
   const size_t esz = x_dtype == FRANK_F32 ? 4 : 2;
   const bool vec_ok = (H % 8 == 0) && ((uintptr_t)x % 16 == 0) && (H * 4 * 1 <= 160 * 1024) &&
                       (E <= 8 || logits != nullptr) && (H * esz) % 16 == 0;

@@ -35,7 +35,7 @@ SIGNATURES = {
     "frank_num_sms": (_c_int, []),
     "frank_swiglu": (_c_int, [_c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp]),
     "frank_softmax_topk": (_c_int, [_c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_vp]),
-    "frank_router_scratch_bytes": (_c_size, [_c_i64, _c_i64]),
+    "frank_router_scratch_bytes": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64]),
     "frank_router_topk": (_c_int, [_c_int, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
                                    _c_vp, _c_vp, _c_vp, _c_vp]),
     "frank_permute_workspace_size": (_c_size, [_c_i64, _c_i64]),

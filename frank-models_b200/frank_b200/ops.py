@@ -78,8 +78,8 @@ def router_topk(x: torch.Tensor, wr: torch.Tensor, k: int, normalize: bool):
     w = torch.empty((k, T), dtype=torch.float32, device=x.device)
     ids = torch.empty((k, T), dtype=torch.int32, device=x.device)
     lib = _lib.load()
-    nbytes = lib.frank_router_scratch_bytes(T, E)
-    scratch = torch.empty(nbytes // 4, dtype=torch.float32, device=x.device) if nbytes else None
+    nbytes = lib.frank_router_scratch_bytes(_dt(x), T, H, E)
+    scratch = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=x.device) if nbytes else None
     _lib.check(lib.frank_router_topk(_dt(x), _ptr(x), _dt(wr), _ptr(wr), T, H, E, k, int(bool(normalize)),
                                      _ptr(w), _ptr(ids), _ptr(scratch), _stream()))
     return w, ids

@@ -85,11 +85,14 @@ int frank_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k,
  * Router: logits = wr @ x.T in fp32, then frank_softmax_topk's rule
  * (moe_ffn_block.mlir:54-128, oracles/moe.py:87-105).
  * x_dtype / wr_dtype: FRANK_F32 or FRANK_BF16.  E <= 256, 1 <= k <= min(E, 32).
- * logits_scratch: fp32 device scratch of frank_router_scratch_bytes(T, E)
- * bytes (0 when E <= 8); with NULL and E > 8 a slower kernel that needs no
- * scratch is used.
+ * logits_scratch: device scratch of frank_router_scratch_bytes(x_dtype, T,
+ * H, E) bytes (0 when E <= 8), 256-byte aligned; with NULL a slower kernel
+ * that needs no scratch is used.  With bf16 x, E a multiple of 16 and
+ * T >= 128 the logits come from a tensor-core GEMM against wr split exactly
+ * into three bf16 terms (hi + mid + lo), accumulated in fp32.
  */
-size_t frank_router_scratch_bytes(int64_t T, int64_t E);
+size_t frank_router_scratch_bytes(int x_dtype, int64_t T, int64_t H,
+                                  int64_t E);
 int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr,
                       int64_t T, int64_t H, int64_t E, int64_t k, int normalize,
                       float* weights, int32_t* ids, float* logits_scratch,
