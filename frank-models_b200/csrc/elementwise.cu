@@ -110,21 +110,10 @@ __global__ void scatter_out_kernel(const float* __restrict__ ys, const int32_t* 
 // -------------------------------------------------------------- combine --
 // y[t, :] = sum_{j=0..k-1} d[slot_pos[j*T + t], :]   (moe_ffn_block.mlir:179-206,
 // oracles/moe.py:126-132).  The gate weight was already applied by the down
-// GEMM epilogue.  Fixed j order, fp32 sums, no atomics: deterministic.  4
-// values per thread; d is fp32 or bf16, y fp32 (16-byte store) or bf16.
-template <class TD>
-__device__ __forceinline__ float4 load4(const TD* p);
-template <>
-__device__ __forceinline__ float4 load4<float>(const float* p) { return *reinterpret_cast<const float4*>(p); }
-template <>
-__device__ __forceinline__ float4 load4<__nv_bfloat16>(const __nv_bfloat16* p) {
-  const uint2 u = *reinterpret_cast<const uint2*>(p);
-  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xffff0000u), __uint_as_float(u.y << 16),
-                     __uint_as_float(u.y & 0xffff0000u));
-}
-
-template <class TD, class TY>
-__global__ void combine_kernel(const TD* __restrict__ d, const int32_t* __restrict__ slot_pos, int64_t T,
+// GEMM epilogue.  Fixed j order, no atomics: deterministic.  4 floats per
+// thread; the store is a 16-byte (fp32) or 8-byte (bf16) vector.
+template <class TY>
+__global__ void combine_kernel(const float* __restrict__ d, const int32_t* __restrict__ slot_pos, int64_t T,
                                int k, int64_t H, TY* __restrict__ y) {
   const int64_t t = blockIdx.y;
   const int64_t h = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
@@ -132,7 +121,7 @@ __global__ void combine_kernel(const TD* __restrict__ d, const int32_t* __restri
   float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
   for (int j = 0; j < k; ++j) {
     int64_t r = slot_pos[(int64_t)j * T + t];
-    float4 v = load4(d + r * H + h);
+    float4 v = *reinterpret_cast<const float4*>(d + r * H + h);
     acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
   }
   if constexpr (sizeof(TY) == 4) {
@@ -145,13 +134,13 @@ __global__ void combine_kernel(const TD* __restrict__ d, const int32_t* __restri
   }
 }
 
-template <class TD, class TY>
-__global__ void combine_scalar_kernel(const TD* __restrict__ d, const int32_t* __restrict__ slot_pos,
+template <class TY>
+__global__ void combine_scalar_kernel(const float* __restrict__ d, const int32_t* __restrict__ slot_pos,
                                       int64_t T, int k, int64_t H, TY* __restrict__ y) {
   const int64_t t = blockIdx.y;
   for (int64_t h = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; h < H; h += (int64_t)gridDim.x * blockDim.x) {
     float acc = 0.f;
-    for (int j = 0; j < k; ++j) acc += load_as_f32(d, (int64_t)slot_pos[(int64_t)j * T + t] * H + h);
+    for (int j = 0; j < k; ++j) acc += d[(int64_t)slot_pos[(int64_t)j * T + t] * H + h];
     y[t * H + h] = from_f32<TY>(acc);
   }
 }
@@ -299,10 +288,10 @@ int launch_scatter_out(const float* ys, const int32_t* slot_pos, int64_t n_slots
   return FRANK_OK;
 }
 
-template <class TD>
-static int launch_combine_t(int dtype, const TD* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H, void* y,
-                            cudaStream_t st) {
-  bool vec_ok = (H % 4 == 0) && ((uintptr_t)d % (4 * sizeof(TD)) == 0) &&
+int launch_combine(int dtype, const float* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H, void* y,
+                   cudaStream_t st) {
+  if (T == 0 || H == 0) return FRANK_OK;
+  bool vec_ok = (H % 4 == 0) && ((uintptr_t)d % 16 == 0) &&
                 ((uintptr_t)y % (dtype == FRANK_F32 ? 16 : 8) == 0);
   for (int64_t t0 = 0; t0 < T; t0 += 65535) {
     int64_t tn = (T - t0) < 65535 ? (T - t0) : 65535;
@@ -311,29 +300,21 @@ static int launch_combine_t(int dtype, const TD* d, const int32_t* slot_pos, int
     if (vec_ok) {
       dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)tn);
       if (dtype == FRANK_F32)
-        combine_kernel<TD, float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H);
+        combine_kernel<float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H);
       else
-        combine_kernel<TD, __nv_bfloat16><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H,
-                                                                (__nv_bfloat16*)y + t0 * H);
+        combine_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H,
+                                                            (__nv_bfloat16*)y + t0 * H);
     } else {
       dim3 grid((unsigned)((H + 127) / 128 < 64 ? (H + 127) / 128 : 64), (unsigned)tn);
       if (dtype == FRANK_F32)
-        combine_scalar_kernel<TD, float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H);
+        combine_scalar_kernel<float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H);
       else
-        combine_scalar_kernel<TD, __nv_bfloat16><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H,
-                                                                       (__nv_bfloat16*)y + t0 * H);
+        combine_scalar_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H,
+                                                                   (__nv_bfloat16*)y + t0 * H);
     }
     FRANK_LAUNCH_CHECK();
   }
   return FRANK_OK;
-}
-
-// y (dtype) from d (d_dtype: FRANK_F32 or FRANK_BF16).
-int launch_combine(int dtype, int d_dtype, const void* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H,
-                   void* y, cudaStream_t st) {
-  if (T == 0 || H == 0) return FRANK_OK;
-  if (d_dtype == FRANK_F32) return launch_combine_t(dtype, (const float*)d, slot_pos, T, k, H, y, st);
-  return launch_combine_t(dtype, (const __nv_bfloat16*)d, slot_pos, T, k, H, y, st);
 }
 
 int launch_copy_row_segments(const void* src, void* dst, const int64_t* src_start, const int64_t* dst_start,

@@ -22,7 +22,7 @@ int launch_prepack(int, const void*, int64_t, int64_t, int64_t, int, void*, cuda
 int launch_gather_rows(int, const void*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
 int launch_gather_cols(int, const void*, const int32_t*, int64_t, int64_t, void*, cudaStream_t);
 int launch_scatter_out(const float*, const int32_t*, int64_t, int64_t, float*, cudaStream_t);
-int launch_combine(int, int, const void*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
+int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
 int launch_sorted_weights(const float*, const int32_t*, int64_t, float*, cudaStream_t);
 int launch_copy_row_segments(const void*, void*, const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t,
                              int64_t, cudaStream_t);
@@ -30,7 +30,7 @@ int launch_grouped_gemm_f32(int, const float*, const float*, const float*, const
                             int64_t, const float*, float*, cudaStream_t);
 int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int32_t*, int64_t, int64_t, int64_t,
                            int64_t, const float*, void*, cudaStream_t, const int32_t* row_rank = nullptr,
-                           const int32_t* row_pos = nullptr, void* const* peer_out = nullptr, int n_peers = 0);
+                           const int32_t* row_pos = nullptr, float* const* peer_out = nullptr, int n_peers = 0);
 int check_tc_shapes(int64_t, int64_t, int64_t, int64_t);
 bool decode_path_ok(int, int64_t, int64_t, int64_t, int64_t, int64_t);
 size_t decode_workspace_size(int64_t, int64_t, int64_t, int64_t, int64_t);
@@ -136,7 +136,7 @@ struct MoeWs {
   float* wsorted;
   void* xs;
   void* hs;
-  void* ds;  // fp32 (fp32 path) or bf16 (bf16 path)
+  float* ds;
   float* logits;
   void* perm_ws;
   size_t perm_bytes;
@@ -157,7 +157,7 @@ static size_t moe_layout(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, 
   l.wsorted = c.take<float>(n);
   l.xs = c.take<char>(n * H * esz);
   l.hs = c.take<char>(n * F * esz);
-  l.ds = c.take<char>(n * H * esz);
+  l.ds = c.take<float>(n * H);
   l.logits = c.take<float>(router_scratch_bytes(dtype, T, H, E) / sizeof(float) + 1);
   l.perm_bytes = permute_workspace_size(n, E);
   l.perm_ws = c.take<char>(l.perm_bytes);
@@ -348,7 +348,7 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
     prof_mark(4, st);
     // 5. d = down(h) * w                             :158-177
     FRANK_TRY(launch_grouped_gemm_f32(1, (const float*)L.hs, (const float*)w_down_p, nullptr, L.offsets, E, n, H, F,
-                                      L.wsorted, (float*)L.ds, st));
+                                      L.wsorted, L.ds, st));
   } else {
     FRANK_TRY(launch_tc_grouped_gemm(0, L.xs, w_gate_p, w_up_p, L.offsets, E, n, F, H, nullptr, L.hs, st));
     prof_mark(4, st);
@@ -356,7 +356,7 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
   }
   prof_mark(5, st);
   // 6. y[t] = sum_j d[slot j of t]                   :179-206
-  FRANK_TRY(launch_combine(y_dtype, dtype, L.ds, L.slot_pos, T, k, H, y, st));
+  FRANK_TRY(launch_combine(y_dtype, L.ds, L.slot_pos, T, k, H, y, st));
   prof_mark(6, st);
   return FRANK_OK;
 }
@@ -378,7 +378,7 @@ size_t frank_expert_ffn_workspace_size(int dtype, int64_t rows, int64_t F) {
 }
 
 int frank_expert_ffn(int dtype, const void* xs, const float* w_rows, const int32_t* offsets, int64_t E, int64_t rows,
-                     int64_t H, int64_t F, const void* w_up_p, const void* w_gate_p, const void* w_down_p, void* d,
+                     int64_t H, int64_t F, const void* w_up_p, const void* w_gate_p, const void* w_down_p, float* d,
                      void* workspace, size_t ws_bytes, void* stream) {
   FRANK_TRY(check_dtype(dtype, "expert_ffn"));
   FRANK_CHECK_ARG(E >= 1 && rows >= 0 && H >= 1 && F >= 1, "expert_ffn: bad shape");
@@ -392,7 +392,7 @@ int frank_expert_ffn(int dtype, const void* xs, const float* w_rows, const int32
     FRANK_TRY(launch_grouped_gemm_f32(2, (const float*)xs, (const float*)w_gate_p, (const float*)w_up_p, offsets, E,
                                       rows, F, H, nullptr, (float*)workspace, st));
     return launch_grouped_gemm_f32(1, (const float*)workspace, (const float*)w_down_p, nullptr, offsets, E, rows, H,
-                                   F, w_rows, (float*)d, st);
+                                   F, w_rows, d, st);
   }
   FRANK_TRY(check_tc_shapes(rows, F, H, E));
   FRANK_TRY(check_tc_shapes(rows, H, F, E));
@@ -417,15 +417,14 @@ int frank_expert_ffn_scatter(const void* xs, const float* w_rows, const int32_t*
   FRANK_TRY(check_tc_shapes(rows, H, F, E));
   FRANK_TRY(launch_tc_grouped_gemm(0, xs, w_gate_p, w_up_p, offsets, E, rows, F, H, nullptr, workspace, st));
   return launch_tc_grouped_gemm(1, workspace, w_down_p, nullptr, offsets, E, rows, H, F, w_rows, nullptr, st,
-                                row_rank, row_pos, peer_out, n_peers);
+                                row_rank, row_pos, reinterpret_cast<float* const*>(peer_out), n_peers);
 }
 
-int frank_combine(int d_dtype, const void* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H, int y_dtype,
-                  void* y, void* stream) {
+int frank_combine(const float* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H, int y_dtype, void* y,
+                  void* stream) {
   FRANK_TRY(check_dtype(y_dtype, "combine"));
-  FRANK_TRY(check_dtype(d_dtype, "combine"));
   FRANK_CHECK_ARG(T >= 0 && k >= 1 && H >= 1, "combine: bad shape");
-  return launch_combine(y_dtype, d_dtype, d, slot_pos, T, k, H, y, as_stream(stream));
+  return launch_combine(y_dtype, d, slot_pos, T, k, H, y, as_stream(stream));
 }
 
 int frank_copy_row_segments(const void* src, void* dst, const int64_t* src_start, const int64_t* dst_start,

@@ -25,9 +25,8 @@
 //   SWIGLU: B tile = 128 gate rows + 128 up rows of the same n range; the
 //           epilogue writes h = gate * silu(up) as bf16 [rows, N]
 //           (swiglu.mlir:37-47, silu on `up`).
-//   SCALE : 256 output columns scaled by the row's gate weight, bf16 out
-//           (moe_ffn_block.mlir:162-177); optionally each row is stored into
-//           another GPU's buffer through a row map (expert parallelism).
+//   SCALE : 256 output columns scaled by the row's gate weight, fp32 out
+//           (moe_ffn_block.mlir:162-177).
 //   PLAIN : 256 output columns, fp32 out (mul_mat_id).
 // Every mbarrier wait is bounded (about 2 s); on expiry the CTA records
 // FRANK_ETIMEOUT in the device error word and unwinds, freeing its TMEM.
@@ -65,7 +64,7 @@ struct Params {
   // (another GPU's buffer reached over NVLink) instead of out + r * ldo.
   const int32_t* row_rank;
   const int32_t* row_pos;
-  __nv_bfloat16* peer_out[kMaxPeers];
+  float* peer_out[kMaxPeers];
 };
 
 // ------------------------------------------------------------ PTX glue --
@@ -293,30 +292,11 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
             dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
           }
         }
-      } else if (MODE == SCALE) {
-        // d = acc * gate weight, stored as bf16 (the combine sums the k rows
-        // of a token in fp32)
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
-        if (p.row_rank != nullptr && valid) out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
-        const float s = valid ? p.wrow[row] : 1.f;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          float v[16];
-          tmem_ld16(taddr + c, v);
-          tmem_wait_ld();
-          const int col = tl.n * BN + c;
-          if (valid && col < p.N_out) {
-            uint32_t pk[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) pk[i] = pack_bf16x2(v[2 * i] * s, v[2 * i + 1] * s);
-            uint4* dst = reinterpret_cast<uint4*>(out + col);
-            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-          }
-        }
       } else {
         float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
-        const float s = 1.f;
+        if (MODE == SCALE && p.row_rank != nullptr && valid)
+          out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
+        const float s = (MODE == SCALE && valid) ? p.wrow[row] : 1.f;
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
           float v[16];
@@ -429,11 +409,11 @@ int check_tc_shapes(int64_t rows, int64_t N, int64_t K, int64_t E) {
   return FRANK_OK;
 }
 
-// mode: 0 SWIGLU (B = gate, B2 = up, out bf16 [rows, N]), 1 SCALE (out bf16
-// [rows, N]), 2 PLAIN (out fp32 [rows, N]).  A: bf16 [rows, K]; B/B2: bf16 [E, N, K].
+// mode: 0 SWIGLU (B = gate, B2 = up, out bf16 [rows, N]), 1 SCALE, 2 PLAIN
+// (out fp32 [rows, N]).  A: bf16 [rows, K]; B/B2: bf16 [E, N, K].
 int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B2, const int32_t* offsets, int64_t E,
                            int64_t rows, int64_t N, int64_t K, const float* wrow, void* out, cudaStream_t st,
-                           const int32_t* row_rank, const int32_t* row_pos, void* const* peer_out, int n_peers) {
+                           const int32_t* row_rank, const int32_t* row_pos, float* const* peer_out, int n_peers) {
   if (rows == 0) return FRANK_OK;
   FRANK_TRY(check_tc_shapes(rows, N, K, E));
   if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)(B2 ? B2 : B) | (uintptr_t)out) % 16 != 0) {
@@ -457,8 +437,7 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
   p.err = device_error_word();
   p.row_rank = row_rank;
   p.row_pos = row_pos;
-  for (int i = 0; i < kMaxPeers; ++i)
-    p.peer_out[i] = (peer_out && i < n_peers) ? static_cast<__nv_bfloat16*>(peer_out[i]) : nullptr;
+  for (int i = 0; i < kMaxPeers; ++i) p.peer_out[i] = (peer_out && i < n_peers) ? peer_out[i] : nullptr;
   if (row_rank && (mode != SCALE || !row_pos || !peer_out || n_peers < 1 || n_peers > kMaxPeers)) {
     set_error("tc_grouped_gemm: a row map needs SCALE mode, row_pos and 1..%d peer buffers", kMaxPeers);
     return FRANK_EINVAL;

@@ -416,7 +416,7 @@ static int launch_router_vec(const void* x, const void* wr, int64_t T, int64_t H
 }
 
 int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int32_t*, int64_t, int64_t, int64_t,
-                           int64_t, const float*, void*, cudaStream_t, const int32_t*, const int32_t*, void* const*,
+                           int64_t, const float*, void*, cudaStream_t, const int32_t*, const int32_t*, float* const*,
                            int);
 
 static bool router_tc_ok(int x_dtype, int64_t T, int64_t H, int64_t E) {

@@ -53,7 +53,7 @@ SIGNATURES = {
     "frank_expert_ffn_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64]),
     "frank_expert_ffn": (_c_int, [_c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp,
                                   _c_vp, _c_vp, _c_size, _c_vp]),
-    "frank_combine": (_c_int, [_c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
+    "frank_combine": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
     "frank_copy_row_segments": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),
     "frank_ep_plan": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp]),
     "frank_ep_dispatch": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp,

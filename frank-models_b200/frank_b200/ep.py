@@ -13,7 +13,7 @@ tokens; a step is
  4. grouped NCCL send/recv of the bf16 token rows and their gate weights,
     one chunk per (peer, local expert), each received straight into its
     expert-major position, then the local experts' grouped GEMMs
- 5. the output rows (compute dtype) go back chunk for chunk (NCCL send/recv) into the
+ 5. the fp32 output rows go back chunk for chunk (NCCL send/recv) into the
     sender's expert-sorted order
  6. combine the k rows of every local token in slot order (local kernel)
 
@@ -221,7 +221,7 @@ class ExpertParallelMoE:
         """Symmetric receive / return buffers sized for T tokens per rank (every
         rank calls with the same T; the dispatch kernel refuses rows beyond the
         capacity):
-        recv_x [P*k*T, H] bf16, recv_w [P*k*T] fp32, ret [k*T, H] bf16, and the
+        recv_x [P*k*T, H] bf16, recv_w [P*k*T] fp32, ret [k*T, H] fp32, and the
         peer addresses of every rank's copy.  Allocated collectively."""
         if self._symm is not None and self._symm["T"] >= T:
             return self._symm
@@ -237,7 +237,7 @@ class ExpertParallelMoE:
         def al(b):
             return (b + 255) // 256 * 256
 
-        sizes = [al(cap * H * 2), al(cap * 4), al(n * H * 2)]
+        sizes = [al(cap * H * 2), al(cap * 4), al(n * H * 4)]
         base = [0, sizes[0], sizes[0] + sizes[1]]
         self._symm = None
         torch.cuda.synchronize()
@@ -252,7 +252,7 @@ class ExpertParallelMoE:
             "T": T, "buf": buf, "hdl": hdl, "cap": cap,
             "recv_x": buf[base[0]:base[0] + cap * H * 2].view(torch.bfloat16).view(cap, H),
             "recv_w": buf[base[1]:base[1] + cap * 4].view(torch.float32),
-            "ret": buf[base[2]:base[2] + n * H * 2].view(torch.bfloat16).view(n, H),
+            "ret": buf[base[2]:base[2] + n * H * 4].view(torch.float32).view(n, H),
             "peer_x": arr([q + base[0] for q in ptrs]),
             "peer_w": arr([q + base[1] for q in ptrs]),
             "peer_ret": arr([q + base[2] for q in ptrs]),
@@ -343,13 +343,13 @@ class ExpertParallelMoE:
         self._mark()
         self._exchange(xs, xl, send_chunks, recv_chunks)
         self._exchange(ws, wl, send_chunks, recv_chunks)
-        dl = torch.empty((R, H), dtype=xs.dtype, device=dev)
+        dl = torch.empty((R, H), dtype=torch.float32, device=dev)
         offs = torch.from_numpy(local_off.astype(np.int32)).to(dev, non_blocking=True)
         self._mark()
         if R:
             pr.expert_ffn(xl, wl, offs, self.w_up, self.w_gate, self.w_down, dl)
         # results go back chunk for chunk into this rank's expert-sorted order
-        ret = torch.empty((n, H), dtype=dl.dtype, device=dev)
+        ret = torch.empty((n, H), dtype=torch.float32, device=dev)
         self._mark()
         self._exchange(dl, ret, recv_chunks, send_chunks)
         self._mark()

@@ -358,11 +358,11 @@ def gather_weights(w: torch.Tensor, sorted_slots: torch.Tensor) -> torch.Tensor:
 def expert_ffn(xs: torch.Tensor, w_rows: torch.Tensor, offsets: torch.Tensor, w_up_p: torch.Tensor,
                w_gate_p: torch.Tensor, w_down_p: torch.Tensor, out: torch.Tensor | None = None,
                workspace: torch.Tensor | None = None) -> torch.Tensor:
-    """Grouped gate/up + swiglu + down x row weight over expert-sorted rows -> [rows, H] in xs's dtype."""
+    """Grouped gate/up + swiglu + down x row weight over expert-sorted rows -> fp32 [rows, H]."""
     rows, H = xs.shape
     E, F, _ = w_up_p.shape
     lib = _lib.load()
-    d = out if out is not None else torch.empty((rows, H), dtype=xs.dtype, device=xs.device)
+    d = out if out is not None else torch.empty((rows, H), dtype=torch.float32, device=xs.device)
     need = lib.frank_expert_ffn_workspace_size(_dt(xs), rows, F)
     if workspace is None or workspace.numel() < need:
         workspace = torch.empty(max(need, 1), dtype=torch.uint8, device=xs.device)
@@ -375,7 +375,7 @@ def expert_ffn(xs: torch.Tensor, w_rows: torch.Tensor, offsets: torch.Tensor, w_
 def combine(d: torch.Tensor, slot_pos: torch.Tensor, T: int, k: int, out: torch.Tensor) -> torch.Tensor:
     """y[t] = sum_j d[slot_pos[j*T + t]] (j in order)."""
     H = d.shape[1]
-    _lib.check(_lib.load().frank_combine(_dt(d), _ptr(d), _ptr(slot_pos), T, k, H, _dt(out), _ptr(out), _stream()))
+    _lib.check(_lib.load().frank_combine(_ptr(d), _ptr(slot_pos), T, k, H, _dt(out), _ptr(out), _stream()))
     return out
 
 

@@ -191,12 +191,10 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr,
  * frank_gather_weights: w_sorted[r] = w[sorted_slots[r]].
  * frank_expert_ffn: for expert-sorted rows xs [rows, H] with expert row
  *   offsets [E+1] and per-row gate weights: d = (gate(xs) * silu(up(xs)))
- *   @ down^T * w_rows, [rows, H] in the compute dtype: fp32 for FRANK_F32,
- *   bf16 for FRANK_BF16 (moe_ffn_block.mlir:146-177).
+ *   @ down^T * w_rows, fp32 [rows, H] (moe_ffn_block.mlir:146-177).
  *   Workspace: frank_expert_ffn_workspace_size(dtype, rows, F).
- * frank_combine: y[t] = sum_{j<k} d[slot_pos[j*T + t]] in order j, fp32
- *   sums (moe_ffn_block.mlir:179-206); d_dtype / y_dtype FRANK_F32 or
- *   FRANK_BF16.
+ * frank_combine: y[t] = sum_{j<k} d[slot_pos[j*T + t]] in order j
+ *   (moe_ffn_block.mlir:179-206); y_dtype FRANK_F32 or FRANK_BF16.
  * frank_copy_row_segments: dst rows [dst_start[s], +len) = src rows
  *   [src_start[s], +len) for nseg segments; seg_prefix [nseg+1] is the
  *   exclusive prefix of the lengths (device int64 arrays); row_bytes % 4 == 0.
@@ -210,11 +208,10 @@ size_t frank_expert_ffn_workspace_size(int dtype, int64_t rows, int64_t F);
 int frank_expert_ffn(int dtype, const void* xs, const float* w_rows,
                      const int32_t* offsets, int64_t E, int64_t rows,
                      int64_t H, int64_t F, const void* w_up_p,
-                     const void* w_gate_p, const void* w_down_p, void* d,
+                     const void* w_gate_p, const void* w_down_p, float* d,
                      void* workspace, size_t ws_bytes, void* stream);
-int frank_combine(int d_dtype, const void* d, const int32_t* slot_pos,
-                  int64_t T, int64_t k, int64_t H, int y_dtype, void* y,
-                  void* stream);
+int frank_combine(const float* d, const int32_t* slot_pos, int64_t T,
+                  int64_t k, int64_t H, int y_dtype, void* y, void* stream);
 int frank_copy_row_segments(const void* src, void* dst,
                             const int64_t* src_start, const int64_t* dst_start,
                             const int64_t* seg_prefix, int64_t nseg,
@@ -238,7 +235,7 @@ int frank_copy_row_segments(const void* src, void* dst,
  *   buffers of `capacity` rows, P <= 8) at the planned rows.  A planned row
  *   outside [0, capacity) is skipped and FRANK_EINVAL is recorded in the
  *   device error word (frank_read_device_error).
- * frank_expert_ffn_scatter: frank_expert_ffn (bf16) whose bf16 output row r
+ * frank_expert_ffn_scatter: frank_expert_ffn (bf16) whose fp32 output row r
  *   is stored at peer_out[row_rank[r]] + row_pos[r] * H, i.e. straight into
  *   the return buffer of the rank the row came from.
  * Stores to other GPUs complete with the kernels; the caller orders the
