@@ -42,20 +42,6 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
   }
 }
 
-// Same as bf16x8_to_f32, but opaque to the optimiser so that the unpacking
-// stays next to its use (it must not be hoisted out of the per-row loops,
-// which would keep 64+ unpacked floats live per lane).
-__device__ __forceinline__ void bf16x8_unpack_here(uint4 u, float (&v)[8]) {
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    uint32_t lo, hi;
-    asm volatile("shl.b32 %0, %2, 16;\n\tand.b32 %1, %2, 0xffff0000;" : "=r"(lo), "=r"(hi) : "r"(w[i]));
-    v[2 * i] = __uint_as_float(lo);
-    v[2 * i + 1] = __uint_as_float(hi);
-  }
-}
-
 template <class TW>
 __device__ __forceinline__ void load8_w(const TW* p, float (&v)[8]);
 template <>
