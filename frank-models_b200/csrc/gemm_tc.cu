@@ -31,6 +31,7 @@
 // Every mbarrier wait is bounded (about 2 s); on expiry the CTA records
 // FRANK_ETIMEOUT in the device error word and unwinds, freeing its TMEM.
 #include <cuda.h>
+#include <cstdlib>
 #include <cudaTypedefs.h>
 
 #include "common.cuh"
@@ -129,7 +130,7 @@ struct Tile {
   int e, m0, m_end, n;
 };
 
-__device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int32_t* offsets, int E) {
+__device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int32_t* offsets, int E, int bm = BM) {
   int lo = 0, hi = E;  // find e: prefix[e] <= t < prefix[e+1]
   while (hi - lo > 1) {
     int mid = (lo + hi) >> 1;
@@ -137,14 +138,58 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int3
   }
   const int e = lo;
   const int r0 = offsets[e], r1 = offsets[e + 1];
-  const int mt = (r1 - r0 + BM - 1) / BM;
+  const int mt = (r1 - r0 + bm - 1) / bm;
   const int local = t - prefix[e];
   Tile tl;
   tl.e = e;
-  tl.m0 = r0 + (local % mt) * BM;
+  tl.m0 = r0 + (local % mt) * bm;
   tl.m_end = r1;
   tl.n = local / mt;
   return tl;
+}
+
+// Epilogue of one accumulator tile for the 32 rows of one warp: thread
+// `lane` owns row `row`; taddr addresses this warp's TMEM lane quadrant.
+template <int MODE>
+__device__ __forceinline__ void epilogue_rows(const Params& p, int row, bool valid, int n, uint32_t taddr) {
+  if (MODE == SWIGLU) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
+#pragma unroll 1
+    for (int c = 0; c < 128; c += 16) {
+      float g[16], u[16];
+      tmem_ld16(taddr + c, g);
+      tmem_ld16(taddr + 128 + c, u);
+      tmem_wait_ld();
+      const int col = n * 128 + c;
+      if (valid && col < p.N_out) {
+        uint32_t pk[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          pk[i] = pack_bf16x2(g[2 * i] * silu_ref(u[2 * i]), g[2 * i + 1] * silu_ref(u[2 * i + 1]));
+        uint4* dst = reinterpret_cast<uint4*>(out + col);
+        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+      }
+    }
+  } else {
+    float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+    if (MODE == SCALE && p.row_rank != nullptr && valid)
+      out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
+    const float s = (MODE == SCALE && valid) ? p.wrow[row] : 1.f;
+#pragma unroll 1
+    for (int c = 0; c < BN; c += 16) {
+      float v[16];
+      tmem_ld16(taddr + c, v);
+      tmem_wait_ld();
+      const int col = n * BN + c;
+      if (valid && col < p.N_out) {
+        float4* dst = reinterpret_cast<float4*>(out + col);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          dst[i] = make_float4(v[4 * i] * s, v[4 * i + 1] * s, v[4 * i + 2] * s, v[4 * i + 3] * s);
+      }
+    }
+  }
 }
 
 template <int MODE>
@@ -271,46 +316,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = tl.m0 + q * 32 + lane;
-      const bool valid = row < tl.m_end;
-      const uint32_t taddr = tmem_base + a * BN + ((uint32_t)(q * 32) << 16);
-      if (MODE == SWIGLU) {
-        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
-#pragma unroll 1
-        for (int c = 0; c < 128; c += 16) {
-          float g[16], u[16];
-          tmem_ld16(taddr + c, g);
-          tmem_ld16(taddr + 128 + c, u);
-          tmem_wait_ld();
-          const int col = tl.n * 128 + c;
-          if (valid && col < p.N_out) {
-            uint32_t pk[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              pk[i] = pack_bf16x2(g[2 * i] * silu_ref(u[2 * i]), g[2 * i + 1] * silu_ref(u[2 * i + 1]));
-            uint4* dst = reinterpret_cast<uint4*>(out + col);
-            dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-            dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
-          }
-        }
-      } else {
-        float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
-        if (MODE == SCALE && p.row_rank != nullptr && valid)
-          out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
-        const float s = (MODE == SCALE && valid) ? p.wrow[row] : 1.f;
-#pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          float v[16];
-          tmem_ld16(taddr + c, v);
-          tmem_wait_ld();
-          const int col = tl.n * BN + c;
-          if (valid && col < p.N_out) {
-            float4* dst = reinterpret_cast<float4*>(out + col);
-#pragma unroll
-            for (int i = 0; i < 4; ++i)
-              dst[i] = make_float4(v[4 * i] * s, v[4 * i + 1] * s, v[4 * i + 2] * s, v[4 * i + 3] * s);
-          }
-        }
-      }
+      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(a));
@@ -325,6 +331,216 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------- CTA-pair (2-SM) form --
+// Same grouped GEMM with tcgen05.mma.cta_group::2: a cluster of two CTAs on
+// two SMs computes a 256-row x 256-column tile.  Each CTA loads its own
+// 128 rows of A and its half of B (128 rows: for SWIGLU the gate rows in
+// CTA 0 and the up rows in CTA 1), so per SM the shared-memory operand traffic
+// per MMA drops from 48 KB to 32 KB per 64-wide K step.  CTA 0 (the leader)
+// issues the MMAs; each CTA's TMEM holds the accumulator rows of its 128 A
+// rows, and both run the same epilogue on their rows.  TMA loads of both CTAs
+// signal the leader's full barrier (.cta_group::2 form, no multicast);
+// tcgen05.commit multicasts stage-free and accumulator-ready arrivals to both
+// CTAs; the peer's epilogue warps arrive on the leader's accumulator-free
+// barrier through its cluster address.
+constexpr int BM2 = 256;
+constexpr int STAGES2 = 6;
+constexpr uint32_t STAGE2_BYTES = A_BYTES + B_HALF_BYTES;  // 32 KiB per CTA
+constexpr uint32_t kIdesc2 =
+    (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM2 >> 4) << 24);
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                                 uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, "
+      "%4}], [%5];" ::"r"(dst),
+      "l"(map), "r"(x), "r"(y), "r"(z), "r"(bar)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(kIdesc2), "r"(accumulate)
+      : "memory");
+}
+
+// arrive on the barrier at this shared offset in both CTAs of the pair
+__device__ __forceinline__ void mma_commit_pair(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(bar),
+      "h"((uint16_t)3)
+      : "memory");
+}
+
+template <int MODE>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                        const __grid_constant__ CUtensorMap tmB2, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* prefix = reinterpret_cast<int*>(tmem_slot + 4);  // [E+1]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (STAGES2 + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * STAGES2 + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * STAGES2 + 2 + a); };
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    int carry = 0;
+    for (int base = 0; base < p.E; base += 32) {
+      int e = base + lane;
+      int v = 0;
+      if (e < p.E) v = ((p.offsets[e + 1] - p.offsets[e] + BM2 - 1) / BM2) * p.n_tiles;
+      int incl = v;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        int u = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += u;
+      }
+      if (e < p.E) prefix[e] = carry + incl - v;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) prefix[p.E] = carry;
+  } else if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the peer's barriers are initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int total = prefix[p.E];
+  const int nk = (p.K + BK - 1) / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------- TMA producer (both CTAs) --
+      uint32_t it = 0;
+      bool ok = true;
+      for (int t = cid; t < total && ok; t += ncl) {
+        Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM2);
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1u;
+          if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
+          uint8_t* st = smem + s * STAGE2_BYTES;
+          if (leader) mbar_expect_tx(full_bar(s), 2 * STAGE2_BYTES);
+          const uint32_t fb = mapa_shared(full_bar(s), 0);
+          tma_load_2d_pair(smem_u32(st), &tmA, kb * BK, tl.m0 + (int)rank * 128, fb);
+          if (MODE == SWIGLU)
+            tma_load_3d_pair(smem_u32(st + A_BYTES), rank == 0 ? &tmB : &tmB2, kb * BK, tl.n * 128, tl.e, fb);
+          else
+            tma_load_3d_pair(smem_u32(st + A_BYTES), &tmB, kb * BK, tl.n * BN + (int)rank * 128, tl.e, fb);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // -------------------------------------------- MMA issuer (leader) --
+      uint32_t it = 0, tc = 0;
+      bool ok = true;
+      for (int t = cid; t < total && ok; t += ncl, ++tc) {
+        const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
+        if (!mbar_wait(tempty_bar(a), aph ^ 1u, abort_flag, p.err)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + a * BN;
+        for (int kb = 0; kb < nk; ++kb, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1u;
+          if (!mbar_wait(full_bar(s), ph, abort_flag, p.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(smem + s * STAGE2_BYTES);
+          const uint64_t adesc = make_sw128_desc(sa);
+          const uint64_t bdesc = make_sw128_desc(sa + A_BYTES);
+#pragma unroll
+          for (int j = 0; j < BK / 16; ++j)
+            mma_bf16_pair(d, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), (kb | j) != 0);
+          mma_commit_pair(empty_bar(s));
+        }
+        if (ok) mma_commit_pair(tfull_bar(a));
+      }
+    }
+  } else {
+    // ------------------------------------------- epilogue (both CTAs) --
+    const int q = warp & 3;
+    uint32_t tc = 0;
+    for (int t = cid; t < total; t += ncl, ++tc) {
+      Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM2);
+      const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
+      if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
+      tc_fence_after();
+      const int row = tl.m0 + (int)rank * 128 + q * 32 + lane;
+      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16));
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(a), 0));
+    }
+    if (MODE == SCALE && p.row_rank != nullptr) __threadfence_system();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // the leader's MMAs read the peer's shared memory until here
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
   }
 }
 
@@ -385,6 +601,19 @@ int make_map_3d(CUtensorMap* m, const void* base, int64_t E, int64_t N, int64_t 
 }
 
 size_t smem_bytes(int E) { return 1024 + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 4) + 16 + 4 * (E + 1) + 64; }
+size_t smem2_bytes(int E) { return 1024 + STAGES2 * STAGE2_BYTES + 8 * (2 * STAGES2 + 4) + 16 + 4 * (E + 1) + 64; }
+
+// CTA pairs pay off when experts have enough rows to fill 256-row tiles.
+// FRANK_TC_PAIR=0 / 1 forces the single-CTA / pair form (measurement aid).
+bool use_cta_pair(int64_t rows, int64_t E) {
+  static int force = -2;
+  if (force == -2) {
+    const char* v = getenv("FRANK_TC_PAIR");
+    force = v ? atoi(v) : -1;
+  }
+  if (force == 0 || force == 1) return force == 1 && frank::num_sms() >= 2;
+  return rows >= 512 * E && frank::num_sms() >= 2;
+}
 
 }  // namespace
 
@@ -441,6 +670,22 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
   if (row_rank && (mode != SCALE || !row_pos || !peer_out || n_peers < 1 || n_peers > kMaxPeers)) {
     set_error("tc_grouped_gemm: a row map needs SCALE mode, row_pos and 1..%d peer buffers", kMaxPeers);
     return FRANK_EINVAL;
+  }
+  if (use_cta_pair(rows, E)) {
+    size_t smem2 = smem2_bytes((int)E);
+    dim3 grid2(num_sms() & ~1), block2(THREADS);
+#define FRANK_TC2_CASE(M)                                                                                      \
+  FRANK_CUDA_TRY(                                                                                              \
+      cudaFuncSetAttribute(tc2_grouped_gemm_kernel<M>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2)); \
+  tc2_grouped_gemm_kernel<M><<<grid2, block2, smem2, st>>>(ma, mb, mb2, p);
+    switch (mode) {
+      case SWIGLU: FRANK_TC2_CASE(SWIGLU) break;
+      case SCALE: FRANK_TC2_CASE(SCALE) break;
+      default: FRANK_TC2_CASE(PLAIN)
+    }
+#undef FRANK_TC2_CASE
+    FRANK_LAUNCH_CHECK();
+    return FRANK_OK;
   }
   size_t smem = smem_bytes((int)E);
   dim3 grid(num_sms()), block(THREADS);
