@@ -270,6 +270,55 @@ class MoEFFNBlock:
         return y
 
 
+def moe_ffn_host(block, x_host: torch.Tensor, y_host: torch.Tensor, chunks: int = 4,
+                 x_dev: torch.Tensor | None = None, y_dev: torch.Tensor | None = None) -> torch.Tensor:
+    """Run ``block`` (a :class:`MoEFFNBlock`, or any callable ``block(x, out=y)``
+    over token rows) on host-resident tokens: x_host [T, H] -> y_host [T, H]
+    (pinned host tensors).  The tokens are split into ``chunks`` pieces that
+    flow through three streams -- host-to-device copy, the block on the
+    current stream, device-to-host copy -- so the PCIe transfers of one chunk
+    overlap the compute of its neighbours.  Tokens are independent in the
+    block, so the result equals one call on all T tokens bit for bit.  Returns
+    y_host once the current stream has been ordered after the last copy
+    (no host synchronisation).  x_dev / y_dev: optional device staging buffers
+    of the full size (allocated when absent)."""
+    T, H = x_host.shape
+    if not (x_host.is_pinned() and y_host.is_pinned()):
+        raise ValueError("moe_ffn_host: x_host and y_host must be pinned host tensors")
+    dev = torch.device("cuda", torch.cuda.current_device())
+    x_dev = x_dev if x_dev is not None else torch.empty((T, H), dtype=x_host.dtype, device=dev)
+    y_dev = y_dev if y_dev is not None else torch.empty((T, H), dtype=y_host.dtype, device=dev)
+    chunks = max(1, min(int(chunks), T))
+    bounds = [T * i // chunks for i in range(chunks + 1)]
+    compute = torch.cuda.current_stream(dev)
+    s_in, s_out = _host_streams(dev)
+    s_in.wait_stream(compute)
+    s_out.wait_stream(compute)
+    for i in range(chunks):
+        a, b = bounds[i], bounds[i + 1]
+        if a == b:
+            continue
+        with torch.cuda.stream(s_in):
+            x_dev[a:b].copy_(x_host[a:b], non_blocking=True)
+        compute.wait_stream(s_in)
+        block(x_dev[a:b], out=y_dev[a:b])
+        s_out.wait_stream(compute)
+        with torch.cuda.stream(s_out):
+            y_host[a:b].copy_(y_dev[a:b], non_blocking=True)
+    compute.wait_stream(s_out)
+    return y_host
+
+
+_HOST_STREAMS: dict = {}
+
+
+def _host_streams(dev):
+    key = dev.index
+    if key not in _HOST_STREAMS:
+        _HOST_STREAMS[key] = (torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev))
+    return _HOST_STREAMS[key]
+
+
 class GraphedMoEFFN:
     """A :class:`MoEFFNBlock` call for a fixed token count captured once in a
     CUDA graph (the small, launch-bound decode steps).  ``x`` and ``y`` are the

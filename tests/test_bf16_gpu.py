@@ -124,3 +124,20 @@ def test_mixtral_full_size_token_subset():
     err = (got - ref).abs().max().item() / ref.pow(2).mean().sqrt().item()
     assert err <= BLOCK_TOL
     assert ops.read_device_error() == 0
+
+
+def test_host_pipeline_equals_device_call():
+    """ops.moe_ffn_host (chunked copies overlapping compute) returns exactly the
+    single device call's output."""
+    cfg = configs.BlockConfig("host_pipe", T=1000, H=512, F=256, E=16, k=4, normalize=True, dtype="bf16")
+    x, wr, wu, wg, wd = configs.block_inputs_numpy(cfg, seed=4)
+    block = ops.MoEFFNBlock(torch.from_numpy(wr).cuda(), *(_bf16(w) for w in (wu, wg, wd)), cfg.E, cfg.k, True)
+    xb = _bf16(x)
+    ref = block(xb)
+    x_host = xb.cpu().pin_memory()
+    y_host = torch.empty((cfg.T, cfg.H), dtype=torch.float32).pin_memory()
+    for chunks in (1, 3, 7):
+        y_host.zero_()
+        ops.moe_ffn_host(block, x_host, y_host, chunks=chunks)
+        torch.cuda.synchronize()
+        assert torch.equal(y_host, ref.cpu())
