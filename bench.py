@@ -328,22 +328,26 @@ def run_frank(args, cfg):
     y_host = torch.empty((cfg.T, cfg.H), dtype=torch.float32).pin_memory()
     x_dev = torch.empty_like(x)
 
-    def e2e_step():
+    def e2e_step(last):
         if graphed is not None or cfg.T < 1024:
             # decode: one copy each way around the (graph-replayed) block
             x_dev.copy_(x_host, non_blocking=True)
             e2e_call(x_dev, out=y)
             y_host.copy_(y, non_blocking=True)
         else:
-            # public host-buffer API: chunked H2D / block / D2H on three streams
-            ops.moe_ffn_host(e2e_call, x_host, y_host, chunks=4, x_dev=x_dev, y_dev=y)
+            # public host-buffer API: chunked H2D / block / D2H on three streams;
+            # a step's copies out overlap the next step, the last is waited for
+            done = ops.moe_ffn_host(e2e_call, x_host, y_host, chunks=4, x_dev=x_dev, y_dev=y,
+                                    order_copy_out=False)
+            if last:
+                stream.wait_event(done)
 
-    for _ in range(min(args.warmup, 2)):
-        e2e_step()
+    for i in range(min(args.warmup, 2)):
+        e2e_step(True)
     barrier()
     ev0.record(stream)
-    for _ in range(args.steps):
-        e2e_step()
+    for i in range(args.steps):
+        e2e_step(i == args.steps - 1)
     ev1.record(stream)
     barrier()
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps

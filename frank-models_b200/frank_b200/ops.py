@@ -271,17 +271,21 @@ class MoEFFNBlock:
 
 
 def moe_ffn_host(block, x_host: torch.Tensor, y_host: torch.Tensor, chunks: int = 4,
-                 x_dev: torch.Tensor | None = None, y_dev: torch.Tensor | None = None) -> torch.Tensor:
+                 x_dev: torch.Tensor | None = None, y_dev: torch.Tensor | None = None,
+                 order_copy_out: bool = True):
     """Run ``block`` (a :class:`MoEFFNBlock`, or any callable ``block(x, out=y)``
     over token rows) on host-resident tokens: x_host [T, H] -> y_host [T, H]
     (pinned host tensors).  The tokens are split into ``chunks`` pieces that
     flow through three streams -- host-to-device copy, the block on the
     current stream, device-to-host copy -- so the PCIe transfers of one chunk
     overlap the compute of its neighbours.  Tokens are independent in the
-    block, so the result equals one call on all T tokens bit for bit.  Returns
-    y_host once the current stream has been ordered after the last copy
-    (no host synchronisation).  x_dev / y_dev: optional device staging buffers
-    of the full size (allocated when absent)."""
+    block, so the result equals one call on all T tokens bit for bit.
+    x_dev / y_dev: optional device staging buffers of the full size
+    (allocated when absent).  No host synchronisation.  Returns a CUDA event
+    that completes when y_host is written; with ``order_copy_out`` (default)
+    the current stream is also ordered after it.  Without, the copies out of
+    this call overlap whatever the caller enqueues next (e.g. the next call),
+    and the caller waits on the event before reading y_host."""
     T, H = x_host.shape
     if not (x_host.is_pinned() and y_host.is_pinned()):
         raise ValueError("moe_ffn_host: x_host and y_host must be pinned host tensors")
@@ -305,8 +309,11 @@ def moe_ffn_host(block, x_host: torch.Tensor, y_host: torch.Tensor, chunks: int 
         s_out.wait_stream(compute)
         with torch.cuda.stream(s_out):
             y_host[a:b].copy_(y_dev[a:b], non_blocking=True)
-    compute.wait_stream(s_out)
-    return y_host
+    done = torch.cuda.Event()
+    done.record(s_out)
+    if order_copy_out:
+        compute.wait_event(done)
+    return done
 
 
 _HOST_STREAMS: dict = {}
