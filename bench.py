@@ -372,18 +372,21 @@ def run_frank(args, cfg):
     if flush is not None:
         line["config"]["l2"] = "L2 flushed (256 MiB write) before every timed step; steps timed individually"
     if stage_ms and cfg.T <= 64:
-        # decode: weight streaming, HBM-bound.  Algorithmic bytes of the gate/up
-        # GEMM = distinct experts x 2 matrices x F x H bf16 + rows read + h written.
-        rows = cfg.k * cfg.T
-        gu_bytes = n_distinct * 2 * cfg.F * cfg.H * 2 + rows * cfg.H * 2 + rows * cfg.F * 2
+        # decode: weight streaming, HBM-bound.  Algorithmic bytes of the block =
+        # distinct experts x 3 matrices x F x H bf16 + router + activations.
+        # Small decode blocks run as one fused kernel, so the roofline kernel
+        # is the whole block (the sum of the recorded stages).
         blk_bytes = (n_distinct * 3 * cfg.F * cfg.H * 2 + cfg.E * cfg.H * 4 + cfg.T * cfg.H * 2 + cfg.T * cfg.H * 4)
-        gu_ms = stage_ms["gate_up_gemm"]
-        achieved = gu_bytes / (gu_ms / 1e3) / 1e9
+        fused = cfg.k * cfg.T <= cfg.E
+        k_ms = sum(stage_ms.values()) if fused else stage_ms["gate_up_gemm"]
+        k_bytes = blk_bytes if fused else (n_distinct * 2 * cfg.F * cfg.H * 2 + cfg.k * cfg.T * (cfg.H + cfg.F) * 2)
+        achieved = k_bytes / (k_ms / 1e3) / 1e9
         peak = float(pk["hbm_gbs"])
         line["roofline"] = {
-            "kernel": "tc_grouped_gemm<SWIGLU> (gate/up GEMM + swiglu)", "bound": "hbm", "achieved": achieved,
-            "peak": peak, "unit": "GB/s", "frac": achieved / peak, "peak_source": f"{pk_kind} hbm_gbs",
-            "traffic": None, "bytes_per_launch": gu_bytes, "ms_per_launch": gu_ms, "distinct_experts": n_distinct,
+            "kernel": "decode_fused_kernel (whole block)" if fused else "tc_grouped_gemm<SWIGLU> (gate/up GEMM + swiglu)",
+            "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_source": f"{pk_kind} hbm_gbs", "traffic": None, "bytes_per_launch": k_bytes, "ms_per_launch": k_ms,
+            "distinct_experts": n_distinct,
         }
         line["stage_ms"] = stage_ms
         line["block_hbm_gbs"] = blk_bytes / (ms / 1e3) / 1e9

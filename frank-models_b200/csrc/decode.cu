@@ -19,6 +19,8 @@
 //   combine_kernel         y[t] = sum of the k slots of t in slot order
 //                          (moe_ffn_block.mlir:179-206), deterministic.
 // Consecutive kernels use programmatic dependent launch; no atomics.
+#include <cstdlib>
+
 #include "common.cuh"
 #include "mbarrier.cuh"
 #include "topk.cuh"
@@ -68,6 +70,7 @@ struct DecodeWs {
   int32_t* nactive;
   float* d;             // [k*T, H] down output x gate weight
   int32_t* err;         // device error word (bounded waits)
+  unsigned* gbar;       // grid-barrier counter of the fused kernel (zeroed per call)
 };
 
 // Programmatic dependent launch: a kernel's blocks may start while the
@@ -77,14 +80,11 @@ __device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol
 
 // ----------------------------------------------------------------- route --
 template <class TW>
-__global__ void __launch_bounds__(kThreads)
-decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr, int T, int H, int E, int k,
-                    int normalize, DecodeWs ws) {
-  asm volatile("griddepcontrol.launch_dependents;" :::);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+__device__ __forceinline__ void route_body(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr, int T,
+                                           int H, int E, const DecodeWs& ws, int gwarp, int nwarps) {
+  const int lane = threadIdx.x & 31;
   const int tchunks = (T + kRouteTok - 1) / kRouteTok;
-  const int item = blockIdx.x * kWarps + warp;
-  if (item < E * tchunks) {
+  for (int item = gwarp; item < E * tchunks; item += nwarps) {
     const int e = item / tchunks, t0 = (item - e * tchunks) * kRouteTok;
     float acc[kRouteTok];
 #pragma unroll
@@ -113,31 +113,40 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   }
 }
 
+template <class TW>
+__global__ void __launch_bounds__(kThreads)
+decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr, int T, int H, int E, int k,
+                    int normalize, DecodeWs ws) {
+  allow_next_grid();
+  route_body<TW>(x, wr, T, H, E, ws, blockIdx.x * kWarps + (threadIdx.x >> 5), gridDim.x * kWarps);
+}
+
 // One block: softmax + top-k + renorm for every token, the stable expert
 // permutation (same order as argsort(ids.reshape(-1), stable)) and the list of
 // active experts.
-__global__ void __launch_bounds__(kThreads)
-decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
-  wait_prior_grid();
-  allow_next_grid();
+// Shared scratch of finalize_body: lg [kWarps][kMaxE] f32, running [kMaxE+1],
+// warp_cnt [kWarps][kMaxE], rank [kMaxSlots] (int32).
+constexpr size_t kFinalizeSmem = sizeof(float) * kWarps * kMaxE + sizeof(int32_t) * (kMaxE + 1 + kWarps * kMaxE + kMaxSlots);
+
+__device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch) {
+  float* lg = reinterpret_cast<float*>(scratch);
+  int32_t* running = reinterpret_cast<int32_t*>(lg + kWarps * kMaxE);
+  int32_t* warp_cnt = running + kMaxE + 1;
+  int32_t* rank = warp_cnt + kWarps * kMaxE;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  __shared__ float lg[kWarps][kMaxE];
   for (int t = warp; t < T; t += kWarps) {
-    for (int e = lane; e < E; e += 32) lg[warp][e] = ws.logits[(int64_t)e * T + t];
+    for (int e = lane; e < E; e += 32) lg[warp * kMaxE + e] = __ldcg(ws.logits + (int64_t)e * T + t);
     __syncwarp();
-    warp_softmax_topk(lg[warp], E, k, normalize, ws.w, ws.ids, T, t);
+    warp_softmax_topk(lg + warp * kMaxE, E, k, normalize, ws.w, ws.ids, T, t);
     __syncwarp();
   }
   __syncthreads();
   // stable counting sort of the n = k*T flat slots by expert (same order as
   // argsort(ids.reshape(-1), stable)); one block, warp-level ranks
-  __shared__ int32_t running[kMaxE + 1];
-  __shared__ int32_t warp_cnt[kWarps][kMaxE];
-  __shared__ int32_t rank[kMaxSlots];
   const int n = k * T;
   for (int e = threadIdx.x; e < E; e += kThreads) {
     running[e] = 0;
-    for (int w2 = 0; w2 < kWarps; ++w2) warp_cnt[w2][e] = 0;
+    for (int w2 = 0; w2 < kWarps; ++w2) warp_cnt[w2 * kMaxE + e] = 0;
   }
   __syncthreads();
   for (int base = 0; base < n; base += kThreads) {
@@ -146,22 +155,22 @@ decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_w = __popc(peers & ((1u << lane) - 1u));
     const int leader = __ffs(peers) - 1;
-    if (e >= 0 && lane == leader) warp_cnt[warp][e] = __popc(peers);
+    if (e >= 0 && lane == leader) warp_cnt[warp * kMaxE + e] = __popc(peers);
     __syncthreads();
     int pos = 0;
     bool last = false;
     if (e >= 0) {
       int before = 0;
-      for (int w2 = 0; w2 < warp; ++w2) before += warp_cnt[w2][e];
+      for (int w2 = 0; w2 < warp; ++w2) before += warp_cnt[w2 * kMaxE + e];
       pos = running[e] + before + rank_w;
       rank[s] = pos;
       last = (lane == 31 - __clz(peers));
       for (int w2 = warp + 1; w2 < kWarps && last; ++w2)
-        if (warp_cnt[w2][e] != 0) last = false;
+        if (warp_cnt[w2 * kMaxE + e] != 0) last = false;
     }
     __syncthreads();
     if (last) running[e] = pos + 1;
-    if (e >= 0 && lane == leader) warp_cnt[warp][e] = 0;
+    if (e >= 0 && lane == leader) warp_cnt[warp * kMaxE + e] = 0;
     __syncthreads();
   }
   if (warp == 0) {  // exclusive scan of the counts and the active-expert list (E <= 256)
@@ -198,6 +207,14 @@ decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
   }
 }
 
+__global__ void __launch_bounds__(kThreads)
+decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
+  __shared__ __align__(16) uint8_t scratch[kFinalizeSmem];
+  wait_prior_grid();
+  allow_next_grid();
+  finalize_body(T, E, k, normalize, ws, scratch);
+}
+
 
 // ----------------------------------------------- weight-streaming GEMVs --
 // Both GEMV kernels stream contiguous chunks of an expert's weight rows from
@@ -217,16 +234,12 @@ struct StreamSmem {
 // gate/up: item = (active expert e, fr rows of F starting at f0): stage =
 // fr gate rows then fr up rows ([2][fr][H] bf16).  Warp w < fr computes row
 // f0 + w for each token row: h = gate . x * silu(up . x).
-__global__ void __launch_bounds__(kThreads)
-decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
+__device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int stages,
-                     DecodeWs ws) {
-  extern __shared__ __align__(128) uint8_t dsm_raw[];
+                     DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort) {
   // routing metadata cached once per block so that refilling a stage needs no
   // global round trips: expert offsets, active experts, token of each row
   __shared__ int32_t sm_off[kMaxE + 1], sm_act[kMaxE], sm_tok[kMaxSlots];
-  __shared__ __align__(8) uint64_t full[4];
-  __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8;
   // stage: [2][fr][H] weights, then [kRC][H] token rows of the item's expert
@@ -235,22 +248,20 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   uint8_t* stage_base = dsm_raw;
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
-    s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  wait_prior_grid();
-  allow_next_grid();
-  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = ws.offsets[i];
-  const int nact = *ws.nactive;
-  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = ws.active[i];
+  fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
+  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = __ldcg(ws.offsets + i);
+  const int nact = __ldcg(ws.nactive);
+  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
   __syncthreads();
-  for (int i = threadIdx.x; i < sm_off[E]; i += kThreads) sm_tok[i] = ws.sorted_slots[i] % T;
+  for (int i = threadIdx.x; i < sm_off[E]; i += kThreads) sm_tok[i] = __ldcg(ws.sorted_slots + i) % T;
   __syncthreads();
   const int nfc = (F + fr - 1) / fr;
   const int items = nact * nfc;
-  const int mine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int mine = items > (int)bid ? (items - 1 - (int)bid) / (int)nblk + 1 : 0;
   auto issue = [&](int j) {
-    const int item = blockIdx.x + j * gridDim.x;
+    const int item = bid + j * nblk;
     const int e = sm_act[item / nfc];
     const int f0 = (item % nfc) * fr;
     const int rows = min(fr, F - f0);
@@ -270,12 +281,12 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   if (threadIdx.x == 0)
     for (int j = 0; j < stages && j < mine; ++j) issue(j);
   for (int j = 0; j < mine; ++j) {
-    const int item = blockIdx.x + j * gridDim.x;
+    const int item = bid + j * nblk;
     const int e = sm_act[item / nfc];
     const int f0 = (item % nfc) * fr;
     const int rows = min(fr, F - f0);
     const int s = j % stages;
-    if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, &s_abort, ws.err)) break;
+    if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, s_abort, ws.err)) break;
     const uint4* gsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
     const uint4* usm = gsm + (size_t)fr * hv;
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
@@ -322,15 +333,24 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   }
 }
 
+__global__ void __launch_bounds__(kThreads)
+decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
+                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int stages,
+                     DecodeWs ws) {
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  __shared__ __align__(8) uint64_t full[4];
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) s_abort = 0;
+  wait_prior_grid();
+  allow_next_grid();
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort);
+}
+
 // down: item = (active expert e, hr rows of H starting at h0): stage =
 // [hr][F] bf16.  Warp w computes rows h0 + w, h0 + w + 8, ...:
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
-__global__ void __launch_bounds__(kThreads)
-decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws) {
-  extern __shared__ __align__(128) uint8_t dsm_raw[];
+__device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort) {
   __shared__ int32_t sm_off[kMaxE + 1], sm_act[kMaxE];
-  __shared__ __align__(8) uint64_t full[4];
-  __shared__ int s_abort;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fv = F / 8;
   // stage: [hr][F] weights, then [kRC][F] h rows of the item's expert
@@ -339,20 +359,18 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
   uint8_t* stage_base = dsm_raw;
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
-    s_abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  wait_prior_grid();
-  allow_next_grid();
-  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = ws.offsets[i];
-  const int nact = *ws.nactive;
-  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = ws.active[i];
+  fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
+  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = __ldcg(ws.offsets + i);
+  const int nact = __ldcg(ws.nactive);
+  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
   __syncthreads();
   const int nhc = (H + hr - 1) / hr;
   const int items = nact * nhc;
-  const int mine = items > (int)blockIdx.x ? (items - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+  const int mine = items > (int)bid ? (items - 1 - (int)bid) / (int)nblk + 1 : 0;
   auto issue = [&](int j) {
-    const int item = blockIdx.x + j * gridDim.x;
+    const int item = bid + j * nblk;
     const int e = sm_act[item / nhc];
     const int h0 = (item % nhc) * hr;
     const uint32_t bytes = (uint32_t)min(hr, H - h0) * F * 2;
@@ -369,12 +387,12 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
   if (threadIdx.x == 0)
     for (int j = 0; j < stages && j < mine; ++j) issue(j);
   for (int j = 0; j < mine; ++j) {
-    const int item = blockIdx.x + j * gridDim.x;
+    const int item = bid + j * nblk;
     const int e = sm_act[item / nhc];
     const int h0 = (item % nhc) * hr;
     const int rows = min(hr, H - h0);
     const int s = j % stages;
-    if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, &s_abort, ws.err)) break;
+    if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, s_abort, ws.err)) break;
     const uint4* wsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += kRC) {
@@ -400,7 +418,7 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
           for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
           if (lane == 0) {
             const int row = r0 + c0 + r;
-            ws.d[(int64_t)row * H + h0 + jr] = acc * ws.wsorted[row];
+            ws.d[(int64_t)row * H + h0 + jr] = acc * __ldcg(ws.wsorted + row);
           }
         }
       }
@@ -413,19 +431,89 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
   }
 }
 
+__global__ void __launch_bounds__(kThreads)
+decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws) {
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  __shared__ __align__(8) uint64_t full[4];
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) s_abort = 0;
+  wait_prior_grid();
+  allow_next_grid();
+  down_body(w_down, H, F, E, hr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort);
+}
+
 // --------------------------------------------------------------- combine --
 // y[t, h] = sum_{j<k} d[slot_pos[j*T + t], h] in slot order (deterministic).
+template <class TY>
+__device__ __forceinline__ void combine_body(int T, int H, int k, TY* __restrict__ y, const DecodeWs& ws, int64_t gtid,
+                                             int64_t nthreads) {
+  for (int64_t i = gtid; i < (int64_t)T * H; i += nthreads) {
+    const int t = (int)(i / H), h = (int)(i - (int64_t)t * H);
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc += __ldcg(ws.d + (int64_t)__ldcg(ws.slot_pos + j * T + t) * H + h);
+    y[i] = from_f32<TY>(acc);
+  }
+}
+
 template <class TY>
 __global__ void __launch_bounds__(kThreads)
 decode_combine_kernel(int T, int H, int k, TY* __restrict__ y, DecodeWs ws) {
   wait_prior_grid();
-  for (int64_t i = (int64_t)blockIdx.x * kThreads + threadIdx.x; i < (int64_t)T * H;
-       i += (int64_t)gridDim.x * kThreads) {
-    const int t = (int)(i / H), h = (int)(i - (int64_t)t * H);
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) acc += ws.d[(int64_t)ws.slot_pos[j * T + t] * H + h];
-    y[i] = from_f32<TY>(acc);
+  combine_body<TY>(T, H, k, y, ws, (int64_t)blockIdx.x * kThreads + threadIdx.x, (int64_t)gridDim.x * kThreads);
+}
+
+// ---------------------------------------------------------- fused kernel --
+// All five phases in one cooperative launch (every block resident): phases
+// are separated by a grid barrier, so the decode step pays one launch and
+// no inter-kernel gaps.  The barrier spins on a counter for at most ~2 s; on
+// expiry it records FRANK_ETIMEOUT and lets the kernel run to its end.
+__device__ __forceinline__ void grid_barrier(unsigned* counter, unsigned target, int* s_abort, int32_t* err) {
+  asm volatile("fence.proxy.async.global;" ::: "memory");  // generic writes before later bulk reads
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    atomicAdd(counter, 1u);
+    uint64_t t0 = 0;
+    for (uint32_t i = 0;; ++i) {
+      unsigned v;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(counter) : "memory");
+      if (v >= target) break;
+      if ((i & 63u) == 63u) {
+        const uint64_t now = global_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > 2000000000ull) {
+          atomicExch(err, FRANK_ETIMEOUT);
+          *s_abort = 1;
+          break;
+        }
+      }
+      __nanosleep(64);
+    }
   }
+  __syncthreads();
+}
+
+template <class TW, class TY>
+__global__ void __launch_bounds__(kThreads, 1)
+decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr,
+                    const __nv_bfloat16* __restrict__ w_gate, const __nv_bfloat16* __restrict__ w_up,
+                    const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int normalize,
+                    int fr, int stages_gu, int hr, int stages_dn, TY* __restrict__ y, DecodeWs ws) {
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  __shared__ __align__(8) uint64_t full_gu[4], full_dn[4];
+  __shared__ int s_abort;
+  if (threadIdx.x == 0) s_abort = 0;
+  const int bid = blockIdx.x, nblk = gridDim.x;
+  route_body<TW>(x, wr, T, H, E, ws, bid * kWarps + (threadIdx.x >> 5), nblk * kWarps);
+  grid_barrier(ws.gbar, 1u * nblk, &s_abort, ws.err);
+  if (bid == 0) finalize_body(T, E, k, normalize, ws, dsm_raw);
+  grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort);
+  grid_barrier(ws.gbar, 3u * nblk, &s_abort, ws.err);
+  down_body(w_down, H, F, E, hr, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort);
+  grid_barrier(ws.gbar, 4u * nblk, &s_abort, ws.err);
+  combine_body<TY>(T, H, k, y, ws, (int64_t)bid * kThreads + threadIdx.x, (int64_t)nblk * kThreads);
 }
 
 template <typename... KArgs, typename... Args>
@@ -442,6 +530,35 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
+template <class TW, class TY>
+int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, const void* wd, int64_t T, int64_t H,
+                 int64_t F, int64_t E, int64_t k, int normalize, int fr, int stages_gu, int hr, int stages_dn,
+                 void* y, const DecodeWs& ws, size_t smem, cudaStream_t st) {
+  auto kern = decode_fused_kernel<TW, TY>;
+  FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  int per_sm = 0;
+  FRANK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
+  if (per_sm < 1) {
+    frank::set_error("decode block: the fused kernel does not fit on an SM");
+    return FRANK_EINVAL;
+  }
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(frank::num_sms());
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  FRANK_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)x, (const TW*)wr, (const __nv_bfloat16*)wg,
+                                    (const __nv_bfloat16*)wu, (const __nv_bfloat16*)wd, (int)T, (int)H, (int)F,
+                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn, (TY*)y, ws));
+  FRANK_LAUNCH_CHECK();
+  return FRANK_OK;
 }
 
 }  // namespace
@@ -467,6 +584,7 @@ size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t
   c.take<int32_t>(E);
   c.take<int32_t>(1);
   c.take<float>(n * H);
+  c.take<unsigned>(1);
   return align_up(c.used, 256);
 }
 
@@ -498,6 +616,47 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.active = c.take<int32_t>(E);
   ws.nactive = c.take<int32_t>(1);
   ws.d = c.take<float>(n * H);
+  ws.gbar = c.take<unsigned>(1);
+  ws.err = device_error_word();
+  const int fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
+  const size_t stage_gu = (size_t)2 * fr * H * 2 + (size_t)kRC * H * 2;
+  const int hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
+  const size_t stage_dn = (size_t)hr * F * 2 + (size_t)kRC * F * 2;
+  const size_t kSmemMax = 227 * 1024;
+  int stages_gu = (int)((kSmemMax - 16 * 1024) / stage_gu);
+  stages_gu = stages_gu > 4 ? 4 : stages_gu;
+  int stages_dn = (int)((kSmemMax - 16 * 1024) / stage_dn);
+  stages_dn = stages_dn > 4 ? 4 : stages_dn;
+  if (stages_gu < 2 || stages_dn < 2) {
+    set_error("decode block: n_embd=%lld / n_ff=%lld too large for the streaming kernels", (long long)H,
+              (long long)F);
+    return FRANK_EINVAL;
+  }
+  const char* fenv = getenv("FRANK_DECODE_FUSED");
+  if (!(fenv && fenv[0] == '0')) {
+    // one cooperative launch (decode_fused_kernel)
+    size_t smem = stages_gu * stage_gu;
+    if (stages_dn * stage_dn > smem) smem = stages_dn * stage_dn;
+    if (kFinalizeSmem > smem) smem = kFinalizeSmem;
+    mark(0, st);
+    FRANK_CUDA_TRY(cudaMemsetAsync(ws.gbar, 0, sizeof(unsigned), st));
+    int st_launch;
+    if (wr_dtype == FRANK_F32 && y_dtype == FRANK_F32)
+      st_launch = launch_fused<float, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
+                                             stages_gu, hr, stages_dn, y, ws, smem, st);
+    else if (wr_dtype == FRANK_F32)
+      st_launch = launch_fused<float, __nv_bfloat16>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
+                                                     stages_gu, hr, stages_dn, y, ws, smem, st);
+    else if (y_dtype == FRANK_F32)
+      st_launch = launch_fused<__nv_bfloat16, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
+                                                     stages_gu, hr, stages_dn, y, ws, smem, st);
+    else
+      st_launch = launch_fused<__nv_bfloat16, __nv_bfloat16>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k,
+                                                             normalize, fr, stages_gu, hr, stages_dn, y, ws, smem,
+                                                             st);
+    FRANK_TRY(st_launch);
+    for (int m = 1; m <= 6; ++m) mark(m, st);
+  } else {
   mark(0, st);
   const int64_t items = E * ((T + kRouteTok - 1) / kRouteTok);
   const unsigned rblocks = (unsigned)((items + kWarps - 1) / kWarps);
@@ -562,6 +721,7 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
     FRANK_LAUNCH_CHECK();
   }
   mark(6, st);
+  }
   if (route_w) FRANK_CUDA_TRY(cudaMemcpyAsync(route_w, ws.w, n * sizeof(float), cudaMemcpyDeviceToDevice, st));
   if (route_ids)
     FRANK_CUDA_TRY(cudaMemcpyAsync(route_ids, ws.ids, n * sizeof(int32_t), cudaMemcpyDeviceToDevice, st));
