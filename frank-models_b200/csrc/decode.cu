@@ -305,15 +305,29 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
         const uint4* ur = usm + (size_t)warp * hv;
         for (int r = 0; r < rc; ++r) {
           float g = 0.f, u = 0.f;
-          for (int v = lane; v < hv; v += 32) {
-            float gv[8], uv[8], xv[8];
-            bf16x8_to_f32(gr[v], gv);
-            bf16x8_to_f32(ur[v], uv);
-            bf16x8_to_f32(xr[r * hv + v], xv);
+          // all shared-memory loads of a 256-slice round are issued before
+          // any is used (independent loads instead of a dependent chain)
+          for (int v0 = 0; v0 < hv; v0 += 32 * 8) {
+            uint4 gq[8], uq[8], xq[8];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) {
-              g = fmaf(gv[q], xv[q], g);
-              u = fmaf(uv[q], xv[q], u);
+            for (int i = 0; i < 8; ++i) {
+              const int v = v0 + lane + 32 * i;
+              const bool ok = v < hv;
+              gq[i] = ok ? gr[v] : make_uint4(0, 0, 0, 0);
+              uq[i] = ok ? ur[v] : make_uint4(0, 0, 0, 0);
+              xq[i] = ok ? xr[r * hv + v] : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              float gv[8], uv[8], xv[8];
+              bf16x8_to_f32(gq[i], gv);
+              bf16x8_to_f32(uq[i], uv);
+              bf16x8_to_f32(xq[i], xv);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                g = fmaf(gv[q], xv[q], g);
+                u = fmaf(uv[q], xv[q], u);
+              }
             }
           }
 #pragma unroll
@@ -407,12 +421,23 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
         const uint4* wr = wsm + (size_t)jr * fv;
         for (int r = 0; r < rc; ++r) {
           float acc = 0.f;
-          for (int v = lane; v < fv; v += 32) {
-            float wv[8], hv8[8];
-            bf16x8_to_f32(wr[v], wv);
-            bf16x8_to_f32(hr8[r * fv + v], hv8);
+          for (int v0 = 0; v0 < fv; v0 += 32 * 4) {
+            uint4 wq[4], hq[4];
 #pragma unroll
-            for (int q = 0; q < 8; ++q) acc = fmaf(wv[q], hv8[q], acc);
+            for (int i = 0; i < 4; ++i) {
+              const int v = v0 + lane + 32 * i;
+              const bool ok = v < fv;
+              wq[i] = ok ? wr[v] : make_uint4(0, 0, 0, 0);
+              hq[i] = ok ? hr8[r * fv + v] : make_uint4(0, 0, 0, 0);
+            }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              float wv[8], hv8[8];
+              bf16x8_to_f32(wq[i], wv);
+              bf16x8_to_f32(hq[i], hv8);
+#pragma unroll
+              for (int q = 0; q < 8; ++q) acc = fmaf(wv[q], hv8[q], acc);
+            }
           }
 #pragma unroll
           for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
