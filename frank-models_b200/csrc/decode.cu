@@ -71,6 +71,7 @@ struct DecodeWs {
   float* d;             // [k*T, H] down output x gate weight
   int32_t* err;         // device error word (bounded waits)
   unsigned* gbar;       // grid-barrier counter of the fused kernel (zeroed per call)
+  int n_slots;          // k * T
 };
 
 // Programmatic dependent launch: a kernel's blocks may start while the
@@ -251,11 +252,11 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
+  // one round trip: every table is loaded in full, independently
   for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = __ldcg(ws.offsets + i);
+  for (int i = threadIdx.x; i < E; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
+  for (int i = threadIdx.x; i < ws.n_slots; i += kThreads) sm_tok[i] = __ldcg(ws.sorted_slots + i) % T;
   const int nact = __ldcg(ws.nactive);
-  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
-  __syncthreads();
-  for (int i = threadIdx.x; i < sm_off[E]; i += kThreads) sm_tok[i] = __ldcg(ws.sorted_slots + i) % T;
   __syncthreads();
   const int nfc = (F + fr - 1) / fr;
   const int items = nact * nfc;
@@ -377,8 +378,8 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
   }
   fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
   for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = __ldcg(ws.offsets + i);
+  for (int i = threadIdx.x; i < E; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
   const int nact = __ldcg(ws.nactive);
-  for (int i = threadIdx.x; i < nact; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
   __syncthreads();
   const int nhc = (H + hr - 1) / hr;
   const int items = nact * nhc;
@@ -642,6 +643,7 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.nactive = c.take<int32_t>(1);
   ws.d = c.take<float>(n * H);
   ws.gbar = c.take<unsigned>(1);
+  ws.n_slots = (int)n;
   ws.err = device_error_word();
   const int fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
   const size_t stage_gu = (size_t)2 * fr * H * 2 + (size_t)kRC * H * 2;
