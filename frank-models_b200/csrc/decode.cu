@@ -366,6 +366,7 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
 __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort) {
   __shared__ int32_t sm_off[kMaxE + 1], sm_act[kMaxE];
+  __shared__ float sm_w[kMaxSlots];  // gate weight of every expert-sorted row
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fv = F / 8;
   // stage: [hr][F] weights, then [kRC][F] h rows of the item's expert
@@ -379,6 +380,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
   fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
   for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = __ldcg(ws.offsets + i);
   for (int i = threadIdx.x; i < E; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
+  for (int i = threadIdx.x; i < ws.n_slots; i += kThreads) sm_w[i] = __ldcg(ws.wsorted + i);
   const int nact = __ldcg(ws.nactive);
   __syncthreads();
   const int nhc = (H + hr - 1) / hr;
@@ -444,7 +446,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
           for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
           if (lane == 0) {
             const int row = r0 + c0 + r;
-            ws.d[(int64_t)row * H + h0 + jr] = acc * __ldcg(ws.wsorted + row);
+            ws.d[(int64_t)row * H + h0 + jr] = acc * sm_w[row];
           }
         }
       }
