@@ -129,19 +129,26 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
 // warp_cnt [kWarps][kMaxE], rank [kMaxSlots] (int32).
 constexpr size_t kFinalizeSmem = sizeof(float) * kWarps * kMaxE + sizeof(int32_t) * (kMaxE + 1 + kWarps * kMaxE + kMaxSlots);
 
-__device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch) {
-  float* lg = reinterpret_cast<float*>(scratch);
-  int32_t* running = reinterpret_cast<int32_t*>(lg + kWarps * kMaxE);
-  int32_t* warp_cnt = running + kMaxE + 1;
-  int32_t* rank = warp_cnt + kWarps * kMaxE;
+// softmax + top-k (+ renorm) of tokens t = gwarp, gwarp + nwarps, ...;
+// lg: shared scratch [kWarps][kMaxE] of this block.
+__device__ __forceinline__ void topk_body(int T, int E, int k, int normalize, const DecodeWs& ws, float* lg, int gwarp,
+                                          int nwarps) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < T; t += kWarps) {
+  for (int t = gwarp; t < T; t += nwarps) {
     for (int e = lane; e < E; e += 32) lg[warp * kMaxE + e] = __ldcg(ws.logits + (int64_t)e * T + t);
     __syncwarp();
     warp_softmax_topk(lg + warp * kMaxE, E, k, normalize, ws.w, ws.ids, T, t);
     __syncwarp();
   }
-  __syncthreads();
+}
+
+// One block: the stable permutation of the top-k slots and the active list.
+__device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs& ws, uint8_t* scratch) {
+  float* lg = reinterpret_cast<float*>(scratch);
+  int32_t* running = reinterpret_cast<int32_t*>(lg + kWarps * kMaxE);
+  int32_t* warp_cnt = running + kMaxE + 1;
+  int32_t* rank = warp_cnt + kWarps * kMaxE;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // stable counting sort of the n = k*T flat slots by expert (same order as
   // argsort(ids.reshape(-1), stable)); one block, warp-level ranks
   const int n = k * T;
@@ -152,7 +159,7 @@ __device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize
   __syncthreads();
   for (int base = 0; base < n; base += kThreads) {
     const int s = base + threadIdx.x;
-    const int e = s < n ? ws.ids[s] : -1;
+    const int e = s < n ? __ldcg(ws.ids + s) : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_w = __popc(peers & ((1u << lane) - 1u));
     const int leader = __ffs(peers) - 1;
@@ -201,10 +208,37 @@ __device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize
   }
   __syncthreads();
   for (int s = threadIdx.x; s < n; s += kThreads) {
-    const int32_t pos = running[ws.ids[s]] + rank[s];
+    const int32_t pos = running[__ldcg(ws.ids + s)] + rank[s];
     ws.sorted_slots[pos] = s;
     ws.slot_pos[s] = pos;
-    ws.wsorted[pos] = ws.w[s];
+    ws.wsorted[pos] = __ldcg(ws.w + s);
+  }
+}
+
+__device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch) {
+  topk_body(T, E, k, normalize, ws, reinterpret_cast<float*>(scratch), threadIdx.x >> 5, kWarps);
+  __syncthreads();
+  permute_body(T, E, k, ws, scratch);
+}
+
+// L2 prefetch of the selected experts' gate, up and down matrices in 64 KiB
+// pieces, spread over the threads of blocks 0 .. nblk-1 (duplicated experts
+// are prefetched more than once, which costs L2 lookups, not HBM).
+__device__ __forceinline__ void prefetch_body(const __nv_bfloat16* w_gate, const __nv_bfloat16* w_up,
+                                              const __nv_bfloat16* w_down, int H, int F, const DecodeWs& ws, int bid,
+                                              int nblk) {
+  const int64_t mat = (int64_t)F * H * 2;
+  const int nchunk = (int)((mat + 65535) / 65536);
+  const int64_t units = (int64_t)ws.n_slots * 3 * nchunk;
+  for (int64_t u = (int64_t)bid * kThreads + threadIdx.x; u < units; u += (int64_t)nblk * kThreads) {
+    const int s = (int)(u / (3 * nchunk));
+    const int rem = (int)(u - (int64_t)s * 3 * nchunk);
+    const int m = rem / nchunk, c = rem - m * nchunk;
+    const int e = __ldcg(ws.ids + s);
+    const char* base = reinterpret_cast<const char*>(m == 0 ? w_gate : m == 1 ? w_up : w_down) + (int64_t)e * mat;
+    const int64_t off = (int64_t)c * 65536;
+    const uint32_t sz = (uint32_t)((mat - off) < 65536 ? (mat - off) : 65536);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(sz) : "memory");
   }
 }
 
@@ -420,33 +454,46 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
           hr8[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
         __syncthreads();
       }
-      for (int jr = warp; jr < rows; jr += kWarps) {
-        const uint4* wr = wsm + (size_t)jr * fv;
+      // each warp takes its rows jr = warp + 8*jj (jj < 4) together: four
+      // independent dot products in flight
+      for (int jb = 0; jb < rows; jb += 4 * kWarps) {
         for (int r = 0; r < rc; ++r) {
-          float acc = 0.f;
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
           for (int v0 = 0; v0 < fv; v0 += 32 * 4) {
-            uint4 wq[4], hq[4];
+            uint4 hq[4];
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const int v = v0 + lane + 32 * i;
-              const bool ok = v < fv;
-              wq[i] = ok ? wr[v] : make_uint4(0, 0, 0, 0);
-              hq[i] = ok ? hr8[r * fv + v] : make_uint4(0, 0, 0, 0);
+              hq[i] = v < fv ? hr8[r * fv + v] : make_uint4(0, 0, 0, 0);
             }
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              float wv[8], hv8[8];
-              bf16x8_to_f32(wq[i], wv);
-              bf16x8_to_f32(hq[i], hv8);
+            for (int jj = 0; jj < 4; ++jj) {
+              const int jr = jb + warp + kWarps * jj;
+              const uint4* wr = wsm + (size_t)min(jr, rows - 1) * fv;
 #pragma unroll
-              for (int q = 0; q < 8; ++q) acc = fmaf(wv[q], hv8[q], acc);
+              for (int i = 0; i < 4; ++i) {
+                const int v = v0 + lane + 32 * i;
+                if (v < fv) {
+                  float wv[8], hv8[8];
+                  bf16x8_to_f32(wr[v], wv);
+                  bf16x8_to_f32(hq[i], hv8);
+#pragma unroll
+                  for (int q = 0; q < 8; ++q) acc[jj] = fmaf(wv[q], hv8[q], acc[jj]);
+                }
+              }
             }
           }
 #pragma unroll
-          for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-          if (lane == 0) {
-            const int row = r0 + c0 + r;
-            ws.d[(int64_t)row * H + h0 + jr] = acc * sm_w[row];
+          for (int o = 16; o; o >>= 1)
+#pragma unroll
+            for (int jj = 0; jj < 4; ++jj) acc[jj] += __shfl_xor_sync(0xffffffffu, acc[jj], o);
+          if (lane < 4) {
+            const int jr = jb + warp + kWarps * lane;
+            const float a = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
+            if (jr < rows) {
+              const int row = r0 + c0 + r;
+              ws.d[(int64_t)row * H + h0 + jr] = a * sm_w[row];
+            }
           }
         }
       }
@@ -527,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr,
                     const __nv_bfloat16* __restrict__ w_gate, const __nv_bfloat16* __restrict__ w_up,
                     const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int normalize,
-                    int fr, int stages_gu, int hr, int stages_dn, TY* __restrict__ y, DecodeWs ws) {
+                    int fr, int stages_gu, int hr, int stages_dn, int prefetch, TY* __restrict__ y, DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full_gu[4], full_dn[4];
   __shared__ int s_abort;
@@ -535,12 +582,20 @@ decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   const int bid = blockIdx.x, nblk = gridDim.x;
   route_body<TW>(x, wr, T, H, E, ws, bid * kWarps + (threadIdx.x >> 5), nblk * kWarps);
   grid_barrier(ws.gbar, 1u * nblk, &s_abort, ws.err);
-  if (bid == 0) finalize_body(T, E, k, normalize, ws, dsm_raw);
+  topk_body(T, E, k, normalize, ws, reinterpret_cast<float*>(dsm_raw), bid * kWarps + (threadIdx.x >> 5),
+            nblk * kWarps);
   grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort);
+  // HBM is idle while one block builds the permutation: the others pull the
+  // selected experts' weights into L2 (when they fit)
+  if (bid == 0)
+    permute_body(T, E, k, ws, dsm_raw);
+  else if (prefetch)
+    prefetch_body(w_gate, w_up, w_down, H, F, ws, bid - 1, nblk - 1);
   grid_barrier(ws.gbar, 3u * nblk, &s_abort, ws.err);
-  down_body(w_down, H, F, E, hr, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort);
   grid_barrier(ws.gbar, 4u * nblk, &s_abort, ws.err);
+  down_body(w_down, H, F, E, hr, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort);
+  grid_barrier(ws.gbar, 5u * nblk, &s_abort, ws.err);
   combine_body<TY>(T, H, k, y, ws, (int64_t)bid * kThreads + threadIdx.x, (int64_t)nblk * kThreads);
 }
 
@@ -584,7 +639,8 @@ int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, 
   cfg.numAttrs = 1;
   FRANK_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)x, (const TW*)wr, (const __nv_bfloat16*)wg,
                                     (const __nv_bfloat16*)wu, (const __nv_bfloat16*)wd, (int)T, (int)H, (int)F,
-                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn, (TY*)y, ws));
+                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn,
+                                    (int)(k * T * 3 * F * H * 2 <= (int64_t)96 << 20), (TY*)y, ws));
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
 }
