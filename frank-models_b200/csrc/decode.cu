@@ -221,26 +221,6 @@ __device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize
   permute_body(T, E, k, ws, scratch);
 }
 
-// L2 prefetch of the selected experts' gate, up and down matrices in 64 KiB
-// pieces, spread over the threads of blocks 0 .. nblk-1 (duplicated experts
-// are prefetched more than once, which costs L2 lookups, not HBM).
-__device__ __forceinline__ void prefetch_body(const __nv_bfloat16* w_gate, const __nv_bfloat16* w_up,
-                                              const __nv_bfloat16* w_down, int H, int F, const DecodeWs& ws, int bid,
-                                              int nblk) {
-  const int64_t mat = (int64_t)F * H * 2;
-  const int nchunk = (int)((mat + 65535) / 65536);
-  const int64_t units = (int64_t)ws.n_slots * 3 * nchunk;
-  for (int64_t u = (int64_t)bid * kThreads + threadIdx.x; u < units; u += (int64_t)nblk * kThreads) {
-    const int s = (int)(u / (3 * nchunk));
-    const int rem = (int)(u - (int64_t)s * 3 * nchunk);
-    const int m = rem / nchunk, c = rem - m * nchunk;
-    const int e = __ldcg(ws.ids + s);
-    const char* base = reinterpret_cast<const char*>(m == 0 ? w_gate : m == 1 ? w_up : w_down) + (int64_t)e * mat;
-    const int64_t off = (int64_t)c * 65536;
-    const uint32_t sz = (uint32_t)((mat - off) < 65536 ? (mat - off) : 65536);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off), "r"(sz) : "memory");
-  }
-}
 
 __global__ void __launch_bounds__(kThreads)
 decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
@@ -574,7 +554,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr,
                     const __nv_bfloat16* __restrict__ w_gate, const __nv_bfloat16* __restrict__ w_up,
                     const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int normalize,
-                    int fr, int stages_gu, int hr, int stages_dn, int prefetch, TY* __restrict__ y, DecodeWs ws) {
+                    int fr, int stages_gu, int hr, int stages_dn, TY* __restrict__ y, DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full_gu[4], full_dn[4];
   __shared__ int s_abort;
@@ -585,12 +565,7 @@ decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   topk_body(T, E, k, normalize, ws, reinterpret_cast<float*>(dsm_raw), bid * kWarps + (threadIdx.x >> 5),
             nblk * kWarps);
   grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
-  // HBM is idle while one block builds the permutation: the others pull the
-  // selected experts' weights into L2 (when they fit)
-  if (bid == 0)
-    permute_body(T, E, k, ws, dsm_raw);
-  else if (prefetch)
-    prefetch_body(w_gate, w_up, w_down, H, F, ws, bid - 1, nblk - 1);
+  if (bid == 0) permute_body(T, E, k, ws, dsm_raw);
   grid_barrier(ws.gbar, 3u * nblk, &s_abort, ws.err);
   gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort);
   grid_barrier(ws.gbar, 4u * nblk, &s_abort, ws.err);
@@ -639,8 +614,7 @@ int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, 
   cfg.numAttrs = 1;
   FRANK_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)x, (const TW*)wr, (const __nv_bfloat16*)wg,
                                     (const __nv_bfloat16*)wu, (const __nv_bfloat16*)wd, (int)T, (int)H, (int)F,
-                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn,
-                                    (int)(k * T * 3 * F * H * 2 <= (int64_t)96 << 20), (TY*)y, ws));
+                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn, (TY*)y, ws));
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
 }
