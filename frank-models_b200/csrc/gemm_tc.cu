@@ -151,34 +151,7 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int3
 // Epilogue of one accumulator tile for the 32 rows of one warp: thread
 // `lane` owns row `row`; taddr addresses this warp's TMEM lane quadrant.
 template <int MODE>
-__device__ __forceinline__ void epilogue_rows(const Params& p, int row, bool valid, int n, uint32_t taddr,
-                                              float* stage, int m_end) {
-  if (MODE != SWIGLU && p.row_rank == nullptr) {
-    // fp32 rows: restage each 32x32 block through shared memory (row stride
-    // 33 floats: conflict-free both ways) so that the warp writes whole
-    // 128-byte row segments instead of 32 rows x 16 bytes per store.
-    const int lane = threadIdx.x & 31;
-    const int row_base = row - lane;
-    const float s = (MODE == SCALE && valid) ? p.wrow[row] : 1.f;
-    float* out = reinterpret_cast<float*>(p.out);
-#pragma unroll 1
-    for (int c = 0; c < BN; c += 32) {
-      float v[32];
-      tmem_ld16(taddr + c, *reinterpret_cast<float(*)[16]>(v));
-      tmem_ld16(taddr + c + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-      tmem_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 32; ++i) stage[lane * 33 + i] = v[i] * s;
-      __syncwarp();
-      const int col = n * BN + c + lane;
-      if (col < p.N_out) {
-        const int rmax = min(32, m_end - row_base);
-        for (int rr = 0; rr < rmax; ++rr) out[(int64_t)(row_base + rr) * p.ldo + col] = stage[rr * 33 + lane];
-      }
-      __syncwarp();
-    }
-    return;
-  }
+__device__ __forceinline__ void epilogue_rows(const Params& p, int row, bool valid, int n, uint32_t taddr) {
   if (MODE == SWIGLU) {
     __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
 #pragma unroll 1
@@ -230,7 +203,6 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* prefix = reinterpret_cast<int*>(tmem_slot + 4);  // [E+1]
-  float* estage = reinterpret_cast<float*>(prefix + ((p.E + 1 + 3) & ~3));  // [4 warps][32][33] epilogue restage
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t bar0 = smem_u32(bars);
@@ -344,8 +316,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = tl.m0 + q * 32 + lane;
-      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16),
-                          estage + q * 32 * 33, tl.m_end);
+      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(a));
@@ -445,7 +416,6 @@ tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* prefix = reinterpret_cast<int*>(tmem_slot + 4);  // [E+1]
-  float* estage = reinterpret_cast<float*>(prefix + ((p.E + 1 + 3) & ~3));  // [4 warps][32][33] epilogue restage
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
@@ -557,8 +527,7 @@ tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = tl.m0 + (int)rank * 128 + q * 32 + lane;
-      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16),
-                          estage + q * 32 * 33, tl.m_end);
+      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(a), 0));
@@ -631,9 +600,8 @@ int make_map_3d(CUtensorMap* m, const void* base, int64_t E, int64_t N, int64_t 
   return FRANK_OK;
 }
 
-constexpr size_t kEpiStage = 4 * 32 * 33 * sizeof(float);
-size_t smem_bytes(int E) { return 1024 + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 4) + 16 + 4 * (E + 4) + 64 + kEpiStage; }
-size_t smem2_bytes(int E) { return 1024 + STAGES2 * STAGE2_BYTES + 8 * (2 * STAGES2 + 4) + 16 + 4 * (E + 4) + 64 + kEpiStage; }
+size_t smem_bytes(int E) { return 1024 + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 4) + 16 + 4 * (E + 1) + 64; }
+size_t smem2_bytes(int E) { return 1024 + STAGES2 * STAGE2_BYTES + 8 * (2 * STAGES2 + 4) + 16 + 4 * (E + 1) + 64; }
 
 // The CTA-pair form is opt-in (FRANK_TC_PAIR=1): on the B200s measured it
 // was ~7% slower than the single-CTA kernel on the Mixtral block, whose
