@@ -101,7 +101,20 @@ __global__ void ep_dispatch_kernel(const uint4* __restrict__ x, int64_t T, int64
     const int32_t s = sorted_slots[r];
     const uint4* src = x + (int64_t)(s % T) * vec_per_row;
     uint4* d = reinterpret_cast<uint4*>(peers.x[p]) + dst * vec_per_row;
-    for (int64_t v = lane; v < vec_per_row; v += 32) d[v] = src[v];
+    // all loads of a 16-vector round in flight before the (remote) stores
+    for (int64_t v0 = 0; v0 < vec_per_row; v0 += 32 * 16) {
+      uint4 buf[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int64_t v = v0 + lane + 32 * i;
+        if (v < vec_per_row) buf[i] = __ldg(src + v);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int64_t v = v0 + lane + 32 * i;
+        if (v < vec_per_row) d[v] = buf[i];
+      }
+    }
     if (lane == 0) peers.w[p][dst] = w[s];
   }
   __threadfence_system();
