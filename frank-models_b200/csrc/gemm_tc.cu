@@ -126,6 +126,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------- kernel --
+constexpr int kBandRows = 2048;
+
 struct Tile {
   int e, m0, m_end, n;
 };
@@ -139,12 +141,20 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int3
   const int e = lo;
   const int r0 = offsets[e], r1 = offsets[e + 1];
   const int mt = (r1 - r0 + bm - 1) / bm;
+  const int nt = (prefix[e + 1] - prefix[e]) / mt;
   const int local = t - prefix[e];
+  // Bands of kBandRows rows (L2-resident: 2048 rows x K bf16 = 16 MiB at
+  // K = 4096); inside a band m runs fastest, so the CTAs running at the same
+  // time share both the band's activation rows and a few weight tiles.
+  const int G = kBandRows / bm;
+  const int band = local / (G * nt);
+  const int gm = min(G, mt - band * G);
+  const int in = local - band * G * nt;
   Tile tl;
   tl.e = e;
-  tl.m0 = r0 + (local % mt) * bm;
+  tl.m0 = r0 + (band * G + in % gm) * bm;
   tl.m_end = r1;
-  tl.n = local / mt;
+  tl.n = in / gm;
   return tl;
 }
 
