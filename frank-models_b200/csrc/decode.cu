@@ -74,6 +74,17 @@ struct DecodeWs {
   int n_slots;          // k * T
 };
 
+// Routing tables of one call in shared memory: expert row offsets [E+1],
+// active experts [E] (first *nact valid), token of each expert-sorted row,
+// gate weight of each expert-sorted row.
+struct Meta {
+  int32_t* off;
+  int32_t* act;
+  int32_t* nact;
+  int32_t* tok;
+  float* w;
+};
+
 // Programmatic dependent launch: a kernel's blocks may start while the
 // previous kernel of the stream finishes; they wait here for its results.
 __device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
@@ -142,8 +153,11 @@ __device__ __forceinline__ void topk_body(int T, int E, int k, int normalize, co
   }
 }
 
-// One block: the stable permutation of the top-k slots and the active list.
-__device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs& ws, uint8_t* scratch) {
+// One block: the stable permutation of the top-k slots and the active list,
+// into the block's shared tables m; the writer block also stores them (and
+// slot_pos) to global memory.
+__device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs& ws, uint8_t* scratch, Meta m,
+                                             bool writer) {
   float* lg = reinterpret_cast<float*>(scratch);
   int32_t* running = reinterpret_cast<int32_t*>(lg + kWarps * kMaxE);
   int32_t* warp_cnt = running + kMaxE + 1;
@@ -193,43 +207,74 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
         if (lane >= o) incl += u;
       }
       if (e < E) {
-        ws.offsets[e] = carry + incl - c;
+        m.off[e] = carry + incl - c;
         running[e] = carry + incl - c;
+        if (writer) ws.offsets[e] = carry + incl - c;
       }
       const unsigned act = __ballot_sync(0xffffffffu, c > 0);
-      if (c > 0) ws.active[na + __popc(act & ((1u << lane) - 1u))] = e;
+      if (c > 0) {
+        const int slot = na + __popc(act & ((1u << lane) - 1u));
+        m.act[slot] = e;
+        if (writer) ws.active[slot] = e;
+      }
       na += __popc(act);
       carry += __shfl_sync(0xffffffffu, incl, 31);
     }
     if (lane == 0) {
-      ws.offsets[E] = carry;
-      *ws.nactive = na;
+      m.off[E] = carry;
+      *m.nact = na;
+      if (writer) {
+        ws.offsets[E] = carry;
+        *ws.nactive = na;
       }
+    }
   }
   __syncthreads();
   for (int s = threadIdx.x; s < n; s += kThreads) {
     const int32_t pos = running[__ldcg(ws.ids + s)] + rank[s];
-    ws.sorted_slots[pos] = s;
-    ws.slot_pos[s] = pos;
-    ws.wsorted[pos] = __ldcg(ws.w + s);
+    const float w = __ldcg(ws.w + s);
+    m.tok[pos] = s % T;
+    m.w[pos] = w;
+    if (writer) {
+      ws.sorted_slots[pos] = s;
+      ws.slot_pos[s] = pos;
+      ws.wsorted[pos] = w;
+    }
   }
+  __syncthreads();
 }
 
-__device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch) {
+__device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch,
+                                              Meta m) {
   topk_body(T, E, k, normalize, ws, reinterpret_cast<float*>(scratch), threadIdx.x >> 5, kWarps);
   __syncthreads();
-  permute_body(T, E, k, ws, scratch);
+  permute_body(T, E, k, ws, scratch, m, true);
 }
 
 
 __global__ void __launch_bounds__(kThreads)
 decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
   __shared__ __align__(16) uint8_t scratch[kFinalizeSmem];
+  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
+  __shared__ float m_w[kMaxSlots];
   wait_prior_grid();
   allow_next_grid();
-  finalize_body(T, E, k, normalize, ws, scratch);
+  finalize_body(T, E, k, normalize, ws, scratch, Meta{m_off, m_act, &m_nact, m_tok, m_w});
 }
 
+
+__device__ __forceinline__ Meta load_meta(const DecodeWs& ws, int T, int E, int32_t* off, int32_t* act, int32_t* nact,
+                                          int32_t* tok, float* w) {
+  for (int i = threadIdx.x; i <= E; i += kThreads) off[i] = __ldcg(ws.offsets + i);
+  for (int i = threadIdx.x; i < E; i += kThreads) act[i] = __ldcg(ws.active + i);
+  for (int i = threadIdx.x; i < ws.n_slots; i += kThreads) {
+    tok[i] = __ldcg(ws.sorted_slots + i) % T;
+    w[i] = __ldcg(ws.wsorted + i);
+  }
+  if (threadIdx.x == 0) *nact = __ldcg(ws.nactive);
+  __syncthreads();
+  return Meta{off, act, nact, tok, w};
+}
 
 // ----------------------------------------------- weight-streaming GEMVs --
 // Both GEMV kernels stream contiguous chunks of an expert's weight rows from
@@ -251,10 +296,11 @@ struct StreamSmem {
 // f0 + w for each token row: h = gate . x * silu(up . x).
 __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int stages,
-                     DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort) {
-  // routing metadata cached once per block so that refilling a stage needs no
-  // global round trips: expert offsets, active experts, token of each row
-  __shared__ int32_t sm_off[kMaxE + 1], sm_act[kMaxE], sm_tok[kMaxSlots];
+                     DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort, Meta m) {
+  // routing tables in shared memory: refilling a stage needs no global round trip
+  const int32_t* sm_off = m.off;
+  const int32_t* sm_act = m.act;
+  const int32_t* sm_tok = m.tok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8;
   // stage: [2][fr][H] weights, then [kRC][H] token rows of the item's expert
@@ -266,11 +312,7 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
-  // one round trip: every table is loaded in full, independently
-  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = __ldcg(ws.offsets + i);
-  for (int i = threadIdx.x; i < E; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
-  for (int i = threadIdx.x; i < ws.n_slots; i += kThreads) sm_tok[i] = __ldcg(ws.sorted_slots + i) % T;
-  const int nact = __ldcg(ws.nactive);
+  const int nact = *m.nact;
   __syncthreads();
   const int nfc = (F + fr - 1) / fr;
   const int items = nact * nfc;
@@ -372,15 +414,19 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   if (threadIdx.x == 0) s_abort = 0;
   wait_prior_grid();
   allow_next_grid();
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort);
+  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
+  __shared__ float m_w[kMaxSlots];
+  const Meta m = load_meta(ws, T, E, m_off, m_act, &m_nact, m_tok, m_w);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
 }
 
 // down: item = (active expert e, hr rows of H starting at h0): stage =
 // [hr][F] bf16.  Warp w computes rows h0 + w, h0 + w + 8, ...:
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
-__device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort) {
-  __shared__ int32_t sm_off[kMaxE + 1], sm_act[kMaxE];
-  __shared__ float sm_w[kMaxSlots];  // gate weight of every expert-sorted row
+__device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort, Meta m) {
+  const int32_t* sm_off = m.off;
+  const int32_t* sm_act = m.act;
+  const float* sm_w = m.w;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fv = F / 8;
   // stage: [hr][F] weights, then [kRC][F] h rows of the item's expert
@@ -392,10 +438,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
-  for (int i = threadIdx.x; i <= E; i += kThreads) sm_off[i] = __ldcg(ws.offsets + i);
-  for (int i = threadIdx.x; i < E; i += kThreads) sm_act[i] = __ldcg(ws.active + i);
-  for (int i = threadIdx.x; i < ws.n_slots; i += kThreads) sm_w[i] = __ldcg(ws.wsorted + i);
-  const int nact = __ldcg(ws.nactive);
+  const int nact = *m.nact;
   __syncthreads();
   const int nhc = (H + hr - 1) / hr;
   const int items = nact * nhc;
@@ -494,7 +537,10 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
   if (threadIdx.x == 0) s_abort = 0;
   wait_prior_grid();
   allow_next_grid();
-  down_body(w_down, H, F, E, hr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort);
+  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
+  __shared__ float m_w[kMaxSlots];
+  const Meta m = load_meta(ws, 1, E, m_off, m_act, &m_nact, m_tok, m_w);
+  down_body(w_down, H, F, E, hr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
 }
 
 // --------------------------------------------------------------- combine --
@@ -565,12 +611,16 @@ decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   topk_body(T, E, k, normalize, ws, reinterpret_cast<float*>(dsm_raw), bid * kWarps + (threadIdx.x >> 5),
             nblk * kWarps);
   grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
-  if (bid == 0) permute_body(T, E, k, ws, dsm_raw);
+  // every block builds the (small) permutation itself, so the streaming
+  // phases start without another barrier; block 0 also publishes it
+  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
+  __shared__ float m_w[kMaxSlots];
+  const Meta m{m_off, m_act, &m_nact, m_tok, m_w};
+  permute_body(T, E, k, ws, dsm_raw, m, bid == 0);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort, m);
   grid_barrier(ws.gbar, 3u * nblk, &s_abort, ws.err);
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort);
+  down_body(w_down, H, F, E, hr, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort, m);
   grid_barrier(ws.gbar, 4u * nblk, &s_abort, ws.err);
-  down_body(w_down, H, F, E, hr, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort);
-  grid_barrier(ws.gbar, 5u * nblk, &s_abort, ws.err);
   combine_body<TY>(T, H, k, y, ws, (int64_t)bid * kThreads + threadIdx.x, (int64_t)nblk * kThreads);
 }
 
