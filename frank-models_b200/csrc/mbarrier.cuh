@@ -43,7 +43,8 @@ __device__ __forceinline__ uint64_t global_ns() {
 }
 
 // Bounded wait: ~2 s of wall time, or until another role raised *abort.
-__device__ __noinline__ inline bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int32_t* err) {
+__device__ __noinline__ inline bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int32_t* err,
+                                              uint64_t limit_ns = 2000000000ull) {
   uint64_t t0 = 0;
   for (uint32_t i = 0;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
@@ -52,7 +53,7 @@ __device__ __noinline__ inline bool mbar_wait(uint32_t bar, uint32_t parity, vol
       uint64_t now = global_ns();
       if (t0 == 0) {
         t0 = now;
-      } else if (now - t0 > 2000000000ull) {
+      } else if (now - t0 > limit_ns) {
         *abort = 1;
         atomicExch(err, FRANK_ETIMEOUT);
         return false;

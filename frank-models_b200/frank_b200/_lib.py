@@ -62,6 +62,7 @@ SIGNATURES = {
                                           _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_size, _c_vp]),
     "frank_read_device_error": (_c_int, [_c_vp, _c_vp]),
     "frank_launch_count": (ctypes.c_uint64, []),
+    "frank_selftest_bounded_wait": (_c_int, [_c_i64, _c_vp, _c_vp]),
     "frank_profile_stages": (_c_int, [_c_int]),
     "frank_profile_read": (_c_int, [_c_vp, _c_int, _c_vp]),
 }

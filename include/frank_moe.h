@@ -266,6 +266,16 @@ int frank_expert_ffn_scatter(const void* xs, const float* w_rows,
  */
 int frank_read_device_error(int32_t* out, void* stream);
 
+/*
+ * Failure-detection self-test (no counterpart in the reference): runs the
+ * library's bounded mbarrier wait on a barrier that nothing completes, with
+ * the given limit in nanoseconds.  The wait must give up: *completed
+ * receives 0 and the device error word holds FRANK_ETIMEOUT (read and clear
+ * it with frank_read_device_error).  Synchronises the stream.
+ */
+int frank_selftest_bounded_wait(int64_t limit_ns, int32_t* completed,
+                                void* stream);
+
 /* Number of kernels this library has launched in this process. */
 uint64_t frank_launch_count(void);
 
