@@ -1,24 +1,28 @@
-// Decode-sized MoE FFN block (a few tokens per step): five launches,
-// weight-streaming on CUDA cores.
+// Decode-sized MoE FFN block (k * T <= E token slots): weight streaming on
+// CUDA cores.
 //
-// With T <= 64 tokens an expert receives a handful of rows, so the block is
+// With a few tokens an expert receives a handful of rows, so the block is
 // bound by reading the active experts' weights from HBM (3 x H x F bf16 per
-// active expert) -- tensor cores would idle on 128-row tiles.  The kernels:
-//   decode_route_kernel    router logits (one warp per (expert, 8 tokens));
-//   decode_finalize_kernel one block: softmax + top-k + renorm for every
-//                          token, the stable expert permutation and the list
-//                          of active experts (moe_ffn_block.mlir:54-128,
-//                          mul_mat_id.mlir:51-53);
-//   decode_gateup_kernel   persistent blocks over (active expert, 8 rows of F):
-//                          one gate row and one up row per warp streamed once
-//                          and dotted with the expert's token rows (gathered
-//                          straight from x), h = gate * silu(up)
-//                          (swiglu.mlir:37-47);
-//   decode_down_kernel     persistent blocks over (active expert, 32 rows of
-//                          H): d = down(h) * gate weight, fp32;
-//   combine_kernel         y[t] = sum of the k slots of t in slot order
-//                          (moe_ffn_block.mlir:179-206), deterministic.
-// Consecutive kernels use programmatic dependent launch; no atomics.
+// active expert) -- tensor cores would idle on 128-row tiles.  Phases:
+//   route    router logits; an item is (expert, 8 tokens) and, with fewer
+//            items than warps, the warps of a block split H for an item
+//            (moe_ffn_block.mlir:54-70);
+//   top-k    softmax + top-k + renorm of every token (moe_ffn_block.mlir:
+//            72-128), the stable expert permutation and the list of active
+//            experts (mul_mat_id.mlir:51-53);
+//   gate/up  persistent blocks over (active expert, fr rows of F): the gate
+//            and up rows streamed once into shared memory with bulk copies
+//            and dotted with the expert's token rows (gathered straight
+//            from x), h = gate * silu(up) (swiglu.mlir:37-47);
+//   down     persistent blocks over (active expert, hr rows of H):
+//            d = down(h) * gate weight, fp32;
+//   combine  y[t] = sum of the k slots of t in slot order
+//            (moe_ffn_block.mlir:179-206), deterministic.
+// decode_fused_kernel runs all phases in one cooperative launch with three
+// grid barriers (after route, gate/up and down): every block computes the
+// top-k and the permutation of all tokens itself.  FRANK_DECODE_FUSED=0 runs
+// the same bodies as five launches chained by programmatic dependent launch.
+// No atomics on data: results are deterministic and identical in both forms.
 #include <cstdlib>
 
 #include "common.cuh"
@@ -32,7 +36,7 @@ using namespace frank_topk;
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kRouteTok = 8;    // tokens per route warp item
-constexpr int kMaxSlots = 2048; // k * T handled by the decode path
+constexpr int kMaxSlots = kMaxE; // k * T handled by the decode path (k * T <= E)
 constexpr int kRC = 8;          // token rows per pass over an expert's weights
 
 __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
@@ -91,27 +95,41 @@ __device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol
 __device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
 // ----------------------------------------------------------------- route --
+// logits[e, t] = Wr[e] . x[t] for items (expert e, kRouteTok tokens).  When
+// there are fewer items than warps in the grid, wpi warps of one block split
+// H for each item (one dependent HBM round trip per warp instead of H/256)
+// and the block sums their partials in shared memory.  red: [kWarps][kRouteTok].
 template <class TW>
 __device__ __forceinline__ void route_body(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr, int T,
-                                           int H, int E, const DecodeWs& ws, int gwarp, int nwarps) {
-  const int lane = threadIdx.x & 31;
+                                           int H, int E, const DecodeWs& ws, float* red, int bid, int nblk) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tchunks = (T + kRouteTok - 1) / kRouteTok;
-  for (int item = gwarp; item < E * tchunks; item += nwarps) {
-    const int e = item / tchunks, t0 = (item - e * tchunks) * kRouteTok;
+  const int items = E * tchunks;
+  int wpi = kWarps;
+  while (wpi > 1 && (int64_t)items * wpi > (int64_t)nblk * kWarps) wpi >>= 1;
+  const int ipb = kWarps / wpi;  // items per block per round
+  const int sub = warp % wpi, slot = warp / wpi;
+  for (int base = bid * ipb; base < items; base += nblk * ipb) {  // uniform across the block
+    const int item = base + slot;
     float acc[kRouteTok];
 #pragma unroll
     for (int a = 0; a < kRouteTok; ++a) acc[a] = 0.f;
-#pragma unroll 8
-    for (int h = lane * 8; h < H; h += 256) {
-      float wv[8];
-      load8_w(wr + (int64_t)e * H + h, wv);
+    int e = 0, t0 = 0;
+    if (item < items) {
+      e = item / tchunks;
+      t0 = (item - e * tchunks) * kRouteTok;
+#pragma unroll 4
+      for (int h = (sub * 32 + lane) * 8; h < H; h += wpi * 256) {
+        float wv[8];
+        load8_w(wr + (int64_t)e * H + h, wv);
 #pragma unroll
-      for (int a = 0; a < kRouteTok; ++a) {
-        if (t0 + a < T) {
-          float xv[8];
-          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)(t0 + a) * H + h)), xv);
+        for (int a = 0; a < kRouteTok; ++a) {
+          if (t0 + a < T) {
+            float xv[8];
+            bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(x + (int64_t)(t0 + a) * H + h)), xv);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) acc[a] = fmaf(wv[i], xv[i], acc[a]);
+            for (int i = 0; i < 8; ++i) acc[a] = fmaf(wv[i], xv[i], acc[a]);
+          }
         }
       }
     }
@@ -120,17 +138,26 @@ __device__ __forceinline__ void route_body(const __nv_bfloat16* __restrict__ x, 
       float v = acc[a];
 #pragma unroll
       for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-      if (lane == 0 && t0 + a < T) ws.logits[(int64_t)e * T + t0 + a] = v;
+      if (lane == 0) red[warp * kRouteTok + a] = v;
     }
+    __syncthreads();
+    if (sub == 0 && lane < kRouteTok && item < items && t0 + lane < T) {
+      float v = 0.f;
+      for (int s2 = 0; s2 < wpi; ++s2) v += red[(slot * wpi + s2) * kRouteTok + lane];
+      ws.logits[(int64_t)e * T + t0 + lane] = v;
+    }
+    __syncthreads();
   }
 }
+
 
 template <class TW>
 __global__ void __launch_bounds__(kThreads)
 decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr, int T, int H, int E, int k,
                     int normalize, DecodeWs ws) {
+  __shared__ float red[kWarps * kRouteTok];
   allow_next_grid();
-  route_body<TW>(x, wr, T, H, E, ws, blockIdx.x * kWarps + (threadIdx.x >> 5), gridDim.x * kWarps);
+  route_body<TW>(x, wr, T, H, E, ws, red, blockIdx.x, gridDim.x);
 }
 
 // One block: softmax + top-k + renorm for every token, the stable expert
@@ -140,24 +167,124 @@ decode_route_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
 // warp_cnt [kWarps][kMaxE], rank [kMaxSlots] (int32).
 constexpr size_t kFinalizeSmem = sizeof(float) * kWarps * kMaxE + sizeof(int32_t) * (kMaxE + 1 + kWarps * kMaxE + kMaxSlots);
 
-// softmax + top-k (+ renorm) of tokens t = gwarp, gwarp + nwarps, ...;
-// lg: shared scratch [kWarps][kMaxE] of this block.
-__device__ __forceinline__ void topk_body(int T, int E, int k, int normalize, const DecodeWs& ws, float* lg, int gwarp,
-                                          int nwarps) {
+// Descending top-k (ties to the lower expert index) of one token's
+// probabilities p[E] by one warp, renormalised when asked: the selection
+// steps of warp_softmax_topk.
+__device__ __forceinline__ void warp_softmax_topk_probs(const float* p_in, int E, int k, int normalize, float* w_out,
+                                                        int32_t* id_out, int T, int t) {
+  const int lane = threadIdx.x & 31;
+  constexpr int kPer = kMaxE / 32;
+  float p[kPer];
+#pragma unroll
+  for (int i = 0; i < kPer; ++i) {
+    const int e = lane + 32 * i;
+    p[i] = e < E ? p_in[e] : -1.f;  // probabilities are >= 0; -1 marks "absent"
+  }
+  float wsum = 0.f;
+  for (int j = 0; j < k; ++j) {
+    float bv = -2.f;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (p[i] > bv) { bv = p[i]; bi = lane + 32 * i; }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i)
+      if (lane + 32 * i == bi) p[i] = -2.f;
+    wsum += bv;  // ascending j, as numpy's sum over a short axis
+    if (lane == 0) {
+      id_out[j * T + t] = bi;
+      w_out[j * T + t] = bv;
+    }
+  }
+  __syncwarp();
+  if (normalize && lane == 0)
+    for (int j = 0; j < k; ++j) w_out[j * T + t] = w_out[j * T + t] / wsum;
+  __syncwarp();
+}
+
+// Softmax over the E experts and the descending top-k (ties to the lower
+// expert index), renormalised when asked, of all T tokens by one block.
+// Warps compute the probabilities (one token per warp, the arithmetic of
+// warp_softmax_topk).  With at most one (token, expert) pair per thread,
+// every thread ranks its pair by counting the larger probabilities of its
+// token (no serial k-step selection); otherwise one warp selects per token.
+// Both give the same ids and weights.  prob: shared [T][E]; w_out / id_out:
+// [k, T], shared or global.
+__device__ __forceinline__ void block_softmax_topk(const float* logits, int T, int E, int k, int normalize,
+                                                   float* prob, float* w_out, int32_t* id_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = gwarp; t < T; t += nwarps) {
-    for (int e = lane; e < E; e += 32) lg[warp * kMaxE + e] = __ldcg(ws.logits + (int64_t)e * T + t);
-    __syncwarp();
-    warp_softmax_topk(lg + warp * kMaxE, E, k, normalize, ws.w, ws.ids, T, t);
-    __syncwarp();
+  constexpr int kPer = kMaxE / 32;
+  for (int t = warp; t < T; t += kWarps) {
+    float v[kPer];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? __ldcg(logits + (int64_t)e * T + t) : -INFINITY;
+      mx = fmaxf(mx, v[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      v[i] = e < E ? expf(v[i] - mx) : 0.f;
+      sum += v[i];
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = lane + 32 * i;
+      if (e < E) prob[t * E + e] = v[i] / sum;
+    }
+  }
+  __syncthreads();
+  if (T * E > kThreads) {
+    // more pairs than threads: a serial k-step selection per token and warp
+    for (int t = warp; t < T; t += kWarps) warp_softmax_topk_probs(prob + t * E, E, k, normalize, w_out, id_out, T, t);
+    __syncthreads();
+    return;
+  }
+  for (int idx = threadIdx.x; idx < T * E; idx += kThreads) {
+    const int t = idx / E, e = idx - t * E;
+    const float* pt = prob + t * E;
+    const float p = pt[e];
+    int r = 0;
+#pragma unroll 4
+    for (int u = 0; u < E; ++u) {
+      const float q = pt[u];
+      r += (q > p) | ((q == p) & (u < e));
+    }
+    if (r < k) {
+      id_out[r * T + t] = e;
+      w_out[r * T + t] = p;
+    }
+  }
+  __syncthreads();
+  if (normalize) {
+    for (int t = threadIdx.x; t < T; t += kThreads) {
+      float s = 0.f;
+      for (int j = 0; j < k; ++j) s += w_out[j * T + t];  // ascending j, as numpy's sum over a short axis
+      for (int j = 0; j < k; ++j) w_out[j * T + t] = w_out[j * T + t] / s;
+    }
+    __syncthreads();
   }
 }
 
-// One block: the stable permutation of the top-k slots and the active list,
-// into the block's shared tables m; the writer block also stores them (and
-// slot_pos) to global memory.
+// One block: the stable permutation of the top-k slots ids / gate weights wts
+// ([k, T], written earlier by this block) and the active list, into the
+// block's shared tables m; the writer block also stores them (and slot_pos)
+// to global memory.
 __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs& ws, uint8_t* scratch, Meta m,
-                                             bool writer) {
+                                             const int32_t* ids, const float* wts, bool writer) {
   float* lg = reinterpret_cast<float*>(scratch);
   int32_t* running = reinterpret_cast<int32_t*>(lg + kWarps * kMaxE);
   int32_t* warp_cnt = running + kMaxE + 1;
@@ -173,7 +300,7 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
   __syncthreads();
   for (int base = 0; base < n; base += kThreads) {
     const int s = base + threadIdx.x;
-    const int e = s < n ? __ldcg(ws.ids + s) : -1;
+    const int e = s < n ? ids[s] : -1;
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int rank_w = __popc(peers & ((1u << lane) - 1u));
     const int leader = __ffs(peers) - 1;
@@ -231,8 +358,8 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
   }
   __syncthreads();
   for (int s = threadIdx.x; s < n; s += kThreads) {
-    const int32_t pos = running[__ldcg(ws.ids + s)] + rank[s];
-    const float w = __ldcg(ws.w + s);
+    const int32_t pos = running[ids[s]] + rank[s];
+    const float w = wts[s];
     m.tok[pos] = s % T;
     m.w[pos] = w;
     if (writer) {
@@ -245,21 +372,21 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
 }
 
 __device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch,
-                                              Meta m) {
-  topk_body(T, E, k, normalize, ws, reinterpret_cast<float*>(scratch), threadIdx.x >> 5, kWarps);
-  __syncthreads();
-  permute_body(T, E, k, ws, scratch, m, true);
+                                              float* prob, Meta m) {
+  block_softmax_topk(ws.logits, T, E, k, normalize, prob, ws.w, ws.ids);
+  permute_body(T, E, k, ws, scratch, m, ws.ids, ws.w, true);
 }
 
 
 __global__ void __launch_bounds__(kThreads)
 decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
   __shared__ __align__(16) uint8_t scratch[kFinalizeSmem];
+  extern __shared__ __align__(16) float prob[];  // [T][E] (dynamic)
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   wait_prior_grid();
   allow_next_grid();
-  finalize_body(T, E, k, normalize, ws, scratch, Meta{m_off, m_act, &m_nact, m_tok, m_w});
+  finalize_body(T, E, k, normalize, ws, scratch, prob, Meta{m_off, m_act, &m_nact, m_tok, m_w});
 }
 
 
@@ -295,7 +422,7 @@ struct StreamSmem {
 // fr gate rows then fr up rows ([2][fr][H] bf16).  Warp w < fr computes row
 // f0 + w for each token row: h = gate . x * silu(up . x).
 __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
-                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int stages,
+                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int rcap, int stages,
                      DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort, Meta m) {
   // routing tables in shared memory: refilling a stage needs no global round trip
   const int32_t* sm_off = m.off;
@@ -303,9 +430,9 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
   const int32_t* sm_tok = m.tok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8;
-  // stage: [2][fr][H] weights, then [kRC][H] token rows of the item's expert
+  // stage: [2][fr][H] weights, then [rcap][H] token rows of the item's expert
   const uint32_t wbytes = 2u * fr * H * 2;
-  const uint32_t stage_bytes = wbytes + (uint32_t)kRC * H * 2;
+  const uint32_t stage_bytes = wbytes + (uint32_t)rcap * H * 2;
   uint8_t* stage_base = dsm_raw;
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
@@ -327,7 +454,7 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
     const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
     const uint32_t bar = smem_u32(&full[s]);
     const int r0 = sm_off[e];
-    const int rc = min(kRC, sm_off[e + 1] - r0);
+    const int rc = min(rcap, sm_off[e + 1] - r0);
     const uint32_t xrow = (uint32_t)H * 2;
     mbar_expect_tx(bar, 2 * bytes + rc * xrow);
     bulk_load(dst, w_gate + ((int64_t)e * F + f0) * H, bytes, bar);
@@ -347,10 +474,10 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
     const uint4* gsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
     const uint4* usm = gsm + (size_t)fr * hv;
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
-    for (int c0 = 0; c0 < cnt; c0 += kRC) {
-      const int rc = min(kRC, cnt - c0);
+    for (int c0 = 0; c0 < cnt; c0 += rcap) {
+      const int rc = min(rcap, cnt - c0);
       uint4* xr = reinterpret_cast<uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
-      if (c0 > 0) {  // more than kRC rows: later chunks are gathered into the same area
+      if (c0 > 0) {  // more than rcap rows: later chunks are gathered into the same area
         for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
           const int r = i / hv, v = i - r * hv;
           xr[i] = reinterpret_cast<const uint4*>(x + (int64_t)sm_tok[r0 + c0 + r] * H)[v];
@@ -406,7 +533,7 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
 
 __global__ void __launch_bounds__(kThreads)
 decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
-                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int stages,
+                     const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int rcap, int stages,
                      DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full[4];
@@ -417,21 +544,23 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   const Meta m = load_meta(ws, T, E, m_off, m_act, &m_nact, m_tok, m_w);
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
 }
 
 // down: item = (active expert e, hr rows of H starting at h0): stage =
 // [hr][F] bf16.  Warp w computes rows h0 + w, h0 + w + 8, ...:
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
-__device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort, Meta m) {
+__device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr,
+                                          int rcap, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw,
+                                          uint64_t* full, int* s_abort, Meta m) {
   const int32_t* sm_off = m.off;
   const int32_t* sm_act = m.act;
   const float* sm_w = m.w;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int fv = F / 8;
-  // stage: [hr][F] weights, then [kRC][F] h rows of the item's expert
+  // stage: [hr][F] weights, then [rcap][F] h rows of the item's expert
   const uint32_t wbytes = (uint32_t)hr * F * 2;
-  const uint32_t stage_bytes = wbytes + (uint32_t)kRC * F * 2;
+  const uint32_t stage_bytes = wbytes + (uint32_t)rcap * F * 2;
   uint8_t* stage_base = dsm_raw;
   if (threadIdx.x == 0) {
     for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
@@ -451,7 +580,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
     const int s = j % stages;
     const uint32_t bar = smem_u32(&full[s]);
     const int r0 = sm_off[e];
-    const int rc = min(kRC, sm_off[e + 1] - r0);
+    const int rc = min(rcap, sm_off[e + 1] - r0);
     const uint32_t hbytes = (uint32_t)rc * F * 2;
     const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
     mbar_expect_tx(bar, bytes + hbytes);
@@ -469,10 +598,10 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
     if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, s_abort, ws.err)) break;
     const uint4* wsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
-    for (int c0 = 0; c0 < cnt; c0 += kRC) {
-      const int rc = min(kRC, cnt - c0);
+    for (int c0 = 0; c0 < cnt; c0 += rcap) {
+      const int rc = min(rcap, cnt - c0);
       uint4* hr8 = reinterpret_cast<uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
-      if (c0 > 0) {  // more than kRC rows: later chunks are loaded into the same area
+      if (c0 > 0) {  // more than rcap rows: later chunks are loaded into the same area
         for (int i = threadIdx.x; i < rc * fv; i += kThreads)
           hr8[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
         __syncthreads();
@@ -530,7 +659,8 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
 }
 
 __global__ void __launch_bounds__(kThreads)
-decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int stages, DecodeWs ws) {
+decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int rcap, int stages,
+                   DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full[4];
   __shared__ int s_abort;
@@ -540,7 +670,7 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   const Meta m = load_meta(ws, 1, E, m_off, m_act, &m_nact, m_tok, m_w);
-  down_body(w_down, H, F, E, hr, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
+  down_body(w_down, H, F, E, hr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
 }
 
 // --------------------------------------------------------------- combine --
@@ -564,9 +694,8 @@ decode_combine_kernel(int T, int H, int k, TY* __restrict__ y, DecodeWs ws) {
 }
 
 // ---------------------------------------------------------- fused kernel --
-// All five phases in one cooperative launch (every block resident): phases
-// are separated by a grid barrier, so the decode step pays one launch and
-// no inter-kernel gaps.  The barrier spins on a counter for at most ~2 s; on
+// All phases in one cooperative launch (every block resident), separated by
+// grid barriers, so the decode step pays one launch and no inter-kernel gaps.  The barrier spins on a counter for at most ~2 s; on
 // expiry it records FRANK_ETIMEOUT and lets the kernel run to its end.
 __device__ __forceinline__ void grid_barrier(unsigned* counter, unsigned target, int* s_abort, int32_t* err) {
   asm volatile("fence.proxy.async.global;" ::: "memory");  // generic writes before later bulk reads
@@ -595,32 +724,57 @@ __device__ __forceinline__ void grid_barrier(unsigned* counter, unsigned target,
   __syncthreads();
 }
 
+// Dynamic shared memory of the fused kernel's routing phases: prob [T][E]
+// f32, the block's top-k weights / ids [kMaxSlots], the permute scratch.
+size_t fused_routing_smem(int64_t T, int64_t E) {
+  return (size_t)((T * E * 4 + 15) / 16) * 16 + (sizeof(float) + sizeof(int32_t)) * kMaxSlots + kFinalizeSmem;
+}
+struct FusedRoutingSmem {
+  float* prob;
+  float* w;
+  int32_t* ids;
+  uint8_t* scratch;
+};
+__device__ __forceinline__ FusedRoutingSmem carve_fused_routing(uint8_t* base, int T, int E) {
+  FusedRoutingSmem r;
+  r.prob = reinterpret_cast<float*>(base);
+  r.w = reinterpret_cast<float*>(base + (((size_t)T * E * 4 + 15) / 16) * 16);
+  r.ids = reinterpret_cast<int32_t*>(r.w + kMaxSlots);
+  r.scratch = reinterpret_cast<uint8_t*>(r.ids + kMaxSlots);
+  return r;
+}
+
 template <class TW, class TY>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr,
                     const __nv_bfloat16* __restrict__ w_gate, const __nv_bfloat16* __restrict__ w_up,
                     const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int normalize,
-                    int fr, int stages_gu, int hr, int stages_dn, TY* __restrict__ y, DecodeWs ws) {
+                    int fr, int stages_gu, int hr, int stages_dn, int rcap, TY* __restrict__ y, DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full_gu[4], full_dn[4];
   __shared__ int s_abort;
   if (threadIdx.x == 0) s_abort = 0;
   const int bid = blockIdx.x, nblk = gridDim.x;
-  route_body<TW>(x, wr, T, H, E, ws, bid * kWarps + (threadIdx.x >> 5), nblk * kWarps);
+  route_body<TW>(x, wr, T, H, E, ws, reinterpret_cast<float*>(dsm_raw), bid, nblk);
   grid_barrier(ws.gbar, 1u * nblk, &s_abort, ws.err);
-  topk_body(T, E, k, normalize, ws, reinterpret_cast<float*>(dsm_raw), bid * kWarps + (threadIdx.x >> 5),
-            nblk * kWarps);
-  grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
-  // every block builds the (small) permutation itself, so the streaming
-  // phases start without another barrier; block 0 also publishes it
+  // every block runs softmax / top-k for all T tokens and builds the (small)
+  // permutation itself, so the streaming phases start without another
+  // barrier; block 0 also publishes the routing
+  const FusedRoutingSmem rs = carve_fused_routing(dsm_raw, T, E);
+  block_softmax_topk(ws.logits, T, E, k, normalize, rs.prob, rs.w, rs.ids);
+  if (bid == 0)
+    for (int i = threadIdx.x; i < k * T; i += kThreads) {
+      ws.w[i] = rs.w[i];
+      ws.ids[i] = rs.ids[i];
+    }
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   const Meta m{m_off, m_act, &m_nact, m_tok, m_w};
-  permute_body(T, E, k, ws, dsm_raw, m, bid == 0);
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort, m);
+  permute_body(T, E, k, ws, rs.scratch, m, rs.ids, rs.w, bid == 0);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort, m);
+  grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
+  down_body(w_down, H, F, E, hr, rcap, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort, m);
   grid_barrier(ws.gbar, 3u * nblk, &s_abort, ws.err);
-  down_body(w_down, H, F, E, hr, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort, m);
-  grid_barrier(ws.gbar, 4u * nblk, &s_abort, ws.err);
   combine_body<TY>(T, H, k, y, ws, (int64_t)bid * kThreads + threadIdx.x, (int64_t)nblk * kThreads);
 }
 
@@ -643,7 +797,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 template <class TW, class TY>
 int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, const void* wd, int64_t T, int64_t H,
                  int64_t F, int64_t E, int64_t k, int normalize, int fr, int stages_gu, int hr, int stages_dn,
-                 void* y, const DecodeWs& ws, size_t smem, cudaStream_t st) {
+                 int rcap, void* y, const DecodeWs& ws, size_t smem, cudaStream_t st) {
   auto kern = decode_fused_kernel<TW, TY>;
   FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
@@ -664,9 +818,45 @@ int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, 
   cfg.numAttrs = 1;
   FRANK_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)x, (const TW*)wr, (const __nv_bfloat16*)wg,
                                     (const __nv_bfloat16*)wu, (const __nv_bfloat16*)wd, (int)T, (int)H, (int)F,
-                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn, (TY*)y, ws));
+                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn, rcap, (TY*)y, ws));
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
+}
+
+// Shared-memory staging of the two streaming phases.  An expert receives at
+// most T rows (the top-k ids of a token are distinct), so a stage holds
+// rcap = min(kRC, T) token rows beside its weights.  Rows per item start at
+// 32 KB of each gate/up matrix and 48 KB of down and halve until two stages
+// fit; a shape where even one row does not leaves the decode path.
+struct DecodePlan {
+  int rcap, fr, hr, stages_gu, stages_dn;
+  size_t stage_gu, stage_dn;
+  bool ok;
+};
+
+DecodePlan decode_plan(int64_t T, int64_t H, int64_t F) {
+  // dynamic shared memory beside the kernels' static tables (< 8 KB)
+  constexpr size_t kSmemDyn = 227 * 1024 - 8 * 1024;
+  DecodePlan p{};
+  p.rcap = (int)(T < kRC ? T : kRC);
+  p.fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
+  p.hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
+  for (;;) {
+    p.stage_gu = (size_t)2 * p.fr * H * 2 + (size_t)p.rcap * H * 2;
+    p.stages_gu = (int)(kSmemDyn / p.stage_gu);
+    if (p.stages_gu >= 2 || p.fr == 1) break;
+    p.fr /= 2;
+  }
+  for (;;) {
+    p.stage_dn = (size_t)p.hr * F * 2 + (size_t)p.rcap * F * 2;
+    p.stages_dn = (int)(kSmemDyn / p.stage_dn);
+    if (p.stages_dn >= 2 || p.hr == 1) break;
+    p.hr /= 2;
+  }
+  p.stages_gu = p.stages_gu > 4 ? 4 : p.stages_gu;
+  p.stages_dn = p.stages_dn > 4 ? 4 : p.stages_dn;
+  p.ok = p.stages_gu >= 2 && p.stages_dn >= 2;
+  return p;
 }
 
 }  // namespace
@@ -675,7 +865,7 @@ namespace frank {
 
 bool decode_path_ok(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
   return dtype == FRANK_BF16 && T >= 1 && T <= 64 && k * T <= kMaxSlots && E <= kMaxE && H % 8 == 0 && F % 8 == 0 &&
-         H <= 4096 && F <= 8192 && k * T <= E;
+         k * T <= E && decode_plan(T, H, F).ok;
 }
 
 size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
@@ -727,48 +917,41 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.gbar = c.take<unsigned>(1);
   ws.n_slots = (int)n;
   ws.err = device_error_word();
-  const int fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
-  const size_t stage_gu = (size_t)2 * fr * H * 2 + (size_t)kRC * H * 2;
-  const int hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
-  const size_t stage_dn = (size_t)hr * F * 2 + (size_t)kRC * F * 2;
-  const size_t kSmemMax = 227 * 1024;
-  int stages_gu = (int)((kSmemMax - 16 * 1024) / stage_gu);
-  stages_gu = stages_gu > 4 ? 4 : stages_gu;
-  int stages_dn = (int)((kSmemMax - 16 * 1024) / stage_dn);
-  stages_dn = stages_dn > 4 ? 4 : stages_dn;
-  if (stages_gu < 2 || stages_dn < 2) {
+  const DecodePlan plan = decode_plan(T, H, F);
+  if (!plan.ok) {
     set_error("decode block: n_embd=%lld / n_ff=%lld too large for the streaming kernels", (long long)H,
               (long long)F);
     return FRANK_EINVAL;
   }
+  const int rcap = plan.rcap, fr = plan.fr, hr = plan.hr, stages_gu = plan.stages_gu, stages_dn = plan.stages_dn;
+  const size_t stage_gu = plan.stage_gu, stage_dn = plan.stage_dn;
   const char* fenv = getenv("FRANK_DECODE_FUSED");
   if (!(fenv && fenv[0] == '0')) {
     // one cooperative launch (decode_fused_kernel)
     size_t smem = stages_gu * stage_gu;
     if (stages_dn * stage_dn > smem) smem = stages_dn * stage_dn;
-    if (kFinalizeSmem > smem) smem = kFinalizeSmem;
+    if (fused_routing_smem(T, E) > smem) smem = fused_routing_smem(T, E);
     mark(0, st);
     FRANK_CUDA_TRY(cudaMemsetAsync(ws.gbar, 0, sizeof(unsigned), st));
     int st_launch;
     if (wr_dtype == FRANK_F32 && y_dtype == FRANK_F32)
       st_launch = launch_fused<float, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
-                                             stages_gu, hr, stages_dn, y, ws, smem, st);
+                                             stages_gu, hr, stages_dn, rcap, y, ws, smem, st);
     else if (wr_dtype == FRANK_F32)
       st_launch = launch_fused<float, __nv_bfloat16>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
-                                                     stages_gu, hr, stages_dn, y, ws, smem, st);
+                                                     stages_gu, hr, stages_dn, rcap, y, ws, smem, st);
     else if (y_dtype == FRANK_F32)
       st_launch = launch_fused<__nv_bfloat16, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
-                                                     stages_gu, hr, stages_dn, y, ws, smem, st);
+                                                     stages_gu, hr, stages_dn, rcap, y, ws, smem, st);
     else
       st_launch = launch_fused<__nv_bfloat16, __nv_bfloat16>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k,
-                                                             normalize, fr, stages_gu, hr, stages_dn, y, ws, smem,
-                                                             st);
+                                                             normalize, fr, stages_gu, hr, stages_dn, rcap, y, ws,
+                                                             smem, st);
     FRANK_TRY(st_launch);
     for (int m = 1; m <= 6; ++m) mark(m, st);
   } else {
   mark(0, st);
-  const int64_t items = E * ((T + kRouteTok - 1) / kRouteTok);
-  const unsigned rblocks = (unsigned)((items + kWarps - 1) / kWarps);
+  const unsigned rblocks = (unsigned)num_sms();
   if (wr_dtype == FRANK_F32)
     decode_route_kernel<float><<<rblocks, kThreads, 0, st>>>((const __nv_bfloat16*)x, (const float*)wr, (int)T,
                                                              (int)H, (int)E, (int)k, normalize, ws);
@@ -776,7 +959,10 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
     decode_route_kernel<__nv_bfloat16><<<rblocks, kThreads, 0, st>>>(
         (const __nv_bfloat16*)x, (const __nv_bfloat16*)wr, (int)T, (int)H, (int)E, (int)k, normalize, ws);
   FRANK_LAUNCH_CHECK();
-  FRANK_CUDA_TRY(launch_pdl(decode_finalize_kernel, dim3(1), dim3(kThreads), 0, st, (int)T, (int)E, (int)k,
+  const size_t prob_smem = (size_t)T * E * sizeof(float);
+  FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                      (int)prob_smem));
+  FRANK_CUDA_TRY(launch_pdl(decode_finalize_kernel, dim3(1), dim3(kThreads), prob_smem, st, (int)T, (int)E, (int)k,
                             normalize, ws));
   FRANK_LAUNCH_CHECK();
   mark(1, st);
@@ -784,37 +970,21 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   mark(3, st);
   ws.err = device_error_word();
   const int grid_p = num_sms();
-  const size_t kSmemMax = 227 * 1024;
   {
-    const int fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
-    const size_t stage = (size_t)2 * fr * H * 2 + (size_t)kRC * H * 2;
-    int stages = (int)((kSmemMax - 16 * 1024) / stage);
-    stages = stages > 4 ? 4 : stages;
-    if (stages < 2) {
-      set_error("decode block: n_embd=%lld too large for the streaming kernel", (long long)H);
-      return FRANK_EINVAL;
-    }
-    const size_t smem = stages * stage;
+    const size_t smem = stages_gu * stage_gu;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kThreads), smem, st,
                               (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
-                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, (int)E, fr, stages, ws));
+                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, (int)E, fr, rcap, stages_gu,
+                              ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(4, st);
   {
-    const int hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
-    const size_t stage = (size_t)hr * F * 2 + (size_t)kRC * F * 2;
-    int stages = (int)((kSmemMax - 4 * 1024) / stage);
-    stages = stages > 4 ? 4 : stages;
-    if (stages < 2) {
-      set_error("decode block: n_ff=%lld too large for the streaming kernel", (long long)F);
-      return FRANK_EINVAL;
-    }
-    const size_t smem = stages * stage;
+    const size_t smem = stages_dn * stage_dn;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     FRANK_CUDA_TRY(launch_pdl(decode_down_kernel, dim3(grid_p), dim3(kThreads), smem, st,
-                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, (int)E, hr, stages, ws));
+                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, (int)E, hr, rcap, stages_dn, ws));
     FRANK_LAUNCH_CHECK();
   }
   mark(5, st);
