@@ -327,6 +327,11 @@ def run_frank(args, cfg):
     x_host = x.cpu().pin_memory()
     y_host = torch.empty((cfg.T, cfg.H), dtype=torch.float32).pin_memory()
     x_dev = torch.empty_like(x)
+    pipe = None
+    if graphed is None and cfg.T >= 1024:
+        del y
+        torch.cuda.empty_cache()
+        pipe = ops.HostPipeline(e2e_call, cfg.T, cfg.H, x.dtype, torch.float32, depth=2, device=dev)
 
     def e2e_step(last):
         if graphed is not None or cfg.T < 1024:
@@ -335,10 +340,10 @@ def run_frank(args, cfg):
             e2e_call(x_dev, out=y)
             y_host.copy_(y, non_blocking=True)
         else:
-            # public host-buffer API: chunked H2D / block / D2H on three streams;
-            # a step's copies out overlap the next step, the last is waited for
-            done = ops.moe_ffn_host(e2e_call, x_host, y_host, chunks=4, x_dev=x_dev, y_dev=y,
-                                    order_copy_out=False)
+            # public host-buffer API: every step copies its tokens in and its
+            # result out; the copies of neighbouring steps overlap this
+            # step's block on separate streams; the last copy out is waited for
+            done = pipe.submit(x_host, y_host)
             if last:
                 stream.wait_event(done)
 

@@ -316,6 +316,68 @@ def moe_ffn_host(block, x_host: torch.Tensor, y_host: torch.Tensor, chunks: int 
     return done
 
 
+class HostPipeline:
+    """Streams batches of host-resident tokens through ``block`` (a
+    :class:`MoEFFNBlock`, or any callable ``block(x, out=y)``) with copies in
+    and out overlapping the neighbouring batches' compute.
+
+    ``submit(x_host, y_host)`` enqueues, for one batch: the host-to-device
+    copy of x_host [T, H] into one of ``depth`` device slots (on a copy
+    stream, once the block call that last read the slot is done), the block
+    on the current stream, and the device-to-host copy into y_host (on a
+    second copy stream).  Batch i+1's input copy therefore runs during batch
+    i's block, and batch i's output copy during batch i+1's block; every
+    batch still moves its own inputs and result across PCIe.  Returns a CUDA
+    event that completes when y_host is written.  Pinned host tensors only;
+    no host synchronisation.  The result of each batch equals one block call
+    on the same tokens, bit for bit."""
+
+    def __init__(self, block, T: int, H: int, x_dtype: torch.dtype, y_dtype: torch.dtype = torch.float32,
+                 depth: int = 2, device=None):
+        dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.block = block
+        self.T, self.H = int(T), int(H)
+        self.depth = int(depth)
+        if self.depth < 1:
+            raise ValueError("HostPipeline: depth must be >= 1")
+        self.x = [torch.empty((T, H), dtype=x_dtype, device=dev) for _ in range(self.depth)]
+        self.y = [torch.empty((T, H), dtype=y_dtype, device=dev) for _ in range(self.depth)]
+        self._computed = [None] * self.depth  # block done reading x[b] / writing y[b]
+        self._copied_out = [None] * self.depth  # y[b] copied to the host
+        self._n = 0
+        self.device = dev
+
+    def submit(self, x_host: torch.Tensor, y_host: torch.Tensor) -> torch.cuda.Event:
+        if not (x_host.is_pinned() and y_host.is_pinned()):
+            raise ValueError("HostPipeline.submit: x_host and y_host must be pinned host tensors")
+        if tuple(x_host.shape) != (self.T, self.H) or tuple(y_host.shape) != (self.T, self.H):
+            raise ValueError(f"HostPipeline.submit: expected [{self.T}, {self.H}] host tensors")
+        b = self._n % self.depth
+        self._n += 1
+        compute = torch.cuda.current_stream(self.device)
+        s_in, s_out = _host_streams(self.device)
+        with torch.cuda.stream(s_in):
+            if self._computed[b] is not None:
+                s_in.wait_event(self._computed[b])
+            self.x[b].copy_(x_host, non_blocking=True)
+            copied_in = torch.cuda.Event()
+            copied_in.record(s_in)
+        compute.wait_event(copied_in)
+        if self._copied_out[b] is not None:
+            compute.wait_event(self._copied_out[b])
+        self.block(self.x[b], out=self.y[b])
+        computed = torch.cuda.Event()
+        computed.record(compute)
+        self._computed[b] = computed
+        with torch.cuda.stream(s_out):
+            s_out.wait_event(computed)
+            y_host.copy_(self.y[b], non_blocking=True)
+            done = torch.cuda.Event()
+            done.record(s_out)
+        self._copied_out[b] = done
+        return done
+
+
 _HOST_STREAMS: dict = {}
 
 

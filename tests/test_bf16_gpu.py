@@ -141,3 +141,24 @@ def test_host_pipeline_equals_device_call():
         ops.moe_ffn_host(block, x_host, y_host, chunks=chunks)
         torch.cuda.synchronize()
         assert torch.equal(y_host, ref.cpu())
+
+
+@pytest.mark.parametrize("depth", [1, 2, 3])
+def test_host_pipeline_batches_equal_device_calls(depth):
+    """ops.HostPipeline: a stream of different batches, copies of neighbouring
+    batches overlapping compute, each equal bit for bit to one device call;
+    host buffers reused across batches once their event completed."""
+    cfg = configs.BlockConfig("host_stream", T=700, H=512, F=256, E=16, k=4, normalize=False, dtype="bf16")
+    _, wr, wu, wg, wd = configs.block_inputs_numpy(cfg, seed=6)
+    block = ops.MoEFFNBlock(torch.from_numpy(wr).cuda(), *(_bf16(w) for w in (wu, wg, wd)), cfg.E, cfg.k, False)
+    pipe = ops.HostPipeline(block, cfg.T, cfg.H, torch.bfloat16, depth=depth)
+    n_batches = 7
+    xs = [torch.randn(cfg.T, cfg.H, generator=torch.Generator().manual_seed(i)).bfloat16().pin_memory()
+          for i in range(n_batches)]
+    refs = [block(x.cuda()).cpu() for x in xs]
+    ys = [torch.empty((cfg.T, cfg.H), dtype=torch.float32).pin_memory() for _ in range(n_batches)]
+    events = [pipe.submit(xs[i], ys[i]) for i in range(n_batches)]
+    for i in range(n_batches):
+        events[i].synchronize()
+        assert torch.equal(ys[i], refs[i]), f"batch {i}"
+    assert ops.read_device_error() == 0
