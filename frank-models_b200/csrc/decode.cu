@@ -75,6 +75,7 @@ struct DecodeWs {
   float* d;             // [k*T, H] down output x gate weight
   int32_t* err;         // device error word (bounded waits)
   unsigned* gbar;       // grid-barrier counter of the fused kernel (zeroed per call)
+  const float* res;     // optional fp32 [T, H] residual added to y (may alias y)
   int n_slots;          // k * T
 };
 
@@ -676,19 +677,20 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
 // --------------------------------------------------------------- combine --
 // y[t, h] = sum_{j<k} d[slot_pos[j*T + t], h] in slot order (deterministic).
 template <class TY>
-__device__ __forceinline__ void combine_body(int T, int H, int k, TY* __restrict__ y, const DecodeWs& ws, int64_t gtid,
+__device__ __forceinline__ void combine_body(int T, int H, int k, TY* y, const DecodeWs& ws, int64_t gtid,
                                              int64_t nthreads) {
   for (int64_t i = gtid; i < (int64_t)T * H; i += nthreads) {
     const int t = (int)(i / H), h = (int)(i - (int64_t)t * H);
     float acc = 0.f;
     for (int j = 0; j < k; ++j) acc += __ldcg(ws.d + (int64_t)__ldcg(ws.slot_pos + j * T + t) * H + h);
+    if (ws.res) acc = ws.res[i] + acc;  // the sub-layer's residual add after the sum
     y[i] = from_f32<TY>(acc);
   }
 }
 
 template <class TY>
 __global__ void __launch_bounds__(kThreads)
-decode_combine_kernel(int T, int H, int k, TY* __restrict__ y, DecodeWs ws) {
+decode_combine_kernel(int T, int H, int k, TY* y, DecodeWs ws) {
   wait_prior_grid();
   combine_body<TY>(T, H, k, y, ws, (int64_t)blockIdx.x * kThreads + threadIdx.x, (int64_t)gridDim.x * kThreads);
 }
@@ -749,7 +751,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr,
                     const __nv_bfloat16* __restrict__ w_gate, const __nv_bfloat16* __restrict__ w_up,
                     const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int normalize,
-                    int fr, int stages_gu, int hr, int stages_dn, int rcap, TY* __restrict__ y, DecodeWs ws) {
+                    int fr, int stages_gu, int hr, int stages_dn, int rcap, TY* y, DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full_gu[4], full_dn[4];
   __shared__ int s_abort;
@@ -890,7 +892,7 @@ size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t
 int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void* w_up_p, const void* w_gate_p,
                         const void* w_down_p, int64_t T, int64_t E, int64_t k, int64_t H, int64_t F, int normalize,
                         int y_dtype, void* y, float* route_w, int32_t* route_ids, void* workspace, size_t ws_bytes,
-                        cudaStream_t st, void (*mark)(int, cudaStream_t)) {
+                        cudaStream_t st, void (*mark)(int, cudaStream_t), const float* residual) {
   if (ws_bytes < decode_workspace_size(T, H, F, E, k)) {
     set_error("decode block: workspace %zu < %zu", ws_bytes, decode_workspace_size(T, H, F, E, k));
     return FRANK_ENOSPC;
@@ -915,6 +917,7 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.nactive = c.take<int32_t>(1);
   ws.d = c.take<float>(n * H);
   ws.gbar = c.take<unsigned>(1);
+  ws.res = residual;
   ws.n_slots = (int)n;
   ws.err = device_error_word();
   const DecodePlan plan = decode_plan(T, H, F);

@@ -111,10 +111,13 @@ __global__ void scatter_out_kernel(const float* __restrict__ ys, const int32_t* 
 // y[t, :] = sum_{j=0..k-1} d[slot_pos[j*T + t], :]   (moe_ffn_block.mlir:179-206,
 // oracles/moe.py:126-132).  The gate weight was already applied by the down
 // GEMM epilogue.  Fixed j order, no atomics: deterministic.  4 floats per
-// thread; the store is a 16-byte (fp32) or 8-byte (bf16) vector.
+// thread; the store is a 16-byte (fp32) or 8-byte (bf16) vector.  With a
+// residual (fp32 [T, H], may alias y) the sub-layer's residual add follows
+// the sum: y = residual + sum (transformer_layer_moe_prefill.mlir:227-245,
+// oracles/transformer_layer.py:123).
 template <class TY>
 __global__ void combine_kernel(const float* __restrict__ d, const int32_t* __restrict__ slot_pos, int64_t T,
-                               int k, int64_t H, TY* __restrict__ y) {
+                               int k, int64_t H, TY* y, const float* res) {
   const int64_t t = blockIdx.y;
   const int64_t h = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (h >= H) return;
@@ -123,6 +126,10 @@ __global__ void combine_kernel(const float* __restrict__ d, const int32_t* __res
     int64_t r = slot_pos[(int64_t)j * T + t];
     float4 v = *reinterpret_cast<const float4*>(d + r * H + h);
     acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+  }
+  if (res) {
+    const float4 rv = *reinterpret_cast<const float4*>(res + t * H + h);
+    acc.x = rv.x + acc.x; acc.y = rv.y + acc.y; acc.z = rv.z + acc.z; acc.w = rv.w + acc.w;
   }
   if constexpr (sizeof(TY) == 4) {
     *reinterpret_cast<float4*>(reinterpret_cast<float*>(y) + t * H + h) = acc;
@@ -136,11 +143,12 @@ __global__ void combine_kernel(const float* __restrict__ d, const int32_t* __res
 
 template <class TY>
 __global__ void combine_scalar_kernel(const float* __restrict__ d, const int32_t* __restrict__ slot_pos,
-                                      int64_t T, int k, int64_t H, TY* __restrict__ y) {
+                                      int64_t T, int k, int64_t H, TY* y, const float* res) {
   const int64_t t = blockIdx.y;
   for (int64_t h = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; h < H; h += (int64_t)gridDim.x * blockDim.x) {
     float acc = 0.f;
     for (int j = 0; j < k; ++j) acc += d[(int64_t)slot_pos[(int64_t)j * T + t] * H + h];
+    if (res) acc = res[t * H + h] + acc;
     y[t * H + h] = from_f32<TY>(acc);
   }
 }
@@ -198,6 +206,40 @@ unsigned grid_1d(int64_t n, int threads) {
   int64_t b = (n + threads - 1) / threads;
   int64_t cap = (int64_t)frank::num_sms() * 16;
   return (unsigned)(b < cap ? (b < 1 ? 1 : b) : cap);
+}
+
+// ------------------------------------------------------------- rms_norm --
+// out[t, :] = (x[t, :] / sqrt(mean(x[t, :]^2) + eps)) * w   in fp32, rounded to
+// the output type (components/normalization/rms_norm.mlir:18-80,
+// oracles/normalization.py:10-43): sum of squares (fused multiply-adds,
+// lane partials then a warp tree), divide by H, add eps, sqrt, divide x by
+// it, scale by the weight -- the reference's steps, IEEE division and square
+// root.  One warp per row; 16-byte loads when H % 4 == 0.
+template <class TO>
+__global__ void rms_norm_kernel(const float* __restrict__ x, const float* __restrict__ w, int64_t T, int64_t H,
+                                float eps, TO* __restrict__ out) {
+  const int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= T) return;
+  const float* xr = x + t * H;
+  float ss = 0.f;
+  const bool vec = (H % 4 == 0) && ((uintptr_t)xr % 16 == 0);
+  if (vec) {
+    for (int64_t h = (int64_t)lane * 4; h < H; h += 128) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + h);
+      ss = fmaf(v.x, v.x, ss);
+      ss = fmaf(v.y, v.y, ss);
+      ss = fmaf(v.z, v.z, ss);
+      ss = fmaf(v.w, v.w, ss);
+    }
+  } else {
+    for (int64_t h = lane; h < H; h += 32) ss = fmaf(xr[h], xr[h], ss);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float rms = sqrtf(ss / (float)H + eps);
+  TO* orow = out + t * H;
+  for (int64_t h = lane; h < H; h += 32) orow[h] = from_f32<TO>((xr[h] / rms) * w[h]);
 }
 
 }  // namespace
@@ -289,10 +331,10 @@ int launch_scatter_out(const float* ys, const int32_t* slot_pos, int64_t n_slots
 }
 
 int launch_combine(int dtype, const float* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H, void* y,
-                   cudaStream_t st) {
+                   cudaStream_t st, const float* residual) {
   if (T == 0 || H == 0) return FRANK_OK;
   bool vec_ok = (H % 4 == 0) && ((uintptr_t)d % 16 == 0) &&
-                ((uintptr_t)y % (dtype == FRANK_F32 ? 16 : 8) == 0);
+                ((uintptr_t)y % (dtype == FRANK_F32 ? 16 : 8) == 0) && ((uintptr_t)residual % 16 == 0);
   for (int64_t t0 = 0; t0 < T; t0 += 65535) {
     int64_t tn = (T - t0) < 65535 ? (T - t0) : 65535;
     // Offsetting y and slot_pos by t0 keeps each launch within grid.y limits;
@@ -300,17 +342,21 @@ int launch_combine(int dtype, const float* d, const int32_t* slot_pos, int64_t T
     if (vec_ok) {
       dim3 grid((unsigned)((H / 4 + 127) / 128), (unsigned)tn);
       if (dtype == FRANK_F32)
-        combine_kernel<float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H);
+        combine_kernel<float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H,
+                                                    residual ? residual + t0 * H : nullptr);
       else
         combine_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H,
-                                                            (__nv_bfloat16*)y + t0 * H);
+                                                            (__nv_bfloat16*)y + t0 * H,
+                                                            residual ? residual + t0 * H : nullptr);
     } else {
       dim3 grid((unsigned)((H + 127) / 128 < 64 ? (H + 127) / 128 : 64), (unsigned)tn);
       if (dtype == FRANK_F32)
-        combine_scalar_kernel<float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H);
+        combine_scalar_kernel<float><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H, (float*)y + t0 * H,
+                                                           residual ? residual + t0 * H : nullptr);
       else
         combine_scalar_kernel<__nv_bfloat16><<<grid, 128, 0, st>>>(d, slot_pos + t0, T, (int)k, H,
-                                                                   (__nv_bfloat16*)y + t0 * H);
+                                                                   (__nv_bfloat16*)y + t0 * H,
+                                                                   residual ? residual + t0 * H : nullptr);
     }
     FRANK_LAUNCH_CHECK();
   }
@@ -343,6 +389,18 @@ int launch_copy_row_segments(const void* src, void* dst, const int64_t* src_star
 int launch_sorted_weights(const float* w, const int32_t* sorted_slots, int64_t n, float* ws, cudaStream_t st) {
   if (n == 0) return FRANK_OK;
   sorted_weights_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(w, sorted_slots, n, ws);
+  FRANK_LAUNCH_CHECK();
+  return FRANK_OK;
+}
+
+int launch_rms_norm(const float* x, const float* w, int64_t T, int64_t H, float eps, int out_dtype, void* out,
+                    cudaStream_t st) {
+  if (T == 0) return FRANK_OK;
+  const unsigned blocks = (unsigned)((T + 3) / 4);
+  if (out_dtype == FRANK_F32)
+    rms_norm_kernel<float><<<blocks, 128, 0, st>>>(x, w, T, H, eps, (float*)out);
+  else
+    rms_norm_kernel<__nv_bfloat16><<<blocks, 128, 0, st>>>(x, w, T, H, eps, (__nv_bfloat16*)out);
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
 }

@@ -22,7 +22,9 @@ int launch_prepack(int, const void*, int64_t, int64_t, int64_t, int, void*, cuda
 int launch_gather_rows(int, const void*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
 int launch_gather_cols(int, const void*, const int32_t*, int64_t, int64_t, void*, cudaStream_t);
 int launch_scatter_out(const float*, const int32_t*, int64_t, int64_t, float*, cudaStream_t);
-int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
+int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t,
+                   const float* residual = nullptr);
+int launch_rms_norm(const float*, const float*, int64_t, int64_t, float, int, void*, cudaStream_t);
 int launch_sorted_weights(const float*, const int32_t*, int64_t, float*, cudaStream_t);
 int launch_copy_row_segments(const void*, void*, const int64_t*, const int64_t*, const int64_t*, int64_t, int64_t,
                              int64_t, cudaStream_t);
@@ -36,7 +38,7 @@ bool decode_path_ok(int, int64_t, int64_t, int64_t, int64_t, int64_t);
 size_t decode_workspace_size(int64_t, int64_t, int64_t, int64_t, int64_t);
 int launch_decode_block(const void*, int, const void*, const void*, const void*, const void*, int64_t, int64_t,
                         int64_t, int64_t, int64_t, int, int, void*, float*, int32_t*, void*, size_t, cudaStream_t,
-                        void (*)(int, cudaStream_t));
+                        void (*)(int, cudaStream_t), const float* residual);
 
 // ---- error state ----
 static thread_local std::string g_err;
@@ -296,10 +298,14 @@ size_t frank_moe_ffn_block_workspace_size(int dtype, int64_t T, int64_t H, int64
   return moe_layout(dtype, T, H, F, E, k, nullptr, 0, nullptr);
 }
 
-int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, const void* w_up_p,
-                        const void* w_gate_p, const void* w_down_p, int64_t T, int64_t E, int64_t k, int64_t H,
-                        int64_t F, int normalize, int y_dtype, void* y, float* route_w, int32_t* route_ids, void* workspace,
-                        size_t ws_bytes, void* stream) {
+namespace {
+
+// The block (see frank_moe_ffn_block); residual: optional fp32 [T, H] added
+// to y after the sum over the k slots (the sub-layer's residual connection).
+int moe_block(int dtype, const void* x, int wr_dtype, const void* wr, const void* w_up_p, const void* w_gate_p,
+              const void* w_down_p, int64_t T, int64_t E, int64_t k, int64_t H, int64_t F, int normalize, int y_dtype,
+              void* y, float* route_w, int32_t* route_ids, void* workspace, size_t ws_bytes, cudaStream_t st,
+              const float* residual) {
   FRANK_TRY(check_dtype(dtype, "moe_ffn_block"));
   FRANK_TRY(check_dtype(wr_dtype, "moe_ffn_block"));
   FRANK_TRY(check_dtype(y_dtype, "moe_ffn_block"));
@@ -308,7 +314,6 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
                   (long long)k);
   FRANK_CHECK_ARG(T >= 0 && H >= 1 && F >= 1, "moe_ffn_block: bad T=%lld H=%lld F=%lld", (long long)T, (long long)H,
                   (long long)F);
-  cudaStream_t st = as_stream(stream);
   if (T == 0) return FRANK_OK;
   const int64_t n = k * T;
   if (dtype == FRANK_BF16) {
@@ -319,7 +324,7 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
   if (decode_path_ok(dtype, T, H, F, E, k)) {
     // a few tokens: weight-streaming decode kernels (csrc/decode.cu)
     return launch_decode_block(x, wr_dtype, wr, w_up_p, w_gate_p, w_down_p, T, E, k, H, F, normalize, y_dtype, y,
-                               route_w, route_ids, workspace, ws_bytes, st, prof_mark);
+                               route_w, route_ids, workspace, ws_bytes, st, prof_mark, residual);
   }
   size_t need = moe_layout(dtype, T, H, F, E, k, nullptr, 0, nullptr);
   if (ws_bytes < need) {
@@ -356,9 +361,53 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, 
   }
   prof_mark(5, st);
   // 6. y[t] = sum_j d[slot j of t]                   :179-206
-  FRANK_TRY(launch_combine(y_dtype, L.ds, L.slot_pos, T, k, H, y, st));
+  FRANK_TRY(launch_combine(y_dtype, L.ds, L.slot_pos, T, k, H, y, st, residual));
   prof_mark(6, st);
   return FRANK_OK;
+}
+
+}  // namespace
+
+int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr, const void* w_up_p,
+                        const void* w_gate_p, const void* w_down_p, int64_t T, int64_t E, int64_t k, int64_t H,
+                        int64_t F, int normalize, int y_dtype, void* y, float* route_w, int32_t* route_ids, void* workspace,
+                        size_t ws_bytes, void* stream) {
+  return moe_block(dtype, x, wr_dtype, wr, w_up_p, w_gate_p, w_down_p, T, E, k, H, F, normalize, y_dtype, y, route_w,
+                   route_ids, workspace, ws_bytes, as_stream(stream), nullptr);
+}
+
+int frank_rms_norm(const float* x, const float* weight, int64_t T, int64_t H, float eps, int out_dtype, void* out,
+                   void* stream) {
+  FRANK_TRY(check_dtype(out_dtype, "rms_norm"));
+  FRANK_CHECK_ARG(T >= 0 && H >= 1, "rms_norm: bad T=%lld H=%lld", (long long)T, (long long)H);
+  FRANK_CHECK_ARG(T == 0 || (x && weight && out), "rms_norm: null pointer");
+  return launch_rms_norm(x, weight, T, H, eps, out_dtype, out, as_stream(stream));
+}
+
+size_t frank_moe_ffn_sublayer_workspace_size(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
+  return align_up((size_t)T * H * (dtype == FRANK_F32 ? 4 : 2), 256) +
+         frank_moe_ffn_block_workspace_size(dtype, T, H, F, E, k);
+}
+
+int frank_moe_ffn_sublayer(int dtype, const float* residual, const float* norm_w, float eps, int wr_dtype,
+                           const void* wr, const void* w_up_p, const void* w_gate_p, const void* w_down_p, int64_t T,
+                           int64_t E, int64_t k, int64_t H, int64_t F, int normalize, float* out, float* route_w,
+                           int32_t* route_ids, void* workspace, size_t ws_bytes, void* stream) {
+  FRANK_TRY(check_dtype(dtype, "moe_ffn_sublayer"));
+  FRANK_CHECK_ARG(T >= 0 && H >= 1, "moe_ffn_sublayer: bad T=%lld H=%lld", (long long)T, (long long)H);
+  if (T == 0) return FRANK_OK;
+  FRANK_CHECK_ARG(residual && norm_w && out, "moe_ffn_sublayer: null pointer");
+  const size_t need = frank_moe_ffn_sublayer_workspace_size(dtype, T, H, F, E, k);
+  if (ws_bytes < need) {
+    set_error("moe_ffn_sublayer: workspace %zu < %zu bytes", ws_bytes, need);
+    return FRANK_ENOSPC;
+  }
+  cudaStream_t st = as_stream(stream);
+  const size_t xn_bytes = align_up((size_t)T * H * (dtype == FRANK_F32 ? 4 : 2), 256);
+  void* xn = workspace;
+  FRANK_TRY(launch_rms_norm(residual, norm_w, T, H, eps, dtype, xn, st));
+  return moe_block(dtype, xn, wr_dtype, wr, w_up_p, w_gate_p, w_down_p, T, E, k, H, F, normalize, FRANK_F32, out,
+                   route_w, route_ids, static_cast<char*>(workspace) + xn_bytes, ws_bytes - xn_bytes, st, residual);
 }
 
 int frank_gather_rows(int dtype, const void* x, const int32_t* sorted_slots, int64_t rows, int64_t T, int64_t H,

@@ -48,6 +48,11 @@ SIGNATURES = {
     "frank_moe_ffn_block_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
     "frank_moe_ffn_block": (_c_int, [_c_int, _c_vp, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64,
                                      _c_i64, _c_i64, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_size, _c_vp]),
+    "frank_rms_norm": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, ctypes.c_float, _c_int, _c_vp, _c_vp]),
+    "frank_moe_ffn_sublayer_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64]),
+    "frank_moe_ffn_sublayer": (_c_int, [_c_int, _c_vp, _c_vp, ctypes.c_float, _c_int, _c_vp, _c_vp, _c_vp, _c_vp,
+                                        _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_vp, _c_vp,
+                                        _c_size, _c_vp]),
     "frank_gather_rows": (_c_int, [_c_int, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp]),
     "frank_gather_weights": (_c_int, [_c_vp, _c_vp, _c_i64, _c_vp, _c_vp]),
     "frank_expert_ffn_workspace_size": (_c_size, [_c_int, _c_i64, _c_i64]),

@@ -76,6 +76,38 @@ class B200Module:
         y = block(x)
         return _host(y) if numpy_in else y
 
+    def rms_norm(self, input, weight, eps):
+        """@rms_norm_components.rms_norm_linalg(input [T, H], weight [H], eps)
+        (components/normalization/rms_norm.mlir:18-80) -> [T, H] float32."""
+        if _is_np(input, weight):
+            return _host(ops.rms_norm(_dev(input, np.float32, "input"), _dev(weight, np.float32, "weight"), eps))
+        return ops.rms_norm(input, weight, eps)
+
+    def moe_ffn_sublayer(self, residual, ffn_norm_w, rms_eps, gate_inp_w, up_exps_w, gate_exps_w, down_exps_w,
+                         n_expert, n_expert_used, n_embd, n_ff, normalize_weights):
+        """The MoE FFN sub-layer of the MoE transformer layer
+        (transformer_layer_moe_prefill.mlir:211-245, decode :228-256,
+        oracles/transformer_layer.py:107-124):
+        residual + moe_ffn_block(rms_norm(residual, ffn_norm_w, rms_eps), ...)
+        -> [T, n_embd] float32.  numpy in: fp32 FFMA path; torch CUDA in: the
+        block runs in the expert weights' dtype (bf16: tcgen05)."""
+        numpy_in = _is_np(residual, ffn_norm_w, gate_inp_w, up_exps_w, gate_exps_w, down_exps_w)
+        if numpy_in:
+            r = _dev(residual, np.float32, "residual")
+            nw = _dev(ffn_norm_w, np.float32, "ffn_norm_w")
+            wr = _dev(gate_inp_w, np.float32, "gate_inp_w")
+            wu, wg, wd = (ops.PackedExperts.from_reference(_dev(w, np.float32, name), torch.float32)
+                          for w, name in ((up_exps_w, "up_exps_w"), (gate_exps_w, "gate_exps_w"),
+                                          (down_exps_w, "down_exps_w")))
+            dtype = torch.float32
+        else:
+            r, nw, wr, wu, wg, wd = residual, ffn_norm_w, gate_inp_w, up_exps_w, gate_exps_w, down_exps_w
+            dtype = wu.packed.dtype if isinstance(wu, ops.PackedExperts) else wu.dtype
+        _check_block_shapes(r, wr, wu, wg, wd, n_expert, n_expert_used, n_embd, n_ff)
+        block = ops.MoEFFNBlock(wr, wu, wg, wd, n_expert, n_expert_used, normalize_weights, dtype=dtype)
+        y = block.sublayer(r, nw, rms_eps)
+        return _host(y) if numpy_in else y
+
 
 def _check_block_shapes(x, wr, wu, wg, wd, E, k, H, F):
     def shp(t):

@@ -242,8 +242,8 @@ class MoEFFNBlock:
     def workspace_bytes(self, T: int) -> int:
         return _lib.load().frank_moe_ffn_block_workspace_size(_DT[self.dtype], T, self.H, self.F, self.E, self.k)
 
-    def _workspace(self, T: int, device) -> torch.Tensor:
-        need = self.workspace_bytes(T)
+    def _workspace(self, T: int, device, need: int | None = None) -> torch.Tensor:
+        need = self.workspace_bytes(T) if need is None else need
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
             self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
         return self._ws
@@ -268,6 +268,57 @@ class MoEFFNBlock:
         if return_routing:
             return y, rw, rid
         return y
+
+    def sublayer(self, residual: torch.Tensor, ffn_norm_w: torch.Tensor, rms_eps: float,
+                 out: torch.Tensor | None = None, return_routing: bool = False):
+        """The MoE FFN sub-layer of the reference's MoE transformer layer
+        (transformer_layer_moe_prefill.mlir:211-245, oracles/transformer_layer.py:107-124):
+        ``residual + moe_ffn_block(rms_norm(residual, ffn_norm_w, rms_eps))``.
+        residual: fp32 [T, H] on the GPU; ffn_norm_w: fp32 [H].  The normalised
+        tokens are rounded to the block's compute dtype; the residual add is
+        fused into the final sum over the k slots.  ``out`` (fp32 [T, H]) may
+        be ``residual`` itself (in-place update)."""
+        residual = _cuda_contig(residual, "residual")
+        ffn_norm_w = _cuda_contig(ffn_norm_w, "ffn_norm_w")
+        if residual.dtype != torch.float32 or residual.dim() != 2 or residual.shape[1] != self.H:
+            raise ValueError(f"moe_ffn_sublayer: residual must be float32 [T, {self.H}], got {residual.dtype} "
+                             f"{tuple(residual.shape)}")
+        if ffn_norm_w.dtype != torch.float32 or tuple(ffn_norm_w.shape) != (self.H,):
+            raise ValueError(f"moe_ffn_sublayer: ffn_norm_w must be float32 [{self.H}]")
+        T = residual.shape[0]
+        if out is not None and (out.dtype != torch.float32 or tuple(out.shape) != (T, self.H)
+                                or not out.is_contiguous()):
+            raise ValueError(f"moe_ffn_sublayer: out must be contiguous float32 [{T}, {self.H}]")
+        y = out if out is not None else torch.empty((T, self.H), dtype=torch.float32, device=residual.device)
+        rw = torch.empty((self.k, T), dtype=torch.float32, device=residual.device) if return_routing else None
+        rid = torch.empty((self.k, T), dtype=torch.int32, device=residual.device) if return_routing else None
+        lib = _lib.load()
+        need = lib.frank_moe_ffn_sublayer_workspace_size(_DT[self.dtype], T, self.H, self.F, self.E, self.k)
+        ws = self._workspace(T, residual.device, need)
+        _lib.check(lib.frank_moe_ffn_sublayer(
+            _DT[self.dtype], _ptr(residual), _ptr(ffn_norm_w), float(rms_eps), _dt(self.wr), _ptr(self.wr),
+            _ptr(self.w_up), _ptr(self.w_gate), _ptr(self.w_down), T, self.E, self.k, self.H, self.F,
+            int(self.normalize), _ptr(y), _ptr(rw), _ptr(rid), _ptr(ws), ws.numel(), _stream()))
+        if return_routing:
+            return y, rw, rid
+        return y
+
+
+def rms_norm(x: torch.Tensor, weight: torch.Tensor, eps: float, out_dtype: torch.dtype = torch.float32,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """@rms_norm_components.rms_norm_linalg (components/normalization/rms_norm.mlir:18-80):
+    (x / sqrt(mean(x^2, -1) + eps)) * weight for fp32 x [T, H], weight [H];
+    the result in ``out_dtype`` (fp32 or bf16)."""
+    x = _cuda_contig(x, "input")
+    weight = _cuda_contig(weight, "weight")
+    if x.dtype != torch.float32 or x.dim() != 2:
+        raise ValueError(f"rms_norm: input must be float32 [T, H], got {x.dtype} {tuple(x.shape)}")
+    if weight.dtype != torch.float32 or tuple(weight.shape) != (x.shape[1],):
+        raise ValueError(f"rms_norm: weight must be float32 [{x.shape[1]}]")
+    y = out if out is not None else torch.empty(tuple(x.shape), dtype=out_dtype, device=x.device)
+    _lib.check(_lib.load().frank_rms_norm(_ptr(x), _ptr(weight), x.shape[0], x.shape[1], float(eps), _DT[y.dtype],
+                                          _ptr(y), _stream()))
+    return y
 
 
 def moe_ffn_host(block, x_host: torch.Tensor, y_host: torch.Tensor, chunks: int = 4,

@@ -183,6 +183,38 @@ int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr,
                         size_t ws_bytes, void* stream);
 
 /*
+ * rms_norm: out[t] = (x[t] / sqrt(mean(x[t]^2) + eps)) * weight, x [T, H]
+ * fp32, weight [H] fp32, out [T, H] in out_dtype (FRANK_F32 or FRANK_BF16).
+ * Replaces @rms_norm_components.rms_norm_linalg
+ * (components/normalization/rms_norm.mlir:18-80; oracle
+ * oracles/normalization.py:10-43).
+ */
+int frank_rms_norm(const float* x, const float* weight, int64_t T, int64_t H,
+                   float eps, int out_dtype, void* out, void* stream);
+
+/*
+ * The MoE FFN sub-layer of the reference's MoE transformer layer
+ * (architectures/llm/transformer_layer_moe_prefill.mlir:211-245 and the
+ * decode layer's :228-256; oracle oracles/transformer_layer.py:107-124):
+ *   out = residual + moe_ffn_block(rms_norm(residual, norm_w, eps), ...)
+ * residual, out: fp32 [T, H] (out may alias residual: in-place update);
+ * norm_w: fp32 [H].  The normalised tokens are rounded to `dtype` (the block's
+ * compute dtype) in the workspace; the residual add is fused into the block's
+ * final sum over the k slots.  Other arguments as frank_moe_ffn_block.
+ * Workspace: frank_moe_ffn_sublayer_workspace_size(dtype, T, H, F, E, k).
+ */
+size_t frank_moe_ffn_sublayer_workspace_size(int dtype, int64_t T, int64_t H,
+                                             int64_t F, int64_t E, int64_t k);
+int frank_moe_ffn_sublayer(int dtype, const float* residual,
+                           const float* norm_w, float eps, int wr_dtype,
+                           const void* wr, const void* w_up_p,
+                           const void* w_gate_p, const void* w_down_p,
+                           int64_t T, int64_t E, int64_t k, int64_t H,
+                           int64_t F, int normalize, float* out,
+                           float* route_w, int32_t* route_ids, void* workspace,
+                           size_t ws_bytes, void* stream);
+
+/*
  * Building blocks of moe_ffn_block, exported for the expert-parallel layer
  * (which runs the stages with NCCL exchanges in between):
  *

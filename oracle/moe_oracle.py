@@ -194,3 +194,30 @@ def moe_ffn_block_grouped(x, wr, w_up, w_gate, w_down, n_expert, k, n_embd, n_ff
         h = swiglu(g, u)
         d_slots[sl] = (h @ w_down[:, :, e].T) * wflat[sl][:, None]
     return d_slots.reshape(k, T, n_embd).sum(axis=0)
+
+
+# --------------------------------------------------------------------------
+# MoE FFN sub-layer  (oracles/transformer_layer.py:107-124,
+# architectures/llm/transformer_layer_moe_prefill.mlir:211-245)
+# --------------------------------------------------------------------------
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float) -> np.ndarray:
+    """(x / sqrt(sum(x^2, -1) / H + eps)) * weight, step for step as
+    oracles/normalization.py:10-43 (components/normalization/rms_norm.mlir:18-80)."""
+    ss = np.sum(x * x, axis=-1, keepdims=True)
+    rms = np.sqrt(ss / x.shape[-1] + eps)
+    return (x / rms) * weight
+
+
+def moe_ffn_sublayer(residual, ffn_norm_w, eps, wr, w_up, w_gate, w_down, n_expert, k, n_embd, n_ff, normalize,
+                     routing=None, grouped=True):
+    """residual + moe_ffn_block(rms_norm(residual, ffn_norm_w, eps)) --
+    oracles/transformer_layer.py:107-124 (rms_norm at :110, block :112-123,
+    residual add :124).  ``routing`` as in :func:`moe_ffn_block_grouped`."""
+    xn = rms_norm(residual, ffn_norm_w, eps)
+    if grouped:
+        moe = moe_ffn_block_grouped(xn, wr, w_up, w_gate, w_down, n_expert, k, n_embd, n_ff, normalize,
+                                    routing=routing)
+    else:
+        moe = moe_ffn_block_literal(xn, wr, w_up, w_gate, w_down, n_expert, k, n_embd, n_ff, normalize)
+    return residual + moe

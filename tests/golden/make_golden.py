@@ -19,7 +19,12 @@ Cases
     draws;
   * the fp32 headline configuration (T=32, H=64, F=128, E=8, k=2, renorm);
   * small shapes of the fine-grained / decode families (E=128, k=8) with
-    reduced H and F so the literal oracle stays cheap.
+    reduced H and F so the literal oracle stays cheap;
+  * rms_norm (oracles/normalization.py) and the MoE FFN sub-layer, composed
+    from the reference's rms_norm and moe_ffn_block exactly as
+    oracles/transformer_layer.py:107-124 does.
+
+``--only PREFIX`` writes just the cases whose names start with PREFIX.
 """
 
 from __future__ import annotations
@@ -116,24 +121,80 @@ def swiglu_cases():
     return out
 
 
+def norm_cases():
+    """rms_norm (oracles/normalization.py:10-43) and the MoE FFN sub-layer
+    (oracles/transformer_layer.py:107-124): seeded residual streams, norm
+    weights around 1, the block weights of moe_cases' shapes."""
+    out = []
+    rng = np.random.default_rng(21)
+    for name, T, H in (("rmsnorm_small", 5, 64), ("rmsnorm_ragged", 7, 130)):
+        x = rng.standard_normal((T, H), dtype=np.float32) * 3
+        w = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        out.append((name, x, w, np.float32(1e-5)))
+    return out
+
+
+def sublayer_cases():
+    out = []
+    for name, seed, (T, H, F), (E, k), norm, eps in (
+        ("sublayer_basic", 31, (6, 32, 48), (4, 2), False, 1e-5),
+        ("sublayer_renorm", 32, (9, 64, 128), (8, 2), True, 1e-6),
+        ("sublayer_fine_grained", 33, (12, 32, 16), (64, 6), False, 1e-5),
+    ):
+        rng = np.random.default_rng(seed)
+        resid = rng.standard_normal((T, H), dtype=np.float32) * 2
+        nw = (1 + 0.1 * rng.standard_normal(H)).astype(np.float32)
+        wr = (rng.standard_normal((E, H)) * 0.1).astype(np.float32)
+        wu = (rng.standard_normal((F, H, E)) * 0.1).astype(np.float32)
+        wg = (rng.standard_normal((F, H, E)) * 0.1).astype(np.float32)
+        wd = (rng.standard_normal((H, F, E)) * 0.1).astype(np.float32)
+        out.append((name, (resid, nw, np.float32(eps), wr, wu, wg, wd), E, k, H, F, norm))
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the frank-models source tree")
+    ap.add_argument("--only", default="", help="write only the cases whose name starts with this prefix")
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
     from oracles import activation as ref_act  # the reference's own oracle
     from oracles import moe as ref_moe
+    from oracles import normalization as ref_norm
+
+    def keep(name):
+        return name.startswith(args.only)
 
     for name, w, x, ids in mul_mat_id_cases():
+        if not keep(name):
+            continue
         y = ref_moe.mul_mat_id(w, x, ids)
         np.savez_compressed(HERE / f"{name}.npz", weights=w, input=x, ids=ids, expected=y)
     for name, (x, wr, wu, wg, wd), E, k, H, F, norm in moe_cases():
+        if not keep(name):
+            continue
         y = ref_moe.moe_ffn_block(x, wr, wu, wg, wd, E, k, H, F, norm)
         np.savez_compressed(HERE / f"{name}.npz", input=x, gate_inp_w=wr, up_exps_w=wu, gate_exps_w=wg,
                             down_exps_w=wd, n_expert=E, n_expert_used=k, n_embd=H, n_ff=F,
                             normalize_weights=norm, expected=y)
     for name, g, u in swiglu_cases():
+        if not keep(name):
+            continue
         np.savez_compressed(HERE / f"{name}.npz", gate=g, up=u, expected=ref_act.swiglu(g, u))
+    for name, x, w, eps in norm_cases():
+        if not keep(name):
+            continue
+        np.savez_compressed(HERE / f"{name}.npz", input=x, weight=w, eps=eps,
+                            expected=ref_norm.rms_norm(x, w, float(eps)))
+    for name, (resid, nw, eps, wr, wu, wg, wd), E, k, H, F, norm in sublayer_cases():
+        if not keep(name):
+            continue
+        # the sub-layer exactly as oracles/transformer_layer.py:107-124 composes it
+        normed = ref_norm.rms_norm(resid, nw, float(eps))
+        moe = ref_moe.moe_ffn_block(normed, wr, wu, wg, wd, E, k, H, F, norm)
+        np.savez_compressed(HERE / f"{name}.npz", residual=resid, ffn_norm_w=nw, rms_eps=eps, gate_inp_w=wr,
+                            up_exps_w=wu, gate_exps_w=wg, down_exps_w=wd, n_expert=E, n_expert_used=k, n_embd=H,
+                            n_ff=F, normalize_weights=norm, expected=resid + moe)
     print("wrote", len(list(HERE.glob("*.npz"))), "fixtures to", HERE)
 
 

@@ -1,7 +1,9 @@
 """Pin the CPU restatement (oracle/) to the reference's own outputs.
 
 The fixtures in tests/golden/ were produced by running the reference's
-oracles/moe.py and oracles/activation.py (tests/golden/make_golden.py).
+oracles/moe.py, oracles/activation.py and oracles/normalization.py, the
+sub-layer composed as oracles/transformer_layer.py:107-124 does
+(tests/golden/make_golden.py).
 """
 
 import numpy as np
@@ -37,6 +39,24 @@ def test_moe_ffn_block_literal_and_grouped_match_reference(name):
 def test_swiglu_matches_reference(name):
     g = load_golden(name)
     assert_close(O.swiglu(g["gate"], g["up"]), g["expected"], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("name", golden_names("rmsnorm_"))
+def test_rms_norm_matches_reference(name):
+    g = load_golden(name)
+    assert_close(O.rms_norm(g["input"], g["weight"], float(g["eps"])), g["expected"], rtol=0, atol=0)
+
+
+@pytest.mark.parametrize("name", golden_names("sublayer_"))
+def test_moe_ffn_sublayer_matches_reference(name):
+    g = load_golden(name)
+    args = (g["residual"], g["ffn_norm_w"], float(g["rms_eps"]), g["gate_inp_w"], g["up_exps_w"], g["gate_exps_w"],
+            g["down_exps_w"], int(g["n_expert"]), int(g["n_expert_used"]), int(g["n_embd"]), int(g["n_ff"]),
+            bool(g["normalize_weights"]))
+    lit = O.moe_ffn_sublayer(*args, grouped=False)
+    grp = O.moe_ffn_sublayer(*args)
+    assert_close(lit, g["expected"], rtol=1e-6, atol=1e-7)
+    assert_close(grp, g["expected"], rtol=1e-5, atol=1e-7)
 
 
 def test_permutation_is_stable_argsort():
