@@ -49,6 +49,11 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # its traffic is that capture x 4.
 GATE_UP_TRAFFIC_BYTES = {"c3_mixtral_8x7b": 4 * (558.111e6 + 223.502e6)}
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one decode_fused_kernel
+# launch of the same workload (seed 0, 8 distinct experts), captured by ncu
+# (76.670 MB read + 1.875 MB written, profiles/decode_fused_c5_T1.md).
+DECODE_TRAFFIC_BYTES = {"c5_decode_T1": 76.670464e6 + 1.874688e6}
+
 
 def peaks():
     p = REPO / "MEASURED_PEAKS.json"
@@ -383,14 +388,19 @@ def run_frank(args, cfg):
         # is the whole block (the sum of the recorded stages).
         blk_bytes = (n_distinct * 3 * cfg.F * cfg.H * 2 + cfg.E * cfg.H * 4 + cfg.T * cfg.H * 2 + cfg.T * cfg.H * 4)
         fused = cfg.k * cfg.T <= cfg.E
-        k_ms = sum(stage_ms.values()) if fused else stage_ms["gate_up_gemm"]
+        # fused: the one cooperative launch sits between the first two stage
+        # marks (the later marks follow it back to back, so their spans hold
+        # no kernel, only the event resolution)
+        k_ms = stage_ms["route"] if fused else stage_ms["gate_up_gemm"]
         k_bytes = blk_bytes if fused else (n_distinct * 2 * cfg.F * cfg.H * 2 + cfg.k * cfg.T * (cfg.H + cfg.F) * 2)
         achieved = k_bytes / (k_ms / 1e3) / 1e9
         peak = float(pk["hbm_gbs"])
         line["roofline"] = {
             "kernel": "decode_fused_kernel (whole block)" if fused else "tc_grouped_gemm<SWIGLU> (gate/up GEMM + swiglu)",
             "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "peak_source": f"{pk_kind} hbm_gbs", "traffic": None, "bytes_per_launch": k_bytes, "ms_per_launch": k_ms,
+            "peak_source": f"{pk_kind} hbm_gbs",
+            "traffic": DECODE_TRAFFIC_BYTES.get(cfg.name) if fused else None,
+            "bytes_per_launch": k_bytes, "ms_per_launch": k_ms,
             "distinct_experts": n_distinct,
         }
         line["stage_ms"] = stage_ms
