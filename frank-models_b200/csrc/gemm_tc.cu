@@ -46,6 +46,7 @@ constexpr uint32_t B_HALF_BYTES = 128 * BK * 2;  // 16 KiB
 constexpr uint32_t B_BYTES = BN * BK * 2;        // 32 KiB
 constexpr uint32_t STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t EPI_STAGE_BYTES = 4 * 32 * 128;  // epilogue staging, 4 KiB per epilogue warp
 constexpr int kMaxExperts = 1024;
 constexpr int kMaxPeers = 8;
 
@@ -160,44 +161,75 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int3
 
 // Epilogue of one accumulator tile for the 32 rows of one warp: thread
 // `lane` owns row `row`; taddr addresses this warp's TMEM lane quadrant.
+// Epilogue of one accumulator tile for this warp's 32 rows (row: this lane's
+// row).  Values pass through a per-warp shared-memory stage of 32 rows x
+// 128 bytes (16-byte chunk c of row r kept at chunk c ^ (r & 7), so the
+// row-per-lane writes and the row-wise reads are both free of bank
+// conflicts): each global store instruction then covers 4 rows x 128
+// contiguous bytes instead of 32 rows x 16 bytes.
 template <int MODE>
-__device__ __forceinline__ void epilogue_rows(const Params& p, int row, bool valid, int n, uint32_t taddr) {
+__device__ __forceinline__ void epilogue_rows(const Params& p, int row, bool valid, int n, uint32_t taddr,
+                                              uint4* stage) {
+  const int lane = threadIdx.x & 31;
+  const uint32_t sw = (uint32_t)(lane & 7);
+  // byte address of this lane's row at the tile's first column (0: no row)
+  unsigned long long my = 0ull;
   if (MODE == SWIGLU) {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo;
+    if (valid)
+      my = (unsigned long long)(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + n * 128);
+  } else if (valid) {
+    float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+    if (MODE == SCALE && p.row_rank != nullptr) out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
+    my = (unsigned long long)(out + n * BN);
+  }
+  // stage -> global: 8 rounds of 4 rows x 8 chunks; chunk_cols columns per
+  // 16-byte chunk; col0: the stage's first column within the tile
+  auto flush = [&](int col0, int chunk_cols, int elem_bytes) {
+    __syncwarp();
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int r = i * 4 + (lane >> 3), c = lane & 7;
+      const unsigned long long base = __shfl_sync(0xffffffffu, my, r);
+      const uint4 v = stage[r * 8 + (c ^ (r & 7))];
+      const int col = (MODE == SWIGLU ? n * 128 : n * BN) + col0 + c * chunk_cols;
+      if (base != 0ull && col < p.N_out)
+        *reinterpret_cast<uint4*>(base + (unsigned long long)(col0 + c * chunk_cols) * elem_bytes) = v;
+    }
+    __syncwarp();
+  };
+  if (MODE == SWIGLU) {
 #pragma unroll 1
-    for (int c = 0; c < 128; c += 16) {
-      float g[16], u[16];
-      tmem_ld16(taddr + c, g);
-      tmem_ld16(taddr + 128 + c, u);
-      tmem_wait_ld();
-      const int col = n * 128 + c;
-      if (valid && col < p.N_out) {
+    for (int c = 0; c < 128; c += 64) {
+#pragma unroll 1
+      for (int sub = 0; sub < 64; sub += 16) {
+        float g[16], u[16];
+        tmem_ld16(taddr + c + sub, g);
+        tmem_ld16(taddr + 128 + c + sub, u);
+        tmem_wait_ld();
         uint32_t pk[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           pk[i] = pack_bf16x2(g[2 * i] * silu_ref(u[2 * i]), g[2 * i + 1] * silu_ref(u[2 * i + 1]));
-        uint4* dst = reinterpret_cast<uint4*>(out + col);
-        dst[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-        dst[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+        const uint32_t j = (uint32_t)(sub >> 3);
+        stage[lane * 8 + (j ^ sw)] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        stage[lane * 8 + ((j + 1) ^ sw)] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
       }
+      flush(c, 8, 2);
     }
   } else {
-    float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
-    if (MODE == SCALE && p.row_rank != nullptr && valid)
-      out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
     const float s = (MODE == SCALE && valid) ? p.wrow[row] : 1.f;
 #pragma unroll 1
-    for (int c = 0; c < BN; c += 16) {
-      float v[16];
-      tmem_ld16(taddr + c, v);
+    for (int c = 0; c < BN; c += 32) {
+      float v[32];
+      tmem_ld16(taddr + c, *reinterpret_cast<float(*)[16]>(v));
+      tmem_ld16(taddr + c + 16, *reinterpret_cast<float(*)[16]>(v + 16));
       tmem_wait_ld();
-      const int col = n * BN + c;
-      if (valid && col < p.N_out) {
-        float4* dst = reinterpret_cast<float4*>(out + col);
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          dst[i] = make_float4(v[4 * i] * s, v[4 * i + 1] * s, v[4 * i + 2] * s, v[4 * i + 3] * s);
-      }
+      for (int j = 0; j < 8; ++j)
+        stage[lane * 8 + ((uint32_t)j ^ sw)] =
+            make_uint4(__float_as_uint(v[4 * j] * s), __float_as_uint(v[4 * j + 1] * s),
+                       __float_as_uint(v[4 * j + 2] * s), __float_as_uint(v[4 * j + 3] * s));
+      flush(c, 4, 4);
     }
   }
 }
@@ -208,7 +240,8 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
                        const __grid_constant__ CUtensorMap tmB2, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint4* epi_stage = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES);  // [4 warps][32 rows][8 chunks]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES + EPI_STAGE_BYTES);
   // bars[0..S) full, [S..2S) empty, [2S, 2S+2) tmem_full, [2S+2, 2S+4) tmem_empty
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -326,7 +359,8 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = tl.m0 + q * 32 + lane;
-      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16));
+      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16),
+                          epi_stage + q * 256);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(a));
@@ -422,7 +456,8 @@ tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
                         const __grid_constant__ CUtensorMap tmB2, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES);
+  uint4* epi_stage = reinterpret_cast<uint4*>(smem + STAGES2 * STAGE2_BYTES);  // [4 warps][32 rows][8 chunks]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + STAGES2 * STAGE2_BYTES + EPI_STAGE_BYTES);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* prefix = reinterpret_cast<int*>(tmem_slot + 4);  // [E+1]
@@ -537,7 +572,8 @@ tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = tl.m0 + (int)rank * 128 + q * 32 + lane;
-      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16));
+      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16),
+                          epi_stage + q * 256);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(tempty_bar(a), 0));
@@ -610,8 +646,12 @@ int make_map_3d(CUtensorMap* m, const void* base, int64_t E, int64_t N, int64_t 
   return FRANK_OK;
 }
 
-size_t smem_bytes(int E) { return 1024 + STAGES * STAGE_BYTES + 8 * (2 * STAGES + 4) + 16 + 4 * (E + 1) + 64; }
-size_t smem2_bytes(int E) { return 1024 + STAGES2 * STAGE2_BYTES + 8 * (2 * STAGES2 + 4) + 16 + 4 * (E + 1) + 64; }
+size_t smem_bytes(int E) {
+  return 1024 + STAGES * STAGE_BYTES + EPI_STAGE_BYTES + 8 * (2 * STAGES + 4) + 16 + 4 * (E + 1) + 64;
+}
+size_t smem2_bytes(int E) {
+  return 1024 + STAGES2 * STAGE2_BYTES + EPI_STAGE_BYTES + 8 * (2 * STAGES2 + 4) + 16 + 4 * (E + 1) + 64;
+}
 
 // The CTA-pair form is opt-in (FRANK_TC_PAIR=1): on the B200s measured it
 // was ~7% slower than the single-CTA kernel on the Mixtral block, whose
