@@ -67,6 +67,7 @@ struct Params {
   const int32_t* row_rank;
   const int32_t* row_pos;
   float* peer_out[kMaxPeers];
+  int swap_small;          // experts with <= BM rows run as swapped (weight-row-major) tiles
 };
 
 // ------------------------------------------------------------ PTX glue --
@@ -109,6 +110,18 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// Same with a run-time instruction descriptor (swapped tiles: M = 128
+// weight rows, N = the expert's token rows rounded up to 16).
+__device__ __forceinline__ void mma_bf16_i(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
 }
@@ -129,11 +142,18 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // ------------------------------------------------------------- kernel --
 constexpr int kBandRows = 2048;
 
+// swapN != 0: a swapped tile.  The expert has at most BM rows, so the MMAs
+// run with the 128 weight rows of each B half as M and the expert's token
+// rows (rounded up to 16) as N: D0 = (B rows 0-127) x tokens in TMEM columns
+// [0, swapN), D1 = (B rows 128-255) x tokens in [swapN, 2 swapN).  The
+// shared-memory tiles are the normal ones; the MMA work falls to swapN/128
+// of a normal tile's.
 struct Tile {
-  int e, m0, m_end, n;
+  int e, m0, m_end, n, swapN;
 };
 
-__device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int32_t* offsets, int E, int bm = BM) {
+__device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int32_t* offsets, int E, int bm = BM,
+                                            bool allow_swap = false) {
   int lo = 0, hi = E;  // find e: prefix[e] <= t < prefix[e+1]
   while (hi - lo > 1) {
     int mid = (lo + hi) >> 1;
@@ -156,6 +176,7 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int3
   tl.m0 = r0 + (band * G + in % gm) * bm;
   tl.m_end = r1;
   tl.n = in / gm;
+  tl.swapN = (allow_swap && mt == 1) ? ((r1 - r0 + 15) & ~15) : 0;
   return tl;
 }
 
@@ -234,6 +255,47 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, int row, bool val
   }
 }
 
+// Epilogue of a swapped tile: this lane owns weight row wr (0..127) of both
+// accumulators, i.e. output column n*128 + wr (SWIGLU: gate in D0, up in D1)
+// or n*BN + wr and n*BN + 128 + wr (SCALE / PLAIN), for each of the
+// expert's token rows.  Per token the 32 lanes of a warp store 32
+// consecutive columns (64 or 128 contiguous bytes).
+template <int MODE>
+__device__ __forceinline__ void epilogue_swapped(const Params& p, const Tile& tl, int wr, uint32_t taddr) {
+  const int rows = tl.m_end - tl.m0;
+  const int N = tl.swapN;
+#pragma unroll 1
+  for (int t0 = 0; t0 < N; t0 += 16) {
+    float v0[16], v1[16];
+    tmem_ld16(taddr + t0, v0);
+    tmem_ld16(taddr + N + t0, v1);
+    tmem_wait_ld();
+    const int nt = min(16, rows - t0);
+    if (MODE == SWIGLU) {
+      const int col = tl.n * 128 + wr;
+      if (col < p.N_out) {
+        __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(p.out) + col;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < nt) out[(int64_t)(tl.m0 + t0 + i) * p.ldo] = __float2bfloat16_rn(v0[i] * silu_ref(v1[i]));
+      }
+    } else {
+      const int c0 = tl.n * BN + wr, c1 = c0 + 128;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        if (i < nt) {
+          const int row = tl.m0 + t0 + i;
+          float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+          if (MODE == SCALE && p.row_rank != nullptr) out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
+          const float sc = MODE == SCALE ? p.wrow[row] : 1.f;
+          if (c0 < p.N_out) out[c0] = v0[i] * sc;
+          if (c1 < p.N_out) out[c1] = v1[i] * sc;
+        }
+      }
+    }
+  }
+}
+
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -303,7 +365,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        Tile tl = decode_tile(t, prefix, p.offsets, p.E);
+        Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM, p.swap_small != 0);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
@@ -331,6 +393,9 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
         if (!mbar_wait(tempty_bar(a), aph ^ 1u, abort_flag, p.err)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + a * BN;
+        const int swapN = p.swap_small ? decode_tile(t, prefix, p.offsets, p.E, BM, true).swapN : 0;
+        const uint32_t idesc_sw =
+            (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(swapN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
@@ -339,10 +404,20 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
           const uint32_t sa = smem_u32(smem + s * STAGE_BYTES);
           const uint64_t adesc = make_sw128_desc(sa);
           const uint64_t bdesc = make_sw128_desc(sa + A_BYTES);
+          if (swapN == 0) {
 #pragma unroll
-          for (int j = 0; j < BK / 16; ++j) {
-            // advance 16 bf16 = 32 B along K inside the 128-B swizzle row
-            mma_bf16(d, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), (kb | j) != 0);
+            for (int j = 0; j < BK / 16; ++j) {
+              // advance 16 bf16 = 32 B along K inside the 128-B swizzle row
+              mma_bf16(d, adesc + (uint64_t)(2 * j), bdesc + (uint64_t)(2 * j), (kb | j) != 0);
+            }
+          } else {
+            const uint64_t b1desc = make_sw128_desc(sa + A_BYTES + B_HALF_BYTES);
+#pragma unroll
+            for (int j = 0; j < BK / 16; ++j) {
+              mma_bf16_i(d, bdesc + (uint64_t)(2 * j), adesc + (uint64_t)(2 * j), idesc_sw, (kb | j) != 0);
+              mma_bf16_i(d + (uint32_t)swapN, b1desc + (uint64_t)(2 * j), adesc + (uint64_t)(2 * j), idesc_sw,
+                         (kb | j) != 0);
+            }
           }
           mma_commit(empty_bar(s));
         }
@@ -354,13 +429,16 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
-      Tile tl = decode_tile(t, prefix, p.offsets, p.E);
+      Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM, p.swap_small != 0);
       const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
       const int row = tl.m0 + q * 32 + lane;
-      epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16),
-                          epi_stage + q * 256);
+      if (tl.swapN)
+        epilogue_swapped<MODE>(p, tl, q * 32 + lane, tmem_base + a * BN + ((uint32_t)(q * 32) << 16));
+      else
+        epilogue_rows<MODE>(p, row, row < tl.m_end, tl.n, tmem_base + a * BN + ((uint32_t)(q * 32) << 16),
+                            epi_stage + q * 256);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(tempty_bar(a));
@@ -720,6 +798,10 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
   p.row_rank = row_rank;
   p.row_pos = row_pos;
   for (int i = 0; i < kMaxPeers; ++i) p.peer_out[i] = (peer_out && i < n_peers) ? peer_out[i] : nullptr;
+  {
+    const char* sw = getenv("FRANK_TC_SWAP");
+    p.swap_small = (sw && sw[0] == '0') ? 0 : 1;
+  }
   if (row_rank && (mode != SCALE || !row_pos || !peer_out || n_peers < 1 || n_peers > kMaxPeers)) {
     set_error("tc_grouped_gemm: a row map needs SCALE mode, row_pos and 1..%d peer buffers", kMaxPeers);
     return FRANK_EINVAL;
