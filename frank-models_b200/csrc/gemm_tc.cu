@@ -299,7 +299,9 @@ __device__ __forceinline__ void epilogue_swapped(const Params& p, const Tile& tl
 template <int MODE>
 __global__ void __launch_bounds__(THREADS, 1)
 tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-                       const __grid_constant__ CUtensorMap tmB2, const Params p) {
+                       const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmA16,
+                       const __grid_constant__ CUtensorMap tmA32, const __grid_constant__ CUtensorMap tmA64,
+                       const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint4* epi_stage = reinterpret_cast<uint4*>(smem + STAGES * STAGE_BYTES);  // [4 warps][32 rows][8 chunks]
@@ -371,8 +373,11 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
           const uint32_t ph = (it / STAGES) & 1u;
           if (!mbar_wait(empty_bar(s), ph ^ 1u, abort_flag, p.err)) { ok = false; break; }
           uint8_t* st = smem + s * STAGE_BYTES;
-          mbar_expect_tx(full_bar(s), STAGE_BYTES);
-          tma_load_2d(smem_u32(st), &tmA, kb * BK, tl.m0, full_bar(s));
+          // swapped tiles read only the expert's rows: a 16/32/64-row A box
+          const int arows = tl.swapN == 0 ? BM : tl.swapN <= 16 ? 16 : tl.swapN <= 32 ? 32 : tl.swapN <= 64 ? 64 : BM;
+          const CUtensorMap* mapA = arows == 16 ? &tmA16 : arows == 32 ? &tmA32 : arows == 64 ? &tmA64 : &tmA;
+          mbar_expect_tx(full_bar(s), (uint32_t)arows * BK * 2 + B_BYTES);
+          tma_load_2d(smem_u32(st), mapA, kb * BK, tl.m0, full_bar(s));
           if (MODE == SWIGLU) {
             tma_load_3d(smem_u32(st + A_BYTES), &tmB, kb * BK, tl.n * 128, tl.e, full_bar(s));
             tma_load_3d(smem_u32(st + A_BYTES + B_HALF_BYTES), &tmB2, kb * BK, tl.n * 128, tl.e, full_bar(s));
@@ -682,7 +687,7 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
 }
 
 // 2-D bf16 map [rows, K], box {64, 128}, 128-B swizzle.
-int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t K) {
+int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t K, uint32_t box_rows = 128) {
   auto enc = get_encode();
   if (!enc) {
     frank::set_error("cuTensorMapEncodeTiled unavailable");
@@ -690,7 +695,7 @@ int make_map_2d(CUtensorMap* m, const void* base, int64_t rows, int64_t K) {
   }
   cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  cuuint32_t box[2] = {BK, 128};
+  cuuint32_t box[2] = {BK, box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -780,8 +785,11 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
     set_error("bf16 tensor-core path needs 16-byte aligned buffers");
     return FRANK_EINVAL;
   }
-  CUtensorMap ma, mb, mb2;
+  CUtensorMap ma, mb, mb2, ma16, ma32, ma64;
   FRANK_TRY(make_map_2d(&ma, A, rows, K));
+  FRANK_TRY(make_map_2d(&ma16, A, rows, K, 16));
+  FRANK_TRY(make_map_2d(&ma32, A, rows, K, 32));
+  FRANK_TRY(make_map_2d(&ma64, A, rows, K, 64));
   FRANK_TRY(make_map_3d(&mb, B, E, N, K));
   if (mode == SWIGLU) FRANK_TRY(make_map_3d(&mb2, B2, E, N, K));
   else mb2 = mb;
@@ -828,17 +836,17 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
     case SWIGLU:
       FRANK_CUDA_TRY(cudaFuncSetAttribute(tc_grouped_gemm_kernel<SWIGLU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem));
-      tc_grouped_gemm_kernel<SWIGLU><<<grid, block, smem, st>>>(ma, mb, mb2, p);
+      tc_grouped_gemm_kernel<SWIGLU><<<grid, block, smem, st>>>(ma, mb, mb2, ma16, ma32, ma64, p);
       break;
     case SCALE:
       FRANK_CUDA_TRY(cudaFuncSetAttribute(tc_grouped_gemm_kernel<SCALE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem));
-      tc_grouped_gemm_kernel<SCALE><<<grid, block, smem, st>>>(ma, mb, mb2, p);
+      tc_grouped_gemm_kernel<SCALE><<<grid, block, smem, st>>>(ma, mb, mb2, ma16, ma32, ma64, p);
       break;
     default:
       FRANK_CUDA_TRY(cudaFuncSetAttribute(tc_grouped_gemm_kernel<PLAIN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           (int)smem));
-      tc_grouped_gemm_kernel<PLAIN><<<grid, block, smem, st>>>(ma, mb, mb2, p);
+      tc_grouped_gemm_kernel<PLAIN><<<grid, block, smem, st>>>(ma, mb, mb2, ma16, ma32, ma64, p);
   }
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
