@@ -20,7 +20,8 @@
 //            (moe_ffn_block.mlir:179-206), deterministic.
 // decode_fused_kernel runs all phases in one cooperative launch with three
 // grid barriers (after route, gate/up and down): every block computes the
-// top-k and the permutation of all tokens itself.  FRANK_DECODE_FUSED=0 runs
+// top-k and the permutation of all tokens itself.  Blocks have eight compute
+// warps plus one warp that issues the streaming phases' bulk copies.  FRANK_DECODE_FUSED=0 runs
 // the same bodies as five launches chained by programmatic dependent launch.
 // No atomics on data: results are deterministic and identical in both forms.
 #include <cstdlib>
@@ -33,8 +34,9 @@ namespace {
 
 using namespace frank_topk;
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 256;           // compute threads (warps 0 .. kWarps-1)
 constexpr int kWarps = kThreads / 32;
+constexpr int kBlockThreads = kThreads + 32;  // + the streaming phases' bulk-copy producer warp
 constexpr int kRouteTok = 8;    // tokens per route warp item
 constexpr int kMaxSlots = kMaxE; // k * T handled by the decode path (k * T <= E)
 constexpr int kRC = 8;          // token rows per pass over an expert's weights
@@ -95,6 +97,10 @@ struct Meta {
 __device__ __forceinline__ void wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void allow_next_grid() { asm volatile("griddepcontrol.launch_dependents;" :::); }
 
+// Barrier of the kThreads compute threads (warps 0 .. kWarps-1): the
+// routing phases run without the producer warp.
+__device__ __forceinline__ void consumer_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kThreads) : "memory"); }
+
 // ----------------------------------------------------------------- route --
 // logits[e, t] = Wr[e] . x[t] for items (expert e, kRouteTok tokens).  When
 // there are fewer items than warps in the grid, wpi warps of one block split
@@ -141,13 +147,13 @@ __device__ __forceinline__ void route_body(const __nv_bfloat16* __restrict__ x, 
       for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
       if (lane == 0) red[warp * kRouteTok + a] = v;
     }
-    __syncthreads();
+    consumer_sync();
     if (sub == 0 && lane < kRouteTok && item < items && t0 + lane < T) {
       float v = 0.f;
       for (int s2 = 0; s2 < wpi; ++s2) v += red[(slot * wpi + s2) * kRouteTok + lane];
       ws.logits[(int64_t)e * T + t0 + lane] = v;
     }
-    __syncthreads();
+    consumer_sync();
   }
 }
 
@@ -247,11 +253,11 @@ __device__ __forceinline__ void block_softmax_topk(const float* logits, int T, i
       if (e < E) prob[t * E + e] = v[i] / sum;
     }
   }
-  __syncthreads();
+  consumer_sync();
   if (T * E > kThreads) {
     // more pairs than threads: a serial k-step selection per token and warp
     for (int t = warp; t < T; t += kWarps) warp_softmax_topk_probs(prob + t * E, E, k, normalize, w_out, id_out, T, t);
-    __syncthreads();
+    consumer_sync();
     return;
   }
   for (int idx = threadIdx.x; idx < T * E; idx += kThreads) {
@@ -269,14 +275,14 @@ __device__ __forceinline__ void block_softmax_topk(const float* logits, int T, i
       w_out[r * T + t] = p;
     }
   }
-  __syncthreads();
+  consumer_sync();
   if (normalize) {
     for (int t = threadIdx.x; t < T; t += kThreads) {
       float s = 0.f;
       for (int j = 0; j < k; ++j) s += w_out[j * T + t];  // ascending j, as numpy's sum over a short axis
       for (int j = 0; j < k; ++j) w_out[j * T + t] = w_out[j * T + t] / s;
     }
-    __syncthreads();
+    consumer_sync();
   }
 }
 
@@ -298,7 +304,7 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
     running[e] = 0;
     for (int w2 = 0; w2 < kWarps; ++w2) warp_cnt[w2 * kMaxE + e] = 0;
   }
-  __syncthreads();
+  consumer_sync();
   for (int base = 0; base < n; base += kThreads) {
     const int s = base + threadIdx.x;
     const int e = s < n ? ids[s] : -1;
@@ -306,7 +312,7 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
     const int rank_w = __popc(peers & ((1u << lane) - 1u));
     const int leader = __ffs(peers) - 1;
     if (e >= 0 && lane == leader) warp_cnt[warp * kMaxE + e] = __popc(peers);
-    __syncthreads();
+    consumer_sync();
     int pos = 0;
     bool last = false;
     if (e >= 0) {
@@ -318,10 +324,10 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
       for (int w2 = warp + 1; w2 < kWarps && last; ++w2)
         if (warp_cnt[w2 * kMaxE + e] != 0) last = false;
     }
-    __syncthreads();
+    consumer_sync();
     if (last) running[e] = pos + 1;
     if (e >= 0 && lane == leader) warp_cnt[warp * kMaxE + e] = 0;
-    __syncthreads();
+    consumer_sync();
   }
   if (warp == 0) {  // exclusive scan of the counts and the active-expert list (E <= 256)
     int carry = 0, na = 0;
@@ -357,7 +363,7 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
       }
     }
   }
-  __syncthreads();
+  consumer_sync();
   for (int s = threadIdx.x; s < n; s += kThreads) {
     const int32_t pos = running[ids[s]] + rank[s];
     const float w = wts[s];
@@ -369,7 +375,7 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
       ws.wsorted[pos] = w;
     }
   }
-  __syncthreads();
+  consumer_sync();
 }
 
 __device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch,
@@ -393,9 +399,9 @@ decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
 
 __device__ __forceinline__ Meta load_meta(const DecodeWs& ws, int T, int E, int32_t* off, int32_t* act, int32_t* nact,
                                           int32_t* tok, float* w) {
-  for (int i = threadIdx.x; i <= E; i += kThreads) off[i] = __ldcg(ws.offsets + i);
-  for (int i = threadIdx.x; i < E; i += kThreads) act[i] = __ldcg(ws.active + i);
-  for (int i = threadIdx.x; i < ws.n_slots; i += kThreads) {
+  for (int i = threadIdx.x; i <= E; i += blockDim.x) off[i] = __ldcg(ws.offsets + i);
+  for (int i = threadIdx.x; i < E; i += blockDim.x) act[i] = __ldcg(ws.active + i);
+  for (int i = threadIdx.x; i < ws.n_slots; i += blockDim.x) {
     tok[i] = __ldcg(ws.sorted_slots + i) % T;
     w[i] = __ldcg(ws.wsorted + i);
   }
@@ -424,7 +430,8 @@ struct StreamSmem {
 // f0 + w for each token row: h = gate . x * silu(up . x).
 __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int rcap, int stages,
-                     DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, int* s_abort, Meta m) {
+                     DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, uint64_t* empty,
+                     int* s_abort, Meta m) {
   // routing tables in shared memory: refilling a stage needs no global round trip
   const int32_t* sm_off = m.off;
   const int32_t* sm_act = m.act;
@@ -436,7 +443,10 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
   const uint32_t stage_bytes = wbytes + (uint32_t)rcap * H * 2;
   uint8_t* stage_base = dsm_raw;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), kWarps);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
@@ -463,8 +473,17 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
     for (int r = 0; r < rc; ++r)
       bulk_load(dst + wbytes + r * xrow, x + (int64_t)sm_tok[r0 + r] * H, xrow, bar);
   };
-  if (threadIdx.x == 0)
-    for (int j = 0; j < stages && j < mine; ++j) issue(j);
+  if (warp == kWarps) {
+    // producer warp: refills a stage as soon as all compute warps released
+    // it, so the compute warps never stall on issuing copies
+    if (lane == 0)
+      for (int j = 0; j < mine; ++j) {
+        const int s = j % stages;
+        if (j >= stages && !mbar_wait(smem_u32(&empty[s]), (uint32_t)(j / stages - 1) & 1u, s_abort, ws.err)) break;
+        issue(j);
+      }
+    return;
+  }
   for (int j = 0; j < mine; ++j) {
     const int item = bid + j * nblk;
     const int e = sm_act[item / nfc];
@@ -483,7 +502,7 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
           const int r = i / hv, v = i - r * hv;
           xr[i] = reinterpret_cast<const uint4*>(x + (int64_t)sm_tok[r0 + c0 + r] * H)[v];
         }
-        __syncthreads();
+        consumer_sync();
       }
       if (warp < rows) {
         const uint4* gr = gsm + (size_t)warp * hv;
@@ -523,21 +542,19 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
           if (lane == 0) ws.hs[(int64_t)(r0 + c0 + r) * F + f0 + warp] = __float2bfloat16_rn(g * silu_ref(u));
         }
       }
-      __syncthreads();
+      if (c0 + rcap < cnt) consumer_sync();  // the next chunk's rows overwrite xr
     }
-    if (threadIdx.x == 0 && j + stages < mine) {
-      fence_proxy_async_smem();  // generic reads of stage s precede the bulk copy that refills it
-      issue(j + stages);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
   }
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kBlockThreads)
 decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int rcap, int stages,
                      DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
-  __shared__ __align__(8) uint64_t full[4];
+  __shared__ __align__(8) uint64_t full[4], empty[4];
   __shared__ int s_abort;
   if (threadIdx.x == 0) s_abort = 0;
   wait_prior_grid();
@@ -545,7 +562,8 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   const Meta m = load_meta(ws, T, E, m_off, m_act, &m_nact, m_tok, m_w);
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, empty,
+              &s_abort, m);
 }
 
 // down: item = (active expert e, hr rows of H starting at h0): stage =
@@ -553,7 +571,7 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
 // d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
 __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr,
                                           int rcap, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw,
-                                          uint64_t* full, int* s_abort, Meta m) {
+                                          uint64_t* full, uint64_t* empty, int* s_abort, Meta m) {
   const int32_t* sm_off = m.off;
   const int32_t* sm_act = m.act;
   const float* sm_w = m.w;
@@ -564,7 +582,10 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
   const uint32_t stage_bytes = wbytes + (uint32_t)rcap * F * 2;
   uint8_t* stage_base = dsm_raw;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) mbar_init(smem_u32(&full[i]), 1);
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(smem_u32(&full[i]), 1);
+      mbar_init(smem_u32(&empty[i]), kWarps);
+    }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
   fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
@@ -588,8 +609,17 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
     bulk_load(dst, w_down + ((int64_t)e * H + h0) * F, bytes, bar);
     bulk_load(dst + wbytes, ws.hs + (int64_t)r0 * F, hbytes, bar);
   };
-  if (threadIdx.x == 0)
-    for (int j = 0; j < stages && j < mine; ++j) issue(j);
+  if (warp == kWarps) {
+    // producer warp: refills a stage as soon as all compute warps released
+    // it, so the compute warps never stall on issuing copies
+    if (lane == 0)
+      for (int j = 0; j < mine; ++j) {
+        const int s = j % stages;
+        if (j >= stages && !mbar_wait(smem_u32(&empty[s]), (uint32_t)(j / stages - 1) & 1u, s_abort, ws.err)) break;
+        issue(j);
+      }
+    return;
+  }
   for (int j = 0; j < mine; ++j) {
     const int item = bid + j * nblk;
     const int e = sm_act[item / nhc];
@@ -605,7 +635,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
       if (c0 > 0) {  // more than rcap rows: later chunks are loaded into the same area
         for (int i = threadIdx.x; i < rc * fv; i += kThreads)
           hr8[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
-        __syncthreads();
+        consumer_sync();
       }
       // each warp takes its rows jr = warp + 8*jj (jj < 4) together: four
       // independent dot products in flight
@@ -650,20 +680,18 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
           }
         }
       }
-      __syncthreads();
+      if (c0 + rcap < cnt) consumer_sync();  // the next chunk's rows overwrite the h area
     }
-    if (threadIdx.x == 0 && j + stages < mine) {
-      fence_proxy_async_smem();
-      issue(j + stages);
-    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
   }
 }
 
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kBlockThreads)
 decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int rcap, int stages,
                    DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
-  __shared__ __align__(8) uint64_t full[4];
+  __shared__ __align__(8) uint64_t full[4], empty[4];
   __shared__ int s_abort;
   if (threadIdx.x == 0) s_abort = 0;
   wait_prior_grid();
@@ -671,7 +699,7 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   const Meta m = load_meta(ws, 1, E, m_off, m_act, &m_nact, m_tok, m_w);
-  down_body(w_down, H, F, E, hr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, &s_abort, m);
+  down_body(w_down, H, F, E, hr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, empty, &s_abort, m);
 }
 
 // --------------------------------------------------------------- combine --
@@ -747,37 +775,42 @@ __device__ __forceinline__ FusedRoutingSmem carve_fused_routing(uint8_t* base, i
 }
 
 template <class TW, class TY>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBlockThreads, 1)
 decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr,
                     const __nv_bfloat16* __restrict__ w_gate, const __nv_bfloat16* __restrict__ w_up,
                     const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int normalize,
                     int fr, int stages_gu, int hr, int stages_dn, int rcap, TY* y, DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
-  __shared__ __align__(8) uint64_t full_gu[4], full_dn[4];
+  __shared__ __align__(8) uint64_t full_gu[4], full_dn[4], empty_gu[4], empty_dn[4];
   __shared__ int s_abort;
   if (threadIdx.x == 0) s_abort = 0;
   const int bid = blockIdx.x, nblk = gridDim.x;
-  route_body<TW>(x, wr, T, H, E, ws, reinterpret_cast<float*>(dsm_raw), bid, nblk);
+  const bool compute = threadIdx.x < kThreads;  // warps 0..kWarps-1; the last warp produces copies
+  if (compute) route_body<TW>(x, wr, T, H, E, ws, reinterpret_cast<float*>(dsm_raw), bid, nblk);
   grid_barrier(ws.gbar, 1u * nblk, &s_abort, ws.err);
   // every block runs softmax / top-k for all T tokens and builds the (small)
   // permutation itself, so the streaming phases start without another
   // barrier; block 0 also publishes the routing
-  const FusedRoutingSmem rs = carve_fused_routing(dsm_raw, T, E);
-  block_softmax_topk(ws.logits, T, E, k, normalize, rs.prob, rs.w, rs.ids);
-  if (bid == 0)
-    for (int i = threadIdx.x; i < k * T; i += kThreads) {
-      ws.w[i] = rs.w[i];
-      ws.ids[i] = rs.ids[i];
-    }
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   const Meta m{m_off, m_act, &m_nact, m_tok, m_w};
-  permute_body(T, E, k, ws, rs.scratch, m, rs.ids, rs.w, bid == 0);
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages_gu, ws, bid, nblk, dsm_raw, full_gu, &s_abort, m);
+  if (compute) {
+    const FusedRoutingSmem rs = carve_fused_routing(dsm_raw, T, E);
+    block_softmax_topk(ws.logits, T, E, k, normalize, rs.prob, rs.w, rs.ids);
+    if (bid == 0)
+      for (int i = threadIdx.x; i < k * T; i += kThreads) {
+        ws.w[i] = rs.w[i];
+        ws.ids[i] = rs.ids[i];
+      }
+    permute_body(T, E, k, ws, rs.scratch, m, rs.ids, rs.w, bid == 0);
+  }
+  __syncthreads();  // the routing tables, for the producer warp too
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages_gu, ws, bid, nblk, dsm_raw, full_gu, empty_gu, &s_abort,
+              m);
   grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
-  down_body(w_down, H, F, E, hr, rcap, stages_dn, ws, bid, nblk, dsm_raw, full_dn, &s_abort, m);
+  down_body(w_down, H, F, E, hr, rcap, stages_dn, ws, bid, nblk, dsm_raw, full_dn, empty_dn, &s_abort, m);
   grid_barrier(ws.gbar, 3u * nblk, &s_abort, ws.err);
-  combine_body<TY>(T, H, k, y, ws, (int64_t)bid * kThreads + threadIdx.x, (int64_t)nblk * kThreads);
+  if (compute) combine_body<TY>(T, H, k, y, ws, (int64_t)bid * kThreads + threadIdx.x, (int64_t)nblk * kThreads);
 }
 
 template <typename... KArgs, typename... Args>
@@ -803,7 +836,7 @@ int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, 
   auto kern = decode_fused_kernel<TW, TY>;
   FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
-  FRANK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem));
+  FRANK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kBlockThreads, smem));
   if (per_sm < 1) {
     frank::set_error("decode block: the fused kernel does not fit on an SM");
     return FRANK_EINVAL;
@@ -813,7 +846,7 @@ int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, 
   attr[0].val.cooperative = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(frank::num_sms());
-  cfg.blockDim = dim3(kThreads);
+  cfg.blockDim = dim3(kBlockThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cfg.attrs = attr;
@@ -984,7 +1017,7 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   {
     const size_t smem = stages_gu * stage_gu;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kThreads), smem, st,
+    FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kBlockThreads), smem, st,
                               (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
                               (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, (int)E, fr, rcap, stages_gu,
                               ws));
@@ -994,7 +1027,7 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   {
     const size_t smem = stages_dn * stage_dn;
     FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    FRANK_CUDA_TRY(launch_pdl(decode_down_kernel, dim3(grid_p), dim3(kThreads), smem, st,
+    FRANK_CUDA_TRY(launch_pdl(decode_down_kernel, dim3(grid_p), dim3(kBlockThreads), smem, st,
                               (const __nv_bfloat16*)w_down_p, (int)H, (int)F, (int)E, hr, rcap, stages_dn, ws));
     FRANK_LAUNCH_CHECK();
   }
