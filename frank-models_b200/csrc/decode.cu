@@ -419,12 +419,6 @@ __device__ __forceinline__ Meta load_meta(const DecodeWs& ws, int T, int E, int3
 // (active expert, chunk of rows), spread over persistent blocks.
 using namespace frank_mbar;
 
-struct StreamSmem {
-  uint32_t stage0;   // shared address of stage 0
-  uint32_t stage_bytes;
-  int stages;
-};
-
 // gate/up: item = (active expert e, fr rows of F starting at f0): stage =
 // fr gate rows then fr up rows ([2][fr][H] bf16).  Warp w < fr computes row
 // f0 + w for each token row: h = gate . x * silu(up . x).
