@@ -379,9 +379,10 @@ class HostPipeline:
     second copy stream).  Batch i+1's input copy therefore runs during batch
     i's block, and batch i's output copy during batch i+1's block; every
     batch still moves its own inputs and result across PCIe.  Returns a CUDA
-    event that completes when y_host is written.  Pinned host tensors only;
-    no host synchronisation.  The result of each batch equals one block call
-    on the same tokens, bit for bit."""
+    event that completes when y_host is written; until then the caller keeps
+    x_host and y_host alive and does not modify them.  Pinned host tensors
+    only; no host synchronisation.  The result of each batch equals one
+    block call on the same tokens, bit for bit."""
 
     def __init__(self, block, T: int, H: int, x_dtype: torch.dtype, y_dtype: torch.dtype = torch.float32,
                  depth: int = 2, device=None):
