@@ -378,6 +378,53 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
   consumer_sync();
 }
 
+// permute_body for at most 32 slots (k * T <= 32): the same tables from one
+// barrier.  Every compute thread counts the slots below its experts for the
+// offsets; warp 0 ranks each slot by shuffles (stable: expert, then slot)
+// and lists the active experts in ascending order.
+__device__ __forceinline__ void small_permute_body(int T, int E, int k, const DecodeWs& ws, Meta m,
+                                                   const int32_t* ids, const float* wts, bool writer) {
+  const int n = k * T;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e <= E; e += kThreads) {
+    int c = 0;
+    for (int s2 = 0; s2 < n; ++s2) c += ids[s2] < e;
+    m.off[e] = c;
+    if (writer) ws.offsets[e] = c;
+  }
+  if (warp == 0) {
+    const int e = lane < n ? ids[lane] : 0x7fffffff;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const bool first = lane < n && (peers & ((1u << lane) - 1u)) == 0u;  // first slot of its expert
+    const unsigned firsts = __ballot_sync(0xffffffffu, first);
+    int pos = 0, aidx = 0;
+    for (int t = 0; t < n; ++t) {
+      const int et = __shfl_sync(0xffffffffu, e, t);
+      pos += (et < e) | ((et == e) & (t < lane));
+      aidx += (int)((firsts >> t) & 1u) & (et < e);
+    }
+    if (first) {
+      m.act[aidx] = e;
+      if (writer) ws.active[aidx] = e;
+    }
+    if (lane == 0) {
+      *m.nact = __popc(firsts);
+      if (writer) *ws.nactive = __popc(firsts);
+    }
+    if (lane < n) {
+      const float w = wts[lane];
+      m.tok[pos] = lane % T;
+      m.w[pos] = w;
+      if (writer) {
+        ws.sorted_slots[pos] = lane;
+        ws.slot_pos[lane] = pos;
+        ws.wsorted[pos] = w;
+      }
+    }
+  }
+  consumer_sync();
+}
+
 __device__ __forceinline__ void finalize_body(int T, int E, int k, int normalize, const DecodeWs& ws, uint8_t* scratch,
                                               float* prob, Meta m) {
   block_softmax_topk(ws.logits, T, E, k, normalize, prob, ws.w, ws.ids);
@@ -796,7 +843,10 @@ decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
         ws.w[i] = rs.w[i];
         ws.ids[i] = rs.ids[i];
       }
-    permute_body(T, E, k, ws, rs.scratch, m, rs.ids, rs.w, bid == 0);
+    if (k * T <= 32)
+      small_permute_body(T, E, k, ws, m, rs.ids, rs.w, bid == 0);
+    else
+      permute_body(T, E, k, ws, rs.scratch, m, rs.ids, rs.w, bid == 0);
   }
   __syncthreads();  // the routing tables, for the producer warp too
   gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages_gu, ws, bid, nblk, dsm_raw, full_gu, empty_gu, &s_abort,
