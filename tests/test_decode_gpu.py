@@ -8,10 +8,11 @@ column slices of the row groups), k*T == E, more rows per expert than one
 pass stages (T > 8), and wide rows (n_embd = n_ff = 4096, and the
 Mixtral-8x7B shapes: one weight row of 28 KB per down item).
 
-The oracle (float64, moe_oracle.moe_ffn_block_grouped) runs on the experts
-the GPU routed to, with the GPU's routing, so near-tied tokens cannot swap
-experts between the two sides; routing is checked separately against the
-oracle's own top-k.  Tolerance: max-abs <= 2e-2 x output RMS (bf16 h).
+The oracle (float64, moe_oracle.moe_ffn_block_grouped) runs with its own
+routing under the strict tier (tests/utils.py ``strict_routing``: ids equal
+the oracle's top-k on float64 logits except on tokens whose k-th/(k+1)-th
+gap is below the fp32 accumulation bound), restricted to the experts routed
+to.  Tolerance: max-abs <= 2e-2 x output RMS (bf16 h).
 """
 
 import numpy as np
@@ -20,7 +21,7 @@ import torch
 
 from frank_b200 import configs, ops
 from oracle import moe_oracle as O
-from tests.utils import rms_rel_maxabs
+from tests.utils import rms_rel_maxabs, strict_route
 
 pytestmark = pytest.mark.gpu
 
@@ -66,14 +67,11 @@ def test_decode_block(cfg, monkeypatch):
     y0, rw0, rid0 = _run(block, x, False, monkeypatch)
     assert np.array_equal(rid, rid0) and np.array_equal(rw, rw0)
     assert torch.equal(y1, y0), "fused and staged decode differ"
-    ref = _oracle_on_active(x, wr, wu, wg, wd, cfg, rw, rid)
+    w, ids, n_near, n_diff = strict_route(_f64(x), wr.cpu().numpy(), rw, rid, cfg.k, cfg.normalize)
+    print(f"{cfg.name}: near-tied tokens {n_near}, routed differently {n_diff} of {cfg.T}")
+    ref = _oracle_on_active(x, wr, wu, wg, wd, cfg, w, ids)
     err = rms_rel_maxabs(y1.float().cpu().numpy(), ref)
     assert err <= TOL, f"{cfg.name}: max-abs/rms {err:.3e}"
-    logits = wr.double().cpu().numpy() @ _f64(x).T
-    ow, oids = O.route_from_logits(logits, cfg.k, cfg.normalize)
-    assert np.all(oids == rid, axis=0).mean() >= 0.99
-    same = np.all(oids == rid, axis=0)
-    np.testing.assert_allclose(rw[:, same], ow[:, same], rtol=1e-4, atol=1e-6)
     assert ops.read_device_error() == 0
 
 
