@@ -33,7 +33,7 @@ struct PeerRows {
 //                + sum_{q<me} C[q][g]
 //   local_off[e] (e = 0..El): sum_{e'<e} sum_q C[q][me*El+e']
 __global__ void ep_plan_kernel(const int32_t* __restrict__ C, int P, int El, int me, int32_t* __restrict__ dst_base,
-                               int32_t* __restrict__ local_off) {
+                               int32_t* __restrict__ local_off, int64_t capacity, int32_t* __restrict__ err) {
   const int E = P * El;
   for (int g = threadIdx.x; g < E; g += blockDim.x) {
     const int p = g / El, e = g - p * El;
@@ -47,6 +47,12 @@ __global__ void ep_plan_kernel(const int32_t* __restrict__ C, int P, int El, int
     int32_t off = 0;
     for (int e2 = 0; e2 < e; ++e2)
       for (int q = 0; q < P; ++q) off += C[q * E + me * El + e2];
+    // rows past the receive buffer were never stored there: the GEMMs must
+    // not read them (nor map them back), so the offsets stop at capacity
+    if ((int64_t)off > capacity) {
+      off = (int32_t)capacity;
+      atomicExch(err, FRANK_EINVAL);
+    }
     local_off[e] = off;
   }
 }
@@ -131,7 +137,8 @@ int frank_ep_plan(const int32_t* counts_all, int P, int El, int rank, int32_t* d
     return FRANK_EINVAL;
   }
   cudaStream_t st = frank::as_stream(stream);
-  ep_plan_kernel<<<1, 1024, 0, st>>>(counts_all, P, El, rank, dst_base, local_offsets);
+  ep_plan_kernel<<<1, 1024, 0, st>>>(counts_all, P, El, rank, dst_base, local_offsets, capacity,
+                                     frank::device_error_word());
   FRANK_LAUNCH_CHECK();
   ep_return_map_kernel<<<P * El, 256, 0, st>>>(counts_all, P, El, rank, local_offsets, row_rank, row_pos,
                                                   capacity);

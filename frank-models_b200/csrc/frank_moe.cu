@@ -32,7 +32,8 @@ int launch_grouped_gemm_f32(int, const float*, const float*, const float*, const
                             int64_t, const float*, float*, cudaStream_t);
 int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int32_t*, int64_t, int64_t, int64_t,
                            int64_t, const float*, void*, cudaStream_t, const int32_t* row_rank = nullptr,
-                           const int32_t* row_pos = nullptr, float* const* peer_out = nullptr, int n_peers = 0);
+                           const int32_t* row_pos = nullptr, float* const* peer_out = nullptr, int n_peers = 0,
+                           int64_t peer_rows = 0);
 int check_tc_shapes(int64_t, int64_t, int64_t, int64_t);
 bool decode_path_ok(int, int64_t, int64_t, int64_t, int64_t, int64_t);
 size_t decode_workspace_size(int64_t, int64_t, int64_t, int64_t, int64_t);
@@ -452,9 +453,10 @@ int frank_expert_ffn(int dtype, const void* xs, const float* w_rows, const int32
 int frank_expert_ffn_scatter(const void* xs, const float* w_rows, const int32_t* offsets, int64_t E, int64_t rows,
                              int64_t H, int64_t F, const void* w_up_p, const void* w_gate_p, const void* w_down_p,
                              const int32_t* row_rank, const int32_t* row_pos, void* const* peer_out, int n_peers,
-                             void* workspace, size_t ws_bytes, void* stream) {
+                             int64_t peer_rows, void* workspace, size_t ws_bytes, void* stream) {
   FRANK_CHECK_ARG(E >= 1 && rows >= 0 && H >= 1 && F >= 1, "expert_ffn_scatter: bad shape");
-  FRANK_CHECK_ARG(row_rank && row_pos && peer_out && n_peers >= 1, "expert_ffn_scatter: missing row map / peers");
+  FRANK_CHECK_ARG(row_rank && row_pos && peer_out && n_peers >= 1 && peer_rows >= 0,
+                  "expert_ffn_scatter: missing row map / peers");
   if (rows == 0) return FRANK_OK;
   if (ws_bytes < frank_expert_ffn_workspace_size(FRANK_BF16, rows, F)) {
     set_error("expert_ffn_scatter: workspace %zu < %zu bytes", ws_bytes,
@@ -466,7 +468,7 @@ int frank_expert_ffn_scatter(const void* xs, const float* w_rows, const int32_t*
   FRANK_TRY(check_tc_shapes(rows, H, F, E));
   FRANK_TRY(launch_tc_grouped_gemm(0, xs, w_gate_p, w_up_p, offsets, E, rows, F, H, nullptr, workspace, st));
   return launch_tc_grouped_gemm(1, workspace, w_down_p, nullptr, offsets, E, rows, H, F, w_rows, nullptr, st,
-                                row_rank, row_pos, reinterpret_cast<float* const*>(peer_out), n_peers);
+                                row_rank, row_pos, reinterpret_cast<float* const*>(peer_out), n_peers, peer_rows);
 }
 
 int frank_combine(const float* d, const int32_t* slot_pos, int64_t T, int64_t k, int64_t H, int y_dtype, void* y,

@@ -67,8 +67,22 @@ struct Params {
   const int32_t* row_rank;
   const int32_t* row_pos;
   float* peer_out[kMaxPeers];
+  int n_peers;             // entries of peer_out in use
+  int64_t peer_rows;       // rows of every peer's return buffer
   int swap_small;          // experts with <= BM rows run as swapped (weight-row-major) tiles
 };
+
+// Destination of row `row` under a row map: another rank's return buffer.
+// A map entry outside [0, n_peers) x [0, peer_rows) is refused (nullptr, the
+// row is not stored) and recorded in the device error word.
+__device__ __forceinline__ float* mapped_row(const Params& p, int row) {
+  const int32_t q = p.row_rank[row], pos = p.row_pos[row];
+  if (q < 0 || q >= p.n_peers || pos < 0 || (int64_t)pos >= p.peer_rows || p.peer_out[q] == nullptr) {
+    atomicExch(p.err, FRANK_EINVAL);
+    return nullptr;
+  }
+  return p.peer_out[q] + (int64_t)pos * p.ldo;
+}
 
 // ------------------------------------------------------------ PTX glue --
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
@@ -199,9 +213,9 @@ __device__ __forceinline__ void epilogue_rows(const Params& p, int row, bool val
     if (valid)
       my = (unsigned long long)(reinterpret_cast<__nv_bfloat16*>(p.out) + (int64_t)row * p.ldo + n * 128);
   } else if (valid) {
-    float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
-    if (MODE == SCALE && p.row_rank != nullptr) out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
-    my = (unsigned long long)(out + n * BN);
+    float* out = MODE == SCALE && p.row_rank != nullptr ? mapped_row(p, row)
+                                                        : reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
+    if (out != nullptr) my = (unsigned long long)(out + n * BN);
   }
   // stage -> global: 8 rounds of 4 rows x 8 chunks; chunk_cols columns per
   // 16-byte chunk; col0: the stage's first column within the tile
@@ -285,11 +299,12 @@ __device__ __forceinline__ void epilogue_swapped(const Params& p, const Tile& tl
       for (int i = 0; i < 16; ++i) {
         if (i < nt) {
           const int row = tl.m0 + t0 + i;
-          float* out = reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
-          if (MODE == SCALE && p.row_rank != nullptr) out = p.peer_out[p.row_rank[row]] + (int64_t)p.row_pos[row] * p.ldo;
+          float* out = MODE == SCALE && p.row_rank != nullptr
+                           ? mapped_row(p, row)
+                           : reinterpret_cast<float*>(p.out) + (int64_t)row * p.ldo;
           const float sc = MODE == SCALE ? p.wrow[row] : 1.f;
-          if (c0 < p.N_out) out[c0] = v0[i] * sc;
-          if (c1 < p.N_out) out[c1] = v1[i] * sc;
+          if (out != nullptr && c0 < p.N_out) out[c0] = v0[i] * sc;
+          if (out != nullptr && c1 < p.N_out) out[c1] = v1[i] * sc;
         }
       }
     }
@@ -778,7 +793,8 @@ int check_tc_shapes(int64_t rows, int64_t N, int64_t K, int64_t E) {
 // (out fp32 [rows, N]).  A: bf16 [rows, K]; B/B2: bf16 [E, N, K].
 int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B2, const int32_t* offsets, int64_t E,
                            int64_t rows, int64_t N, int64_t K, const float* wrow, void* out, cudaStream_t st,
-                           const int32_t* row_rank, const int32_t* row_pos, float* const* peer_out, int n_peers) {
+                           const int32_t* row_rank, const int32_t* row_pos, float* const* peer_out, int n_peers,
+                           int64_t peer_rows) {
   if (rows == 0) return FRANK_OK;
   FRANK_TRY(check_tc_shapes(rows, N, K, E));
   if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)(B2 ? B2 : B) | (uintptr_t)out) % 16 != 0) {
@@ -806,6 +822,8 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
   p.row_rank = row_rank;
   p.row_pos = row_pos;
   for (int i = 0; i < kMaxPeers; ++i) p.peer_out[i] = (peer_out && i < n_peers) ? peer_out[i] : nullptr;
+  p.n_peers = row_rank ? n_peers : 0;
+  p.peer_rows = peer_rows;
   {
     const char* sw = getenv("FRANK_TC_SWAP");
     p.swap_small = (sw && sw[0] == '0') ? 0 : 1;

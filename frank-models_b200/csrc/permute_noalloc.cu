@@ -17,7 +17,11 @@
 // names a host-side stand-in).  The device address is looked up once per
 // device with cudaGetSymbolAddress, with that device current, on the first
 // call made on the device; that first call should therefore come before
-// any stream capture.
+// any stream capture.  The looked-up address is cached per device ordinal
+// for the life of the process, which assumes one context per device: after
+// cudaDeviceReset (or anything else that destroys and recreates the
+// device's primary context) the module is reloaded, the array may move, and
+// this entry point must not be called again in that process.
 //
 // All calls share the one array, which keeps whatever the last call left in
 // it: calls that overlap on the GPU (different streams, or different host

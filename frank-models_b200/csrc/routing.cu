@@ -417,7 +417,7 @@ static int launch_router_vec(const void* x, const void* wr, int64_t T, int64_t H
 
 int launch_tc_grouped_gemm(int, const void*, const void*, const void*, const int32_t*, int64_t, int64_t, int64_t,
                            int64_t, const float*, void*, cudaStream_t, const int32_t*, const int32_t*, float* const*,
-                           int);
+                           int, int64_t);
 
 static bool router_tc_ok(int x_dtype, int64_t T, int64_t H, int64_t E) {
   return x_dtype == FRANK_BF16 && E >= 16 && E % 16 == 0 && E <= kMaxE && H % 8 == 0 && T >= 128;
@@ -444,7 +444,7 @@ static int launch_router_tc(const void* x, int wr_dtype, const void* wr, int64_t
                                                                 offs);
   FRANK_LAUNCH_CHECK();
   FRANK_TRY(launch_tc_grouped_gemm(2, x, wr3, nullptr, offs, 1, T, 3 * E, H, nullptr, l3, st, nullptr, nullptr,
-                                   nullptr, 0));
+                                   nullptr, 0, 0));
   softmax_topk3_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(l3, T, (int)E, (int)k, normalize, w, ids);
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;

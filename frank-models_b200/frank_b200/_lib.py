@@ -64,7 +64,7 @@ SIGNATURES = {
     "frank_ep_dispatch": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp,
                                    _c_vp, _c_int, _c_i64, _c_vp]),
     "frank_expert_ffn_scatter": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp,
-                                          _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_size, _c_vp]),
+                                          _c_vp, _c_vp, _c_vp, _c_int, _c_i64, _c_vp, _c_size, _c_vp]),
     "frank_read_device_error": (_c_int, [_c_vp, _c_vp]),
     "frank_launch_count": (ctypes.c_uint64, []),
     "frank_selftest_bounded_wait": (_c_int, [_c_i64, _c_vp, _c_vp]),

@@ -20,7 +20,7 @@ tokens; a step is
 Each token row is processed by exactly the same kernels with the same
 accumulation order as on one GPU, so the result equals the single-GPU
 result bit for bit.  The row counts are read on the host once per step
-(they size the all-to-all-v).
+(they size the all-to-all-v, or the peer buffers of the p2p mode).
 
 The device primitives are reached through ``prims`` (default: the C ABI
 via :mod:`frank_b200.ops`) so that the host-side exchange logic can be
@@ -217,22 +217,27 @@ class ExpertParallelMoE:
         return self._call_nccl(x, out)
 
     # ------------------------------------------------------------ p2p mode --
-    def _symmetric(self, T: int, dev):
-        """Symmetric receive / return buffers sized for T tokens per rank (every
-        rank calls with the same T; the dispatch kernel refuses rows beyond the
-        capacity):
-        recv_x [P*k*T, H] bf16, recv_w [P*k*T] fp32, ret [k*T, H] fp32, and the
-        peer addresses of every rank's copy.  Allocated collectively."""
-        if self._symm is not None and self._symm["T"] >= T:
-            return self._symm
+    def _symmetric(self, T: int, rows: int, dev):
+        """Symmetric receive / return buffers: recv_x [cap, H] bf16, recv_w [cap]
+        fp32 (cap >= the most rows any rank receives this step), ret [k*Tmax, H]
+        fp32 (Tmax >= every rank's token count), hs [cap, F] bf16, and the peer
+        addresses of every rank's copy.  ``T`` and ``rows`` are the same on
+        every rank (derived from the all-gathered counts), so every rank takes
+        the same grow-or-keep decision and the collective allocation below is
+        entered by all of them or by none.  Buffers only grow (by 25% headroom)."""
+        S = self._symm
+        if S is not None and S["T"] >= T and S["cap"] >= rows:
+            return S
         import os
 
         # plain peer mappings only: no multicast object is bound to these buffers
         os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
         import torch.distributed._symmetric_memory as symm_mem
 
-        H, k, P = self.H, self.k, self.P
-        cap, n = P * k * T, k * T
+        H, k = self.H, self.k
+        T = max(T, S["T"] if S else 0)
+        cap = max(rows + rows // 4, S["cap"] if S else 0, 1)
+        n = k * T
 
         def al(b):
             return (b + 255) // 256 * 256
@@ -248,8 +253,9 @@ class ExpertParallelMoE:
         import ctypes
 
         arr = lambda vals: (ctypes.c_void_p * self.P)(*vals)  # noqa: E731
+        counts = S["counts"] if S else torch.empty((self.P, self.E), dtype=torch.int32, device=dev)
         self._symm = {
-            "T": T, "buf": buf, "hdl": hdl, "cap": cap,
+            "T": T, "buf": buf, "hdl": hdl, "cap": cap, "ret_rows": n,
             "recv_x": buf[base[0]:base[0] + cap * H * 2].view(torch.bfloat16).view(cap, H),
             "recv_w": buf[base[1]:base[1] + cap * 4].view(torch.float32),
             "ret": buf[base[2]:base[2] + n * H * 4].view(torch.float32).view(n, H),
@@ -260,11 +266,20 @@ class ExpertParallelMoE:
             "local_off": torch.empty(self.El + 1, dtype=torch.int32, device=dev),
             "row_rank": torch.empty(cap, dtype=torch.int32, device=dev),
             "row_pos": torch.empty(cap, dtype=torch.int32, device=dev),
-            "counts": torch.empty((self.P, self.E), dtype=torch.int32, device=dev),
+            "counts": counts,
             "flag": torch.zeros(1, dtype=torch.int32, device=dev),
-            "hs": torch.empty(max(cap * self.F * 2 + 256, 1), dtype=torch.uint8, device=dev),
+            "hs": torch.empty(cap * self.F * 2 + 256, dtype=torch.uint8, device=dev),
         }
         return self._symm
+
+    def step_sizes(self, counts: np.ndarray):
+        """(max tokens of any rank, max rows any rank receives) from the
+        all-gathered per-expert counts [P, E]: rank q routed counts[q].sum()
+        = k * T_q slots; rank r receives the column block of its experts."""
+        counts = np.asarray(counts, dtype=np.int64)
+        t_max = int(counts.sum(axis=1).max()) // self.k
+        per_rank = counts.sum(axis=0).reshape(self.P, self.El).sum(axis=1)
+        return t_max, int(per_rank.max())
 
     def _barrier(self, flag):
         # stream-ordered: every rank's preceding kernels (and their stores into
@@ -278,7 +293,8 @@ class ExpertParallelMoE:
         dev = x.device
         lib = _lib.load()
         st = torch.cuda.current_stream().cuda_stream
-        S = self._symmetric(T, dev)
+        if self._symm is None:
+            self._counts = torch.empty((self.P, self.E), dtype=torch.int32, device=dev)
         if self.profile:
             self._marks.append([])
         self._mark()
@@ -286,7 +302,12 @@ class ExpertParallelMoE:
         sorted_slots, offsets, slot_pos, _ = ops.permute(ids, self.E)
         cnt = (offsets[1:] - offsets[:-1]).contiguous()
         self._mark()
-        dist.all_gather_into_tensor(S["counts"], cnt, group=self.group)
+        counts = self._symm["counts"] if self._symm is not None else self._counts
+        dist.all_gather_into_tensor(counts, cnt, group=self.group)
+        # the one host read per step: the buffers are sized from the counts
+        # every rank now holds, so no rank can plan past a receive buffer
+        t_max, rows_max = self.step_sizes(counts.cpu().numpy())
+        S = self._symmetric(t_max, rows_max, dev)
         _lib.check(lib.frank_ep_plan(S["counts"].data_ptr(), self.P, self.El, self.rank, S["dst_base"].data_ptr(),
                                      S["local_off"].data_ptr(), S["row_rank"].data_ptr(), S["row_pos"].data_ptr(),
                                      S["cap"], st))
@@ -299,12 +320,12 @@ class ExpertParallelMoE:
         _lib.check(lib.frank_expert_ffn_scatter(
             S["recv_x"].data_ptr(), S["recv_w"].data_ptr(), S["local_off"].data_ptr(), self.El, S["cap"], H, self.F,
             self.w_up.data_ptr(), self.w_gate.data_ptr(), self.w_down.data_ptr(), S["row_rank"].data_ptr(),
-            S["row_pos"].data_ptr(), S["peer_ret"], self.P, S["hs"].data_ptr(), S["hs"].numel(), st))
+            S["row_pos"].data_ptr(), S["peer_ret"], self.P, S["ret_rows"], S["hs"].data_ptr(), S["hs"].numel(), st))
         self._mark()
         self._barrier(S["flag"])
         self._mark()
         y = out if out is not None else torch.empty((T, H), dtype=self.out_dtype, device=dev)
-        ops.combine(S["ret"], slot_pos, T, self.k, y)
+        ops.combine(S["ret"][:self.k * T], slot_pos, T, self.k, y)
         self._mark()
         return y
 

@@ -126,8 +126,9 @@ int frank_permute(const int32_t* ids, int64_t n_slots, int64_t E,
  * library until exit.  Returns FRANK_EINVAL when
  * frank_permute_workspace_size(n_slots, E) exceeds it (1 MiB covers, e.g.,
  * 65536 slots with any E <= 1024).  The first call on a device looks up the
- * array's device address and should come before any stream capture.  All
- * calls share the array: calls that overlap on the GPU race and must be
+ * array's device address and should come before any stream capture; the
+ * address is cached for the process's life (one context per device: do not
+ * call it again after cudaDeviceReset).  All calls share the array: calls that overlap on the GPU race and must be
  * serialised by the caller.  Allocates nothing.
  */
 #define FRANK_PERMUTE_NOALLOC_SCRATCH_BYTES (1u << 20)
@@ -269,7 +270,12 @@ int frank_copy_row_segments(const void* src, void* dst,
  *   device error word (frank_read_device_error).
  * frank_expert_ffn_scatter: frank_expert_ffn (bf16) whose fp32 output row r
  *   is stored at peer_out[row_rank[r]] + row_pos[r] * H, i.e. straight into
- *   the return buffer of the rank the row came from.
+ *   the return buffer of the rank the row came from.  Every return buffer
+ *   holds peer_rows rows; a map entry outside [0, n_peers) x [0, peer_rows)
+ *   is not stored and records FRANK_EINVAL in the device error word.
+ * frank_ep_plan clamps the local expert offsets to `capacity`, so rows
+ *   beyond the receive buffer are never read by the GEMMs either (and
+ *   FRANK_EINVAL is recorded when the gathered counts exceed it).
  * Stores to other GPUs complete with the kernels; the caller orders the
  *   ranks' steps (e.g. an NCCL collective on the same stream) before a rank
  *   reads what its peers wrote.  No kernel here waits on another GPU.
@@ -289,7 +295,8 @@ int frank_expert_ffn_scatter(const void* xs, const float* w_rows,
                              const void* w_gate_p, const void* w_down_p,
                              const int32_t* row_rank, const int32_t* row_pos,
                              void* const* peer_out, int n_peers,
-                             void* workspace, size_t ws_bytes, void* stream);
+                             int64_t peer_rows, void* workspace,
+                             size_t ws_bytes, void* stream);
 
 /*
  * Device error word written by bounded waits inside the persistent GEMM

@@ -1,6 +1,8 @@
 """Expert parallelism on real GPUs (NCCL): every rank's output must equal the
-single-GPU block on the same tokens bit for bit.  Needs >= 2 visible GPUs;
-ranks are child processes, one per GPU."""
+single-GPU block on the same tokens bit for bit, also when the ranks hold
+different numbers of tokens (the peer buffers are sized from the gathered
+counts of every step).  Needs >= 2 visible GPUs; ranks are child processes,
+one per GPU."""
 
 import os
 import socket
@@ -20,7 +22,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, cfg, mode, q):
+def _worker(rank, world, port, cfg, mode, ragged, q):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -32,10 +34,16 @@ def _worker(rank, world, port, cfg, mode, q):
 
         wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, dev, seed=0)
         x = configs.block_x_torch(cfg, dev, seed=10 + rank)
+        if ragged:  # rank r holds T - 37 r tokens
+            x = x[:cfg.T - 37 * rank].contiguous()
         El = cfg.E // world
         sl = slice(rank * El, (rank + 1) * El)
         moe = ep.ExpertParallelMoE(wr, wu[sl].contiguous(), wg[sl].contiguous(), wd[sl].contiguous(), cfg.E, cfg.k,
                                    cfg.normalize, mode=mode)
+        y = moe(x)
+        if ragged and rank == world - 1:
+            # the last rank's batch grows to T: every rank's buffers grow together
+            x = configs.block_x_torch(cfg, dev, seed=99)
         y = moe(x)
         y2 = moe(x)
         single = ops.MoEFFNBlock(wr, ops.PackedExperts(wu), ops.PackedExperts(wg), ops.PackedExperts(wd), cfg.E,
@@ -49,9 +57,10 @@ def _worker(rank, world, port, cfg, mode, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+@pytest.mark.parametrize("ragged", [False, True], ids=["equal_T", "ragged_T"])
 @pytest.mark.parametrize("mode", ["p2p", "nccl"])
 @pytest.mark.parametrize("cfg_name", ["bf16_fg_ep", "bf16_c3like_ep"])
-def test_ep_equals_single_gpu(cfg_name, mode):
+def test_ep_equals_single_gpu(cfg_name, mode, ragged):
     from frank_b200 import configs
 
     cfg = {
@@ -66,7 +75,7 @@ def test_ep_equals_single_gpu(cfg_name, mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, mode, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, mode, ragged, q)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
