@@ -7,16 +7,22 @@ At N=1 the workload is the Mixtral-8x7B block (T=16384, H=4096, F=14336,
 E=8, top-2, bf16, fp32 accumulation).  With N>1 (launched by torchrun, one
 process per GPU, NCCL) every rank holds T tokens and E/N experts and the
 block runs expert-parallel: tokens are dispatched to the ranks owning their
-experts and the results combined back (weak scaling: T tokens per rank).
+experts and the results combined back.  Scaling is strong: the global
+batch stays T tokens, each rank holds T/N of them (the weak-scaling figure,
+T tokens per rank, is reported under "weak").  The default N=1 run also
+measures the decode blocks (T=1, T=8) and the fine-grained Zipf block under
+"extra_configs".
 
 Printed (rank 0, one JSON line):
   value       tokens/s over all ranks, inputs resident in HBM, device-timed with
               CUDA events, max over ranks
   e2e         the same through the public API with the step's x copied from
               pinned host memory and y copied back inside the timed region
-  roofline    the gate/up GEMM (dominant kernel): algorithmic flops per launch /
-              its CUDA-event duration inside the timed region, against the
-              measured dense bf16 peak
+  roofline    the dominant kernel (gate/up GEMM, or the fused decode kernel):
+              algorithmic flops or bytes per launch / its CUDA-event duration
+              (a separate loop of the same steps with events between the
+              stages), against the measured peak (burst bf16 for a timed
+              region under 2 s, HBM copy bandwidth for decode)
   cpu_baseline the CPU restatement of the reference (NumPy, grouped form) on a
               bounded token sample, rank 0 at N=1
 --impl reference times that CPU restatement alone (the reference is a NumPy
@@ -48,6 +54,8 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 # per-expert GEMM (4096 rows x 4096 x 2*14336) for 8 experts instead of 2, so
 # its traffic is that capture x 4.
 GATE_UP_TRAFFIC_BYTES = {"c3_mixtral_8x7b": 4 * (558.111e6 + 223.502e6)}
+GATE_UP_TRAFFIC_SOURCE = {"c3_mixtral_8x7b": "ncu DRAM read + write of one gate/up launch on the C3-shaped "
+                                             "2-expert case, x 4 (8 experts of the same GEMM shape)"}
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one decode_fused_kernel
 # launch of the same workload (seed 0, 8 distinct experts), captured by ncu
@@ -190,7 +198,7 @@ def run_reference(args, cfg):
     line = {
         "impl": "reference", "metric": METRIC, "value": v, "unit": "tokens/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": sec * 1e3, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": config_dict(cfg, world),
         "cpu_baseline": {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port",
                          "sample": f"{Ts} of {cfg.T} tokens per step, full H/F/E weights; the NumPy oracle's "
@@ -201,191 +209,133 @@ def run_reference(args, cfg):
 
 
 def config_dict(cfg, world):
-    return {"workload": cfg.name, "tokens_per_rank": cfg.T, "global_batch": cfg.T * world, "n_embd": cfg.H,
+    return {"workload": cfg.name, "tokens_per_rank": cfg.T // world, "global_batch": cfg.T, "n_embd": cfg.H,
             "n_ff": cfg.F, "n_expert": cfg.E, "n_expert_used": cfg.k, "normalize_weights": cfg.normalize,
             "parallelism": f"ep{world}",
             "l2": "inputs larger than L2: expert weights and per-step activations exceed the 126 MB L2"}
 
 
 # ----------------------------------------------------------------- GPU arm --
-def run_frank(args, cfg):
-    import numpy as np
+def _barrier(dist):
+    import torch
+
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def _max_over_ranks(dist, dev, v: float) -> float:
+    import torch
+
+    if dist is None:
+        return v
+    t = torch.tensor([v], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _gemm_peak(pk, timed_s):
+    """The bf16 denominator: the burst figure for a kernel timed in a region
+    shorter than ~2 s (the clocks stay near maximum), else the sustained one."""
+    key = "bf16_tflops" if timed_s < 2.0 else "bf16_tflops_sustained"
+    return float(pk[key]), key
+
+
+def bench_block_1gpu(args, cfg, dev, local, cpu=True):
+    """One configuration on one GPU.  Returns the measurement dict (value,
+    ms_per_step, roofline, stage_ms, e2e, gpu_launches, clocks, cpu_baseline)."""
     import torch
 
     from frank_b200 import configs, ops
 
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    graphed = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", device_id=dev)
-        from frank_b200 import ep
-
-        runner = ep.ExpertParallelMoE.synthetic(cfg, rank, world, dev, seed=0)
-        block_call = runner.__call__
-    else:
-        runner = None
-        dist = None
-        wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, dev, seed=0)
-        block = ops.MoEFFNBlock(wr, ops.PackedExperts(wu), ops.PackedExperts(wg), ops.PackedExperts(wd), cfg.E,
-                                cfg.k, cfg.normalize, dtype=torch.bfloat16, out_dtype=torch.float32)
-        block_call = block.__call__
-        graphed = None
-        if cfg.T <= 64:
-            # decode steps are launch-bound: replay the block from a CUDA graph
-            l_cap = ops.launch_count()
-            graphed = ops.GraphedMoEFFN(block, cfg.T, dev)
-            graphed_launches = (ops.launch_count() - l_cap) // 2  # warm-up call + captured call
-            block_call = graphed.__call__
-    x = configs.block_x_torch(cfg, dev, seed=rank)
+    wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, dev, seed=0)
+    block = ops.MoEFFNBlock(wr, ops.PackedExperts(wu), ops.PackedExperts(wg), ops.PackedExperts(wd), cfg.E,
+                            cfg.k, cfg.normalize, dtype=torch.bfloat16, out_dtype=torch.float32)
+    x = configs.block_x_torch(cfg, dev, seed=0)
     y = torch.empty((cfg.T, cfg.H), dtype=torch.float32, device=dev)
-    e2e_call = block_call
-    if graphed is not None:
-        graphed.x.copy_(x)  # the resident input of the timed replays
-
-        def block_call(x_, out=None):  # noqa: F811 -- value loop: replay only, x already resident
-            return graphed.replay()
     stream = torch.cuda.current_stream()
+    decode = cfg.T <= 64
+    graphed = None
+    if decode:
+        # decode steps are launch-bound: replay the block from a CUDA graph
+        l_cap = ops.launch_count()
+        graphed = ops.GraphedMoEFFN(block, cfg.T, dev)
+        graphed_launches = (ops.launch_count() - l_cap) // 2  # warm-up call + captured call
+        graphed.x.copy_(x)
 
-    def barrier():
-        torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier()
-        torch.cuda.synchronize()
-
-    def max_over_ranks(v: float) -> float:
-        if dist is None:
-            return v
-        t = torch.tensor([v], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        def step():
+            graphed.replay()
+    else:
+        def step():
+            block(x, out=y)
 
     for _ in range(args.warmup):
-        block_call(x, out=y)
-    barrier()
+        step()
+    _barrier(None)
 
-    # ---- value: inputs resident in HBM -------------------------------------
-    ops.profile_stages(True)
-    if runner is not None:
-        runner.profile = True
+    # ---- value: inputs resident in HBM, no instrumentation in the loop ------
     # Decode-sized steps touch less than the 126 MB L2 (T=1 reads ~75 MB of
     # weights): flush L2 between steps (a 256 MiB write, outside the timed
     # spans) and time every step on its own.
-    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if cfg.T <= 64 else None
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if decode else None
     l0 = ops.launch_count()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     step_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)] if flush is not None else []
+               for _ in range(args.steps)] if decode else []
     with ClockSampler(local) as clk:
-        barrier()
+        _barrier(None)
         ev0.record(stream)
         for i in range(args.steps):
-            if flush is not None:
+            if decode:
                 flush.zero_()
                 step_ev[i][0].record(stream)
-            block_call(x, out=y)
-            if flush is not None:
+            step()
+            if decode:
                 step_ev[i][1].record(stream)
         ev1.record(stream)
-        barrier()
-    launches = ops.launch_count() - l0
-    ops.profile_stages(False)
-    if world == 1 and graphed is not None:
-        # The timed graph carries no stage events; a second capture of the same
-        # block with events between the stages gives the per-stage device times
-        # (replayed with the same L2 flush, averaged).
-        launches = graphed_launches * args.steps
+        _barrier(None)
+    launches = graphed_launches * args.steps if decode else ops.launch_count() - l0
+    region_ms = ev0.elapsed_time(ev1)
+    ms = (sum(a.elapsed_time(b) for a, b in step_ev) if decode else region_ms) / args.steps
+
+    # ---- per-stage device times: a separate loop of the same steps ---------
+    n_prof = min(args.steps, 10)
+    acc = {}
+    if decode:
+        # the timed graph carries no stage events; a second capture of the same
+        # block records events between the stages (replayed with the same flush)
         ops.profile_stages(2)
         g2 = ops.GraphedMoEFFN(block, cfg.T, dev)
         ops.profile_stages(False)
-        acc = {}
-        for _ in range(args.steps):
+        g2.x.copy_(x)
+        for _ in range(n_prof):
             flush.zero_()
-            g2.x.copy_(x)
             g2.replay()
             for kk, vv in ops.profile_read().items():
-                acc[kk] = acc.get(kk, 0.0) + vv / args.steps
-        stage_ms = acc
+                acc[kk] = acc.get(kk, 0.0) + vv / n_prof
         del g2
     else:
-        stage_ms = ops.profile_read() if world == 1 else {}
-    ep_info = None
-    if runner is not None:
-        runner.profile = False
-        mine = {"rank": rank, "phase_ms": runner.phase_ms(), "rows_received": runner.rows_received(), "mode": runner.mode}
-        ep_info = [None] * world
-        dist.all_gather_object(ep_info, mine)
-    if flush is not None:
-        ms = max_over_ranks(sum(a.elapsed_time(b) for a, b in step_ev)) / args.steps
-    else:
-        ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
-    value = cfg.T * world / (ms / 1e3)
-    n_distinct = None
-    if world == 1:
-        _, _, rid = block(x, return_routing=True)
-        n_distinct = int(torch.unique(rid).numel())
-
-    # ---- e2e: host x in, host y out, through the public API ---------------
-    x_host = x.cpu().pin_memory()
-    y_host = torch.empty((cfg.T, cfg.H), dtype=torch.float32).pin_memory()
-    x_dev = torch.empty_like(x)
-    pipe = None
-    if graphed is None and cfg.T >= 1024:
-        del y
-        torch.cuda.empty_cache()
-        pipe = ops.HostPipeline(e2e_call, cfg.T, cfg.H, x.dtype, torch.float32, depth=2, device=dev)
-
-    def e2e_step(last):
-        if graphed is not None or cfg.T < 1024:
-            # decode: one copy each way around the (graph-replayed) block
-            x_dev.copy_(x_host, non_blocking=True)
-            e2e_call(x_dev, out=y)
-            y_host.copy_(y, non_blocking=True)
-        else:
-            # public host-buffer API: every step copies its tokens in and its
-            # result out; the copies of neighbouring steps overlap this
-            # step's block on separate streams; the last copy out is waited for
-            done = pipe.submit(x_host, y_host)
-            if last:
-                stream.wait_event(done)
-
-    for i in range(min(args.warmup, 2)):
-        e2e_step(True)
-    barrier()
-    ev0.record(stream)
-    for i in range(args.steps):
-        e2e_step(i == args.steps - 1)
-    ev1.record(stream)
-    barrier()
-    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1)) / args.steps
-    e2e = {"value": cfg.T * world / (e2e_ms / 1e3), "unit": "tokens/s",
-           "h2d_bytes_per_step": x_host.numel() * x_host.element_size() * world,
-           "d2h_bytes_per_step": y_host.numel() * y_host.element_size() * world}
-
-    if rank != 0:
-        if dist is not None:
-            dist.barrier()
-            dist.destroy_process_group()
-        return
+        ops.profile_stages(True)
+        for _ in range(n_prof):
+            block(x, out=y)
+            for kk, vv in ops.profile_read().items():
+                acc[kk] = acc.get(kk, 0.0) + vv / n_prof
+        ops.profile_stages(False)
+    stage_ms = acc
+    _, _, rid = block(x, return_routing=True)
+    rid_h = rid.cpu()
+    n_distinct = int(torch.unique(rid_h).numel())
+    rows = torch.bincount(rid_h.reshape(-1).long(), minlength=cfg.E)
 
     pk, pk_kind = peaks()
-    line = {
-        "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-        "dtype": "bf16", "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; no dataset)",
-        "config": config_dict(cfg, world),
-        "tflops": cfg.flops * world / (ms / 1e3) / 1e12,
-    }
-    if flush is not None:
-        line["config"]["l2"] = "L2 flushed (256 MiB write) before every timed step; steps timed individually"
-    if stage_ms and cfg.T <= 64:
-        # decode: weight streaming, HBM-bound.  Algorithmic bytes of the block =
+    res = {"value": cfg.T / (ms / 1e3), "unit": "tokens/s", "ms_per_step": ms,
+           "tflops": cfg.flops / (ms / 1e3) / 1e12, "config": config_dict(cfg, 1), "stage_ms": stage_ms,
+           "gpu_launches": int(launches), "clocks": clk.summary()}
+    if decode:
+        res["config"]["l2"] = "L2 flushed (256 MiB write) before every timed step; steps timed individually"
+        # weight streaming, HBM-bound.  Algorithmic bytes of the block =
         # distinct experts x 3 matrices x F x H bf16 + router + activations.
-        # Small decode blocks run as one fused kernel, so the roofline kernel
-        # is the whole block (the sum of the recorded stages).
         blk_bytes = (n_distinct * 3 * cfg.F * cfg.H * 2 + cfg.E * cfg.H * 4 + cfg.T * cfg.H * 2 + cfg.T * cfg.H * 4)
         fused = cfg.k * cfg.T <= cfg.E
         # fused: the one cooperative launch sits between the first two stage
@@ -395,41 +345,216 @@ def run_frank(args, cfg):
         k_bytes = blk_bytes if fused else (n_distinct * 2 * cfg.F * cfg.H * 2 + cfg.k * cfg.T * (cfg.H + cfg.F) * 2)
         achieved = k_bytes / (k_ms / 1e3) / 1e9
         peak = float(pk["hbm_gbs"])
-        line["roofline"] = {
+        tr = DECODE_TRAFFIC_BYTES.get(cfg.name) if fused else None
+        res["roofline"] = {
             "kernel": "decode_fused_kernel (whole block)" if fused else "tc_grouped_gemm<SWIGLU> (gate/up GEMM + swiglu)",
             "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-            "peak_source": f"{pk_kind} hbm_gbs",
-            "traffic": DECODE_TRAFFIC_BYTES.get(cfg.name) if fused else None,
-            "bytes_per_launch": k_bytes, "ms_per_launch": k_ms,
-            "distinct_experts": n_distinct,
+            "peak_source": f"{pk_kind} hbm_gbs", "traffic": tr,
+            "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch, same workload"
+                              if tr else None,
+            "bytes_per_launch": k_bytes, "ms_per_launch": k_ms, "distinct_experts": n_distinct,
         }
-        line["stage_ms"] = stage_ms
-        line["block_hbm_gbs"] = blk_bytes / (ms / 1e3) / 1e9
-        line["block_frac_of_hbm"] = line["block_hbm_gbs"] / peak
-    elif stage_ms:
+        res["block_hbm_gbs"] = blk_bytes / (ms / 1e3) / 1e9
+        res["block_frac_of_hbm"] = res["block_hbm_gbs"] / peak
+    else:
         gu_flops = 4.0 * cfg.k * cfg.T * cfg.H * cfg.F
         gu_ms = stage_ms["gate_up_gemm"]
         achieved = gu_flops / (gu_ms / 1e3) / 1e12
-        peak = float(pk["bf16_tflops_sustained"])
-        line["roofline"] = {
+        peak, peak_key = _gemm_peak(pk, region_ms / 1e3)
+        tr = GATE_UP_TRAFFIC_BYTES.get(cfg.name)
+        res["roofline"] = {
             "kernel": "tc_grouped_gemm<SWIGLU> (gate/up GEMM + swiglu)", "bound": "tensor",
             "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
-            "peak_source": f"{pk_kind} bf16_tflops_sustained", "traffic": GATE_UP_TRAFFIC_BYTES.get(cfg.name),
+            "peak_source": f"{pk_kind} {peak_key} (timed region {region_ms / 1e3:.2f} s)",
+            "frac_of_sustained": achieved / float(pk["bf16_tflops_sustained"]),
+            "traffic": tr, "traffic_source": GATE_UP_TRAFFIC_SOURCE.get(cfg.name) if tr else None,
             "flops_per_launch": gu_flops, "ms_per_launch": gu_ms,
+            "stage_ms_from": f"separate loop of {n_prof} steps with stage events",
         }
-        line["stage_ms"] = stage_ms
-        line["block_frac_of_peak"] = line["tflops"] / peak
-    if ep_info:
-        line["ep_ranks"] = ep_info
-    line["e2e"] = e2e
-    line["gpu_launches"] = int(launches)
-    line["clocks"] = clk.summary()
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline_from_device(cfg, x, block if world == 1 else None)
+        res["block_frac_of_peak"] = res["tflops"] / peak
+    if cfg.E >= 16:
+        res["rows_per_expert"] = {"max": int(rows.max()), "mean": float(rows.float().mean()),
+                                  "below_64": int((rows < 64).sum())}
+
+    # ---- e2e: host x in, host y out, through the public API ---------------
+    x_host = x.cpu().pin_memory()
+    y_host = torch.empty((cfg.T, cfg.H), dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+    pipe = None
+    if not decode and cfg.T >= 1024:
+        pipe = ops.HostPipeline(block, cfg.T, cfg.H, x.dtype, torch.float32, depth=2, device=dev)
+
+    def e2e_step(last):
+        if pipe is None:
+            # one copy each way around the (graph-replayed) block
+            x_dev.copy_(x_host, non_blocking=True)
+            if graphed is not None:
+                graphed(x_dev, out=y)
+            else:
+                block(x_dev, out=y)
+            y_host.copy_(y, non_blocking=True)
+        else:
+            # public host-buffer API: every step copies its tokens in and its
+            # result out; the copies of neighbouring steps overlap this
+            # step's block on separate streams; the last copy out is waited for
+            done = pipe.submit(x_host, y_host)
+            if last:
+                stream.wait_event(done)
+
+    for _ in range(min(args.warmup, 2)):
+        e2e_step(True)
+    _barrier(None)
+    ev0.record(stream)
+    for i in range(args.steps):
+        e2e_step(i == args.steps - 1)
+    ev1.record(stream)
+    _barrier(None)
+    e2e_ms = ev0.elapsed_time(ev1) / args.steps
+    res["e2e"] = {"value": cfg.T / (e2e_ms / 1e3), "unit": "tokens/s",
+                  "h2d_bytes_per_step": x_host.numel() * x_host.element_size(),
+                  "d2h_bytes_per_step": y_host.numel() * y_host.element_size()}
+    del pipe
+    if cpu:
+        res["cpu_baseline"] = cpu_baseline_from_device(cfg, x, block)
+    return res
+
+
+def run_frank(args, cfg):
+    import torch
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        return run_frank_ep(args, cfg, dev, rank, world, local)
+    res = bench_block_1gpu(args, cfg, dev, local, cpu=not args.no_cpu_baseline)
+    torch.cuda.empty_cache()
+    line = {
+        "metric": METRIC, "value": res.pop("value"), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": res.pop("ms_per_step"), "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; no dataset)",
+    }
+    line.update(res)
+    if args.extras and cfg.name == configs_default():
+        from frank_b200 import configs
+
+        extra = {}
+        for c in (configs.c5(1), configs.c5(8), configs.C4):
+            r = bench_block_1gpu(args, c, dev, local, cpu=not args.no_cpu_baseline)
+            torch.cuda.empty_cache()
+            extra[c.name] = r
+        line["extra_configs"] = extra
     print(json.dumps(line), flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+
+
+def configs_default():
+    return "c3_mixtral_8x7b"
+
+
+def run_frank_ep(args, cfg, dev, rank, world, local):
+    """Expert parallelism over ``world`` GPUs: strong scaling at the
+    configuration's global token count (each rank holds T / world of the
+    same seeded tokens) for ``value``; the weak-scaling figure (T tokens per
+    rank) rides along under ``weak``."""
+    import torch
+    import torch.distributed as dist
+
+    from frank_b200 import configs, ep, ops
+
+    dist.init_process_group("nccl", device_id=dev)
+    runner = ep.ExpertParallelMoE.synthetic(cfg, rank, world, dev, seed=0)
+    stream = torch.cuda.current_stream()
+
+    def measure(cfg, T_rank, x, e2e=True):
+        y = torch.empty((T_rank, cfg.H), dtype=torch.float32, device=dev)
+        for _ in range(args.warmup):
+            runner(x, out=y)
+        _barrier(dist)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = ops.launch_count()
+        with ClockSampler(local) as clk:
+            _barrier(dist)
+            ev0.record(stream)
+            for _ in range(args.steps):
+                runner(x, out=y)
+            ev1.record(stream)
+            _barrier(dist)
+        launches = ops.launch_count() - l0
+        ms = _max_over_ranks(dist, dev, ev0.elapsed_time(ev1)) / args.steps
+        # phases and rows received: a separate profiled loop
+        runner.profile = True
+        for _ in range(min(args.steps, 5)):
+            runner(x, out=y)
+        runner.profile = False
+        mine = {"rank": rank, "phase_ms": runner.phase_ms(), "rows_received": runner.rows_received(),
+                "mode": runner.mode}
+        info = [None] * world
+        dist.all_gather_object(info, mine)
+        out = {"value": cfg.T * (world if T_rank == cfg.T else 1) / (ms / 1e3), "ms_per_step": ms,
+               "tokens_per_rank": T_rank, "gpu_launches": int(launches), "clocks": clk.summary(),
+               "ep_ranks": info}
+        r = [i["rows_received"] for i in info]
+        out["rows_per_rank"] = {"max": max(r), "mean": sum(r) / len(r), "max_over_mean": max(r) / (sum(r) / len(r))}
+        if e2e:
+            x_host = x.cpu().pin_memory()
+            y_host = torch.empty((T_rank, cfg.H), dtype=torch.float32).pin_memory()
+            del y
+            torch.cuda.empty_cache()
+            pipe = ops.HostPipeline(runner, T_rank, cfg.H, x.dtype, torch.float32, depth=2, device=dev)
+            for _ in range(2):
+                stream.wait_event(pipe.submit(x_host, y_host))
+            _barrier(dist)
+            ev0.record(stream)
+            for i in range(args.steps):
+                done = pipe.submit(x_host, y_host)
+                if i == args.steps - 1:
+                    stream.wait_event(done)
+            ev1.record(stream)
+            _barrier(dist)
+            e2e_ms = _max_over_ranks(dist, dev, ev0.elapsed_time(ev1)) / args.steps
+            tot = T_rank * world
+            out["e2e"] = {"value": tot / (e2e_ms / 1e3), "unit": "tokens/s",
+                          "h2d_bytes_per_step": x_host.numel() * x_host.element_size() * world,
+                          "d2h_bytes_per_step": y_host.numel() * y_host.element_size() * world}
+        return out
+
+    # strong scaling: the global batch of cfg.T seeded tokens split over the ranks
+    T_rank = cfg.T // world
+    x_all = configs.block_x_torch(cfg, dev, seed=0)
+    x = x_all[rank * T_rank:(rank + 1) * T_rank].contiguous()
+    del x_all
+    strong = measure(cfg, T_rank, x)
+    # weak scaling: cfg.T tokens on every rank
+    weak = measure(cfg, cfg.T, configs.block_x_torch(cfg, dev, seed=rank), e2e=False) if args.extras else None
+    extra = None
+    if args.extras and cfg.name == configs_default():
+        # the fine-grained Zipf block, strong scaling: per-rank load under skew
+        c4 = configs.C4
+        runner = None
+        torch.cuda.empty_cache()
+        runner = ep.ExpertParallelMoE.synthetic(c4, rank, world, dev, seed=0)
+        xa = configs.block_x_torch(c4, dev, seed=0)
+        Tr = c4.T // world
+        extra = {c4.name: measure(c4, Tr, xa[rank * Tr:(rank + 1) * Tr].contiguous(), e2e=False)}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": strong["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": strong["ms_per_step"], "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) tokens, N(0,0.02) weights; no dataset)",
+            "config": config_dict(cfg, world),
+            "e2e": strong["e2e"], "gpu_launches": strong["gpu_launches"], "clocks": strong["clocks"],
+            "ep_ranks": strong["ep_ranks"], "rows_per_rank": strong["rows_per_rank"],
+            "tflops": cfg.flops / (strong["ms_per_step"] / 1e3) / 1e12,
+        }
+        if weak is not None:
+            line["weak"] = {k: weak[k] for k in ("value", "ms_per_step", "tokens_per_rank", "rows_per_rank")}
+        if extra:
+            line["extra_configs"] = extra
+        print(json.dumps(line), flush=True)
+    dist.barrier()
+    dist.destroy_process_group()
 
 
 def run_mul_mat_id(args, cfg):
@@ -500,6 +625,8 @@ def main():
     ap.add_argument("--config", default="c3_mixtral_8x7b")
     ap.add_argument("--impl", default="frank", choices=["frank", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extras", dest="extras", action="store_false",
+                    help="skip the extra configurations (decode T=1, T=8 and the fine-grained block)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # at least 3 untimed warm-up steps
     from frank_b200 import configs
