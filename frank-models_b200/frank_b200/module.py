@@ -83,6 +83,10 @@ class B200Module:
             return _host(ops.rms_norm(_dev(input, np.float32, "input"), _dev(weight, np.float32, "weight"), eps))
         return ops.rms_norm(input, weight, eps)
 
+    # the reference module's exported name for the same function
+    # (components/normalization/rms_norm.mlir:18, tests/components/test_rms_norm.py:22)
+    rms_norm_linalg = rms_norm
+
     def moe_ffn_sublayer(self, residual, ffn_norm_w, rms_eps, gate_inp_w, up_exps_w, gate_exps_w, down_exps_w,
                          n_expert, n_expert_used, n_embd, n_ff, normalize_weights):
         """The MoE FFN sub-layer of the MoE transformer layer
