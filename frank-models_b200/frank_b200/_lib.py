@@ -22,6 +22,7 @@ EIDS = -2
 ECUDA = -3
 ENOSPC = -4
 ETIMEOUT = -5
+ENCCL = -6
 
 _c_i64 = ctypes.c_int64
 _c_int = ctypes.c_int

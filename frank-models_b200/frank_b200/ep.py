@@ -119,7 +119,8 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, wr, w_up_local, w_gate_local, w_down_local, n_expert: int, n_expert_used: int,
-                 normalize_weights: bool, group=None, prims=None, out_dtype=torch.float32, mode: str | None = None):
+                 normalize_weights: bool, group=None, prims=None, out_dtype=torch.float32, mode: str | None = None,
+                 step_timeout_s: float | None = None, monitor_group=None):
         self.group = group
         self.P = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -146,6 +147,24 @@ class ExpertParallelMoE:
             raise ValueError(f"mode must be 'p2p' or 'nccl', got {mode!r}")
         self.mode = mode
         self._symm = None
+        # Failure detection.  With step_timeout_s set, every step starts with a
+        # host-side presence check of all ranks (a gloo monitored barrier with
+        # that deadline): a rank that never joins the step makes the others
+        # raise FrankError(FRANK_ETIMEOUT) naming it, before any of this step's
+        # kernels or collectives is issued, instead of waiting forever.  A
+        # collective that fails later in the step (a peer that died mid-step,
+        # ended by the process group's own timeout) raises
+        # FrankError(FRANK_ENCCL).  The presence check needs a gloo group: the
+        # given monitor_group, the step's own group when that is gloo, or a
+        # gloo group created here (collectively: every rank constructs its
+        # ExpertParallelMoE at the same point).
+        self.step_timeout_s = step_timeout_s
+        self.monitor_group = monitor_group
+        if step_timeout_s is not None and monitor_group is None:
+            if dist.get_backend(group) == "gloo":
+                self.monitor_group = group if group is not None else dist.group.WORLD
+            else:
+                self.monitor_group = dist.new_group(ranks=list(range(dist.get_world_size())), backend="gloo")
 
     @classmethod
     def synthetic(cls, cfg, rank, world, device, seed=0, group=None):
@@ -181,8 +200,8 @@ class ExpertParallelMoE:
                 if m:
                     ops.append(dist.P2POp(dist.irecv, recv_buf[d0:d0 + m], peer, self.group))
         if ops:
-            for req in dist.batch_isend_irecv(ops):
-                req.wait()
+            for req in self._comm(dist.batch_isend_irecv, ops):
+                self._comm(req.wait)
 
     # phase boundaries (nccl mode / p2p mode):
     #   route+permute(+gather) | counts (+plan) | dispatch (+barrier) | expert GEMMs
@@ -212,9 +231,30 @@ class ExpertParallelMoE:
         return dict(zip(self.PHASES, (acc / max(len(calls), 1)).tolist()))
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        from ._lib import ETIMEOUT, FrankError
+
+        if self.step_timeout_s is not None:
+            import datetime
+
+            try:
+                dist.monitored_barrier(group=self.monitor_group,
+                                       timeout=datetime.timedelta(seconds=self.step_timeout_s))
+            except RuntimeError as e:
+                raise FrankError(ETIMEOUT, f"expert-parallel step on rank {self.rank}: a peer did not join within "
+                                           f"{self.step_timeout_s} s ({e})") from e
         if self.mode == "p2p":
             return self._call_p2p(x, out)
         return self._call_nccl(x, out)
+
+    def _comm(self, fn, *args, **kwargs):
+        """Run one collective of the step; its failure (a peer gone, the
+        process group's timeout) becomes FrankError(FRANK_ENCCL)."""
+        from ._lib import ENCCL, FrankError
+
+        try:
+            return fn(*args, **kwargs)
+        except RuntimeError as e:
+            raise FrankError(ENCCL, f"expert-parallel step on rank {self.rank}: {fn.__name__} failed ({e})") from e
 
     # ------------------------------------------------------------ p2p mode --
     def _symmetric(self, T: int, rows: int, dev):
@@ -284,7 +324,7 @@ class ExpertParallelMoE:
     def _barrier(self, flag):
         # stream-ordered: every rank's preceding kernels (and their stores into
         # peer memory) have completed when this collective completes
-        dist.all_reduce(flag, group=self.group)
+        self._comm(dist.all_reduce, flag, group=self.group)
 
     def _call_p2p(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         from . import _lib, ops
@@ -303,7 +343,7 @@ class ExpertParallelMoE:
         cnt = (offsets[1:] - offsets[:-1]).contiguous()
         self._mark()
         counts = self._symm["counts"] if self._symm is not None else self._counts
-        dist.all_gather_into_tensor(counts, cnt, group=self.group)
+        self._comm(dist.all_gather_into_tensor, counts, cnt, group=self.group)
         # the one host read per step: the buffers are sized from the counts
         # every rank now holds, so no rank can plan past a receive buffer
         t_max, rows_max = self.step_sizes(counts.cpu().numpy())
@@ -344,7 +384,7 @@ class ExpertParallelMoE:
         cnt = (offsets[1:] - offsets[:-1]).to(torch.int64).reshape(self.P, self.El)
         self._mark()
         recv_cnt_t = torch.empty_like(cnt)
-        dist.all_to_all_single(recv_cnt_t, cnt.contiguous(), group=self.group)
+        self._comm(dist.all_to_all_single, recv_cnt_t, cnt.contiguous(), group=self.group)
         both = torch.stack([cnt, recv_cnt_t]).cpu().numpy()  # the one host sync per step
         send_cnt, recv_cnt = both[0], both[1]
         _, recv_splits, seg, local_off = plan_exchange(send_cnt, recv_cnt)
