@@ -12,7 +12,10 @@ namespace frank {
 // ---- kernels implemented in the other translation units ----
 int launch_softmax_topk(const float*, int64_t, int64_t, int64_t, int, float*, int32_t*, cudaStream_t);
 int launch_router_topk(int, const void*, int, const void*, int64_t, int64_t, int64_t, int64_t, int, float*, int32_t*,
-                       float*, cudaStream_t);
+                       float*, cudaStream_t, const __nv_bfloat16* wr3_pre = nullptr);
+size_t router_pack_offset(int64_t, int64_t);
+size_t router_pack_bytes(int64_t, int64_t);
+int launch_router_pack(int, const void*, int64_t, int64_t, void*, cudaStream_t);
 size_t router_scratch_bytes(int, int64_t, int64_t, int64_t);
 size_t permute_workspace_size(int64_t, int64_t);
 int launch_permute(const int32_t*, int64_t, int64_t, int32_t*, int32_t*, int32_t*, int32_t*, void*, size_t,
@@ -195,6 +198,14 @@ static size_t mmid_layout(int dtype, int64_t O, int64_t I, int64_t E, int64_t k,
   return align_up(c.used, 256);
 }
 
+// A router pack (FRANK_ROUTER_PACKED) is an fp32 wr followed by its bf16
+// split: every path reads the fp32 part, the tensor-core router the split.
+static const __nv_bfloat16* resolve_router(int* wr_dtype, const void* wr, int64_t E, int64_t H) {
+  if (*wr_dtype != FRANK_ROUTER_PACKED) return nullptr;
+  *wr_dtype = FRANK_F32;
+  return reinterpret_cast<const __nv_bfloat16*>(static_cast<const char*>(wr) + router_pack_offset(E, H));
+}
+
 static int check_dtype(int d, const char* what) {
   if (d != FRANK_F32 && d != FRANK_BF16) {
     set_error("%s: dtype %d is neither FRANK_F32 (0) nor FRANK_BF16 (1)", what, d);
@@ -211,7 +222,7 @@ extern "C" {
 
 const char* frank_last_error(void) { return g_err.c_str(); }
 
-int frank_abi_version(void) { return 100; }
+int frank_abi_version(void) { return 101; }
 
 int frank_num_sms(void) { return num_sms(); }
 
@@ -237,12 +248,23 @@ size_t frank_router_scratch_bytes(int x_dtype, int64_t T, int64_t H, int64_t E) 
 int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H, int64_t E,
                       int64_t k, int normalize, float* weights, int32_t* ids, float* logits_scratch, void* stream) {
   FRANK_TRY(check_dtype(x_dtype, "router_topk"));
+  const __nv_bfloat16* wr3 = resolve_router(&wr_dtype, wr, E, H);
   FRANK_TRY(check_dtype(wr_dtype, "router_topk"));
   FRANK_CHECK_ARG(E >= 1 && E <= 256, "router_topk: E=%lld outside [1, 256]", (long long)E);
   FRANK_CHECK_ARG(k >= 1 && k <= E && k <= 32, "router_topk: k=%lld outside [1, min(E, 32)]", (long long)k);
   FRANK_CHECK_ARG(T >= 0 && H >= 1, "router_topk: bad T=%lld / H=%lld", (long long)T, (long long)H);
   return launch_router_topk(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, weights, ids, logits_scratch,
-                            as_stream(stream));
+                            as_stream(stream), wr3);
+}
+
+size_t frank_router_pack_size(int64_t E, int64_t H) { return router_pack_bytes(E, H); }
+size_t frank_router_pack_offset(int64_t E, int64_t H) { return router_pack_offset(E, H); }
+
+int frank_router_pack(int wr_dtype, const void* wr, int64_t E, int64_t H, void* pack, void* stream) {
+  FRANK_TRY(check_dtype(wr_dtype, "router_pack"));
+  FRANK_CHECK_ARG(E >= 1 && E <= 256 && H >= 1, "router_pack: bad E=%lld / H=%lld", (long long)E, (long long)H);
+  FRANK_CHECK_ARG(wr && pack && (uintptr_t)pack % 256 == 0, "router_pack: null or unaligned pointer");
+  return launch_router_pack(wr_dtype, wr, E, H, pack, as_stream(stream));
 }
 
 size_t frank_permute_workspace_size(int64_t n_slots, int64_t E) { return permute_workspace_size(n_slots, E); }
@@ -308,6 +330,7 @@ int moe_block(int dtype, const void* x, int wr_dtype, const void* wr, const void
               void* y, float* route_w, int32_t* route_ids, void* workspace, size_t ws_bytes, cudaStream_t st,
               const float* residual) {
   FRANK_TRY(check_dtype(dtype, "moe_ffn_block"));
+  const __nv_bfloat16* wr3 = resolve_router(&wr_dtype, wr, E, H);
   FRANK_TRY(check_dtype(wr_dtype, "moe_ffn_block"));
   FRANK_TRY(check_dtype(y_dtype, "moe_ffn_block"));
   FRANK_CHECK_ARG(E >= 1 && E <= 256, "moe_ffn_block: n_expert=%lld outside [1, 256]", (long long)E);
@@ -338,7 +361,7 @@ int moe_block(int dtype, const void* x, int wr_dtype, const void* wr, const void
   int32_t* ids = route_ids ? route_ids : L.ids;
   prof_mark(0, st);
   // 1. router + softmax + top-k (+ renorm)          moe_ffn_block.mlir:54-128
-  FRANK_TRY(launch_router_topk(dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, L.logits, st));
+  FRANK_TRY(launch_router_topk(dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, L.logits, st, wr3));
   prof_mark(1, st);
   // 2. stable expert permutation                    mul_mat_id.mlir:51-61
   FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, nullptr, L.perm_ws, L.perm_bytes, st));

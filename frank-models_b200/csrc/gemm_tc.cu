@@ -53,8 +53,9 @@ constexpr int kMaxPeers = 8;
 enum Mode { SWIGLU = 0, SCALE = 1, PLAIN = 2 };
 
 struct Params {
-  const int32_t* offsets;  // [E+1] expert row offsets (permutation output)
+  const int32_t* offsets;  // [E+1] expert row offsets (permutation output); null: one group of `rows`
   int E;
+  int rows;                // total rows (used when offsets is null, E == 1)
   int n_tiles;             // output column tiles per expert
   int N_out;               // output columns
   int K;
@@ -166,15 +167,20 @@ struct Tile {
   int e, m0, m_end, n, swapN;
 };
 
-__device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const int32_t* offsets, int E, int bm = BM,
+// Row offset of group e (offsets[e], or 0 / rows for the single-group form).
+__device__ __forceinline__ int off_at(const Params& p, int e) {
+  return p.offsets != nullptr ? p.offsets[e] : (e == 0 ? 0 : p.rows);
+}
+
+__device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const Params& p, int bm = BM,
                                             bool allow_swap = false) {
-  int lo = 0, hi = E;  // find e: prefix[e] <= t < prefix[e+1]
+  int lo = 0, hi = p.E;  // find e: prefix[e] <= t < prefix[e+1]
   while (hi - lo > 1) {
     int mid = (lo + hi) >> 1;
     if (prefix[mid] <= t) lo = mid; else hi = mid;
   }
   const int e = lo;
-  const int r0 = offsets[e], r1 = offsets[e + 1];
+  const int r0 = off_at(p, e), r1 = off_at(p, e + 1);
   const int mt = (r1 - r0 + bm - 1) / bm;
   const int nt = (prefix[e + 1] - prefix[e]) / mt;
   const int local = t - prefix[e];
@@ -352,7 +358,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
     for (int base = 0; base < p.E; base += 32) {
       int e = base + lane;
       int v = 0;
-      if (e < p.E) v = ((p.offsets[e + 1] - p.offsets[e] + BM - 1) / BM) * p.n_tiles;
+      if (e < p.E) v = ((off_at(p, e + 1) - off_at(p, e) + BM - 1) / BM) * p.n_tiles;
       int incl = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -382,7 +388,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
       uint32_t it = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM, p.swap_small != 0);
+        Tile tl = decode_tile(t, prefix, p, BM, p.swap_small != 0);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
@@ -413,7 +419,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
         if (!mbar_wait(tempty_bar(a), aph ^ 1u, abort_flag, p.err)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + a * BN;
-        const int swapN = p.swap_small ? decode_tile(t, prefix, p.offsets, p.E, BM, true).swapN : 0;
+        const int swapN = p.swap_small ? decode_tile(t, prefix, p, BM, true).swapN : 0;
         const uint32_t idesc_sw =
             (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(swapN >> 3) << 17) | ((uint32_t)(128 >> 4) << 24);
         for (int kb = 0; kb < nk; ++kb, ++it) {
@@ -449,7 +455,7 @@ tc_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_con
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     uint32_t tc = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, ++tc) {
-      Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM, p.swap_small != 0);
+      Tile tl = decode_tile(t, prefix, p, BM, p.swap_small != 0);
       const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
@@ -587,7 +593,7 @@ tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     for (int base = 0; base < p.E; base += 32) {
       int e = base + lane;
       int v = 0;
-      if (e < p.E) v = ((p.offsets[e + 1] - p.offsets[e] + BM2 - 1) / BM2) * p.n_tiles;
+      if (e < p.E) v = ((off_at(p, e + 1) - off_at(p, e) + BM2 - 1) / BM2) * p.n_tiles;
       int incl = v;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
@@ -618,7 +624,7 @@ tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
       uint32_t it = 0;
       bool ok = true;
       for (int t = cid; t < total && ok; t += ncl) {
-        Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM2);
+        Tile tl = decode_tile(t, prefix, p, BM2);
         for (int kb = 0; kb < nk; ++kb, ++it) {
           const int s = it % STAGES2;
           const uint32_t ph = (it / STAGES2) & 1u;
@@ -665,7 +671,7 @@ tc2_grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_co
     const int q = warp & 3;
     uint32_t tc = 0;
     for (int t = cid; t < total; t += ncl, ++tc) {
-      Tile tl = decode_tile(t, prefix, p.offsets, p.E, BM2);
+      Tile tl = decode_tile(t, prefix, p, BM2);
       const uint32_t a = tc & 1u, aph = (tc >> 1) & 1u;
       if (!mbar_wait(tfull_bar(a), aph, abort_flag, p.err)) break;
       tc_fence_after();
@@ -810,8 +816,13 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
   if (mode == SWIGLU) FRANK_TRY(make_map_3d(&mb2, B2, E, N, K));
   else mb2 = mb;
   Params p;
+  if (offsets == nullptr && E != 1) {
+    set_error("tc_grouped_gemm: row offsets may be omitted only for a single group");
+    return FRANK_EINVAL;
+  }
   p.offsets = offsets;
   p.E = (int)E;
+  p.rows = (int)rows;
   p.n_tiles = (int)(mode == SWIGLU ? (N + 127) / 128 : (N + BN - 1) / BN);
   p.N_out = (int)N;
   p.K = (int)K;

@@ -200,11 +200,12 @@ router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T
 // accumulation (x is bf16, hence exact in the products).  The three partial
 // dot products are added in fp32 before softmax + top-k.
 template <class TW>
-__global__ void router_split_kernel(const TW* __restrict__ wr, int E, int H, int64_t T,
-                                    __nv_bfloat16* __restrict__ wr3, int32_t* __restrict__ offs) {
+__global__ void router_split_kernel(const TW* __restrict__ wr, int E, int H, __nv_bfloat16* __restrict__ wr3,
+                                    float* __restrict__ wr32) {
   const int64_t EH = (int64_t)E * H;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < EH; i += (int64_t)gridDim.x * blockDim.x) {
     const float w = load_as_f32(wr, i);
+    if (wr32 != nullptr) wr32[i] = w;
     const __nv_bfloat16 hi = __float2bfloat16_rn(w);
     const float r1 = w - __bfloat162float(hi);
     const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
@@ -212,10 +213,6 @@ __global__ void router_split_kernel(const TW* __restrict__ wr, int E, int H, int
     wr3[i] = hi;
     wr3[EH + i] = mid;
     wr3[2 * EH + i] = lo;
-  }
-  if (blockIdx.x == 0 && threadIdx.x == 0) {
-    offs[0] = 0;
-    offs[1] = (int32_t)T;
   }
 }
 
@@ -429,22 +426,38 @@ size_t router_scratch_bytes(int x_dtype, int64_t T, int64_t H, int64_t E) {
   return E <= 8 ? 0 : (size_t)T * E * sizeof(float);
 }
 
-static int launch_router_tc(const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H, int64_t E, int64_t k,
-                            int normalize, float* w, int32_t* ids, void* scratch, cudaStream_t st) {
-  Carve c(scratch, router_scratch_bytes(FRANK_BF16, T, H, E));
-  float* l3 = c.take<float>(T * 3 * E);
-  __nv_bfloat16* wr3 = c.take<__nv_bfloat16>(3 * E * H);
-  int32_t* offs = c.take<int32_t>(2);
+static int launch_router_split(int wr_dtype, const void* wr, int64_t E, int64_t H, __nv_bfloat16* wr3, float* wr32,
+                               cudaStream_t st) {
   const int64_t EH = E * H;
   const unsigned blocks = (unsigned)((EH + 255) / 256 < 1024 ? (EH + 255) / 256 : 1024);
   if (wr_dtype == FRANK_F32)
-    router_split_kernel<float><<<blocks, 256, 0, st>>>((const float*)wr, (int)E, (int)H, T, wr3, offs);
+    router_split_kernel<float><<<blocks, 256, 0, st>>>((const float*)wr, (int)E, (int)H, wr3, wr32);
   else
-    router_split_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)wr, (int)E, (int)H, T, wr3,
-                                                                offs);
+    router_split_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>((const __nv_bfloat16*)wr, (int)E, (int)H, wr3, wr32);
   FRANK_LAUNCH_CHECK();
-  FRANK_TRY(launch_tc_grouped_gemm(2, x, wr3, nullptr, offs, 1, T, 3 * E, H, nullptr, l3, st, nullptr, nullptr,
-                                   nullptr, 0, 0));
+  return FRANK_OK;
+}
+
+size_t router_pack_offset(int64_t E, int64_t H) { return align_up((size_t)E * H * 4, 256); }
+size_t router_pack_bytes(int64_t E, int64_t H) { return router_pack_offset(E, H) + align_up((size_t)3 * E * H * 2, 256); }
+
+int launch_router_pack(int wr_dtype, const void* wr, int64_t E, int64_t H, void* pack, cudaStream_t st) {
+  char* base = static_cast<char*>(pack);
+  return launch_router_split(wr_dtype, wr, E, H, reinterpret_cast<__nv_bfloat16*>(base + router_pack_offset(E, H)),
+                             reinterpret_cast<float*>(base), st);
+}
+
+// wr3_pre: the prepared split of a router pack (or null: split wr here).
+static int launch_router_tc(const void* x, int wr_dtype, const void* wr, const __nv_bfloat16* wr3_pre, int64_t T,
+                            int64_t H, int64_t E, int64_t k, int normalize, float* w, int32_t* ids, void* scratch,
+                            cudaStream_t st) {
+  Carve c(scratch, router_scratch_bytes(FRANK_BF16, T, H, E));
+  float* l3 = c.take<float>(T * 3 * E);
+  __nv_bfloat16* wr3 = c.take<__nv_bfloat16>(3 * E * H);
+  if (wr3_pre == nullptr) FRANK_TRY(launch_router_split(wr_dtype, wr, E, H, wr3, nullptr, st));
+  // one group of T rows: no offsets array needed
+  FRANK_TRY(launch_tc_grouped_gemm(2, x, wr3_pre ? wr3_pre : wr3, nullptr, nullptr, 1, T, 3 * E, H, nullptr, l3, st,
+                                   nullptr, nullptr, nullptr, 0, 0));
   softmax_topk3_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(l3, T, (int)E, (int)k, normalize, w, ids);
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
@@ -452,10 +465,11 @@ static int launch_router_tc(const void* x, int wr_dtype, const void* wr, int64_t
 
 // logits: scratch of router_scratch_bytes(x_dtype, T, H, E) bytes (may be null: slower kernels).
 int launch_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr, int64_t T, int64_t H,
-                       int64_t E, int64_t k, int normalize, float* w, int32_t* ids, float* logits, cudaStream_t st) {
+                       int64_t E, int64_t k, int normalize, float* w, int32_t* ids, float* logits, cudaStream_t st,
+                       const __nv_bfloat16* wr3_pre) {
   if (T == 0) return FRANK_OK;
   if (logits != nullptr && router_tc_ok(x_dtype, T, H, E) && (uintptr_t)x % 16 == 0)
-    return launch_router_tc(x, wr_dtype, wr, T, H, E, k, normalize, w, ids, logits, st);
+    return launch_router_tc(x, wr_dtype, wr, wr3_pre, T, H, E, k, normalize, w, ids, logits, st);
   const size_t esz = x_dtype == FRANK_F32 ? 4 : 2;
   const bool vec_ok = (H % 8 == 0) && ((uintptr_t)x % 16 == 0) && (H * 4 * 1 <= 160 * 1024) &&
                       (E <= 8 || logits != nullptr) && (H * esz) % 16 == 0;

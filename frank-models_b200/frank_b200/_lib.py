@@ -15,6 +15,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libfrankmoe.so"
 
 F32 = 0
 BF16 = 1
+ROUTER_PACKED = 16  # wr_dtype of a router pack (frank_router_pack)
 
 OK = 0
 EINVAL = -1
@@ -37,6 +38,9 @@ SIGNATURES = {
     "frank_swiglu": (_c_int, [_c_int, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp]),
     "frank_softmax_topk": (_c_int, [_c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_vp]),
     "frank_router_scratch_bytes": (_c_size, [_c_int, _c_i64, _c_i64, _c_i64]),
+    "frank_router_pack_size": (_c_size, [_c_i64, _c_i64]),
+    "frank_router_pack_offset": (_c_size, [_c_i64, _c_i64]),
+    "frank_router_pack": (_c_int, [_c_int, _c_vp, _c_i64, _c_i64, _c_vp, _c_vp]),
     "frank_router_topk": (_c_int, [_c_int, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_int,
                                    _c_vp, _c_vp, _c_vp, _c_vp]),
     "frank_permute_workspace_size": (_c_size, [_c_i64, _c_i64]),

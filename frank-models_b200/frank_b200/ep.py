@@ -338,7 +338,9 @@ class ExpertParallelMoE:
         if self.profile:
             self._marks.append([])
         self._mark()
-        w, ids = ops.router_topk(x, self.wr, self.k, self.normalize)
+        if getattr(self, "_wr_pack", None) is None:
+            self._wr_pack = ops.router_pack(self.wr)
+        w, ids = ops.router_topk(x, self.wr, self.k, self.normalize, pack=self._wr_pack)
         sorted_slots, offsets, slot_pos, _ = ops.permute(ids, self.E)
         cnt = (offsets[1:] - offsets[:-1]).contiguous()
         self._mark()

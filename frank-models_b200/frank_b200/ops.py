@@ -67,8 +67,23 @@ def softmax_topk(logits: torch.Tensor, k: int, normalize: bool):
     return w, ids
 
 
-def router_topk(x: torch.Tensor, wr: torch.Tensor, k: int, normalize: bool):
-    """Router logits + softmax + top-k (+ renorm) -> (w [k,T] f32, ids [k,T] i32)."""
+def router_pack(wr: torch.Tensor) -> torch.Tensor:
+    """The router weights prepared once (frank_router_pack): an fp32 copy of
+    wr [E, H] followed by its exact three-term bf16 split, as a uint8 device
+    tensor.  Pass it as ``pack=`` to :func:`router_topk`; blocks build it at
+    construction."""
+    wr = _cuda_contig(wr, "wr")
+    E, H = wr.shape
+    lib = _lib.load()
+    pack = torch.empty(lib.frank_router_pack_size(E, H), dtype=torch.uint8, device=wr.device)
+    _lib.check(lib.frank_router_pack(_dt(wr), _ptr(wr), E, H, _ptr(pack), _stream()))
+    return pack
+
+
+def router_topk(x: torch.Tensor, wr: torch.Tensor, k: int, normalize: bool, pack: torch.Tensor | None = None):
+    """Router logits + softmax + top-k (+ renorm) -> (w [k,T] f32, ids [k,T] i32).
+    ``pack``: optional :func:`router_pack` of ``wr`` (same results, no
+    per-call split of the router weights)."""
     x = _cuda_contig(x, "x")
     wr = _cuda_contig(wr, "wr")
     T, H = x.shape
@@ -80,7 +95,8 @@ def router_topk(x: torch.Tensor, wr: torch.Tensor, k: int, normalize: bool):
     lib = _lib.load()
     nbytes = lib.frank_router_scratch_bytes(_dt(x), T, H, E)
     scratch = torch.empty((nbytes + 3) // 4, dtype=torch.float32, device=x.device) if nbytes else None
-    _lib.check(lib.frank_router_topk(_dt(x), _ptr(x), _dt(wr), _ptr(wr), T, H, E, k, int(bool(normalize)),
+    wr_dt, wr_ptr = (_lib.ROUTER_PACKED, _ptr(pack)) if pack is not None else (_dt(wr), _ptr(wr))
+    _lib.check(lib.frank_router_topk(_dt(x), _ptr(x), wr_dt, wr_ptr, T, H, E, k, int(bool(normalize)),
                                      _ptr(w), _ptr(ids), _ptr(scratch), _stream()))
     return w, ids
 
@@ -238,6 +254,9 @@ class MoEFFNBlock:
             raise ValueError(f"MoEFFNBlock: gate_inp_w {tuple(self.wr.shape)} != [{E}, {H}]")
         self.H, self.F = H, F
         self._ws = None
+        # router weights prepared once (fp32 copy + the tensor-core router's
+        # exact bf16 split), passed as FRANK_ROUTER_PACKED
+        self.wr_pack = router_pack(self.wr)
 
     def workspace_bytes(self, T: int) -> int:
         return _lib.load().frank_moe_ffn_block_workspace_size(_DT[self.dtype], T, self.H, self.F, self.E, self.k)
@@ -262,7 +281,7 @@ class MoEFFNBlock:
         rid = torch.empty((self.k, T), dtype=torch.int32, device=x.device) if return_routing else None
         ws = self._workspace(T, x.device)
         _lib.check(_lib.load().frank_moe_ffn_block(
-            _DT[self.dtype], _ptr(x), _dt(self.wr), _ptr(self.wr), _ptr(self.w_up), _ptr(self.w_gate),
+            _DT[self.dtype], _ptr(x), _lib.ROUTER_PACKED, _ptr(self.wr_pack), _ptr(self.w_up), _ptr(self.w_gate),
             _ptr(self.w_down), T, self.E, self.k, self.H, self.F, int(self.normalize), _DT[self.out_dtype], _ptr(y), _ptr(rw), _ptr(rid),
             _ptr(ws), ws.numel(), _stream()))
         if return_routing:
@@ -296,7 +315,7 @@ class MoEFFNBlock:
         need = lib.frank_moe_ffn_sublayer_workspace_size(_DT[self.dtype], T, self.H, self.F, self.E, self.k)
         ws = self._workspace(T, residual.device, need)
         _lib.check(lib.frank_moe_ffn_sublayer(
-            _DT[self.dtype], _ptr(residual), _ptr(ffn_norm_w), float(rms_eps), _dt(self.wr), _ptr(self.wr),
+            _DT[self.dtype], _ptr(residual), _ptr(ffn_norm_w), float(rms_eps), _lib.ROUTER_PACKED, _ptr(self.wr_pack),
             _ptr(self.w_up), _ptr(self.w_gate), _ptr(self.w_down), T, self.E, self.k, self.H, self.F,
             int(self.normalize), _ptr(y), _ptr(rw), _ptr(rid), _ptr(ws), ws.numel(), _stream()))
         if return_routing:

@@ -42,6 +42,8 @@ extern "C" {
 /* element types */
 #define FRANK_F32 0
 #define FRANK_BF16 1
+/* router weights prepared once by frank_router_pack (a wr_dtype value) */
+#define FRANK_ROUTER_PACKED 16
 
 /* status codes */
 #define FRANK_OK 0
@@ -93,6 +95,23 @@ int frank_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k,
  */
 size_t frank_router_scratch_bytes(int x_dtype, int64_t T, int64_t H,
                                   int64_t E);
+
+/*
+ * Router weights prepared once per block: an fp32 copy of wr [E, H]
+ * followed (at byte offset frank_router_pack_offset(E, H)) by its exact
+ * three-term bf16 split [3, E, H] (hi, mid = bf16(wr - hi),
+ * lo = bf16(wr - hi - mid)).  Passing the pack with wr_dtype =
+ * FRANK_ROUTER_PACKED to frank_router_topk, frank_moe_ffn_block or
+ * frank_moe_ffn_sublayer gives the same results as passing wr itself; the
+ * tensor-core router then skips rebuilding the split on every call.  No
+ * counterpart in the reference (whose router is one fp32 matmul,
+ * moe_ffn_block.mlir:54-70).  wr_dtype FRANK_F32 or FRANK_BF16; pack:
+ * frank_router_pack_size(E, H) bytes, 256-byte aligned.
+ */
+size_t frank_router_pack_size(int64_t E, int64_t H);
+size_t frank_router_pack_offset(int64_t E, int64_t H);
+int frank_router_pack(int wr_dtype, const void* wr, int64_t E, int64_t H,
+                      void* pack, void* stream);
 int frank_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr,
                       int64_t T, int64_t H, int64_t E, int64_t k, int normalize,
                       float* weights, int32_t* ids, float* logits_scratch,

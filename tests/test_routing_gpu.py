@@ -93,3 +93,16 @@ def test_permute_flags_bad_ids():
     _, off, _, err = ops.permute(ids, 4)
     assert int(err.item()) == 1
     assert int(off[-1].item()) == 4
+
+
+@pytest.mark.parametrize("E,k,H,T,wdt", [(128, 8, 2048, 8192, torch.float32), (16, 4, 512, 300, torch.bfloat16),
+                                         (8, 2, 4096, 1000, torch.float32), (128, 8, 2048, 5, torch.float32)])
+def test_router_pack_same_results(E, k, H, T, wdt):
+    """A router pack (fp32 copy + prepared bf16 split) routes exactly like the
+    raw router weights on every router path (tensor-core, E <= 8, few tokens)."""
+    rng = np.random.default_rng(E + T)
+    x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).bfloat16().cuda()
+    wr = torch.from_numpy((rng.standard_normal((E, H)) * 0.02).astype(np.float32)).to(wdt).cuda()
+    w0, i0 = ops.router_topk(x, wr, k, False)
+    w1, i1 = ops.router_topk(x, wr, k, False, pack=ops.router_pack(wr))
+    assert torch.equal(i0, i1) and torch.equal(w0, w1)
