@@ -22,7 +22,10 @@ Cases
     reduced H and F so the literal oracle stays cheap;
   * rms_norm (oracles/normalization.py) and the MoE FFN sub-layer, composed
     from the reference's rms_norm and moe_ffn_block exactly as
-    oracles/transformer_layer.py:107-124 does.
+    oracles/transformer_layer.py:107-124 does;
+  * whole MoE transformer layers of the toy model (transformer_layer_moe,
+    oracles/transformer_layer.py:14-124) on the token batches of the toy
+    model's prefill tests, with the attention half's residual stored beside.
 
 ``--only PREFIX`` writes just the cases whose names start with PREFIX.
 """
@@ -152,6 +155,82 @@ def sublayer_cases():
     return out
 
 
+TOY = dict(vocab_size=256, n_embd=64, n_head=4, n_head_kv=2, head_dim=16, n_ff=128, n_expert=4, n_expert_used=2,
+           n_layers=2, rms_eps=1e-5, rope_freq_base=10000.0)
+
+
+def toy_params(seed=42):
+    """The toy MoE model's parameters, drawn in the order of the reference's
+    generator (tests/models/test_toy_llm.py:49-124: default_rng(42), model
+    tensors, then per layer the norms, attention projections, zero biases and
+    the MoE weights) so the layers below are the toy model's own layers."""
+    rng = np.random.default_rng(seed)
+    c = TOY
+    n = lambda *s: rng.standard_normal(s).astype(np.float32)  # noqa: E731
+    p = {"token_embd.weight": n(c["vocab_size"], c["n_embd"]), "output_norm.weight": n(c["n_embd"]),
+         "output.weight": n(c["n_embd"], c["vocab_size"])}
+    kv = c["n_head_kv"] * c["head_dim"]
+    for i in range(c["n_layers"]):
+        b = f"blk.{i}"
+        p[f"{b}.attn_norm.weight"] = n(c["n_embd"])
+        p[f"{b}.ffn_norm.weight"] = n(c["n_embd"])
+        p[f"{b}.attn_q.weight"] = n(c["n_embd"], c["n_embd"])
+        p[f"{b}.attn_k.weight"] = n(c["n_embd"], kv)
+        p[f"{b}.attn_v.weight"] = n(c["n_embd"], kv)
+        p[f"{b}.attn_output.weight"] = n(c["n_embd"], c["n_embd"])
+        p[f"{b}.attn_q.bias"] = np.zeros(c["n_embd"], dtype=np.float32)
+        p[f"{b}.attn_k.bias"] = np.zeros(kv, dtype=np.float32)
+        p[f"{b}.attn_v.bias"] = np.zeros(kv, dtype=np.float32)
+        p[f"{b}.attn_output.bias"] = np.zeros(c["n_embd"], dtype=np.float32)
+        p[f"{b}.ffn_gate_inp.weight"] = n(c["n_expert"], c["n_embd"])
+        p[f"{b}.ffn_up_exps.weight"] = n(c["n_ff"], c["n_embd"], c["n_expert"])
+        p[f"{b}.ffn_gate_exps.weight"] = n(c["n_ff"], c["n_embd"], c["n_expert"])
+        p[f"{b}.ffn_down_exps.weight"] = n(c["n_embd"], c["n_ff"], c["n_expert"])
+    return p
+
+
+# the token batches of the toy model's prefill tests (test_toy_llm.py:677-801)
+TOY_BATCHES = {"tok4": np.array([[1, 2, 3, 4]]), "batch2": np.array([[10, 20, 30], [40, 50, 60]]),
+               "tok8": np.arange(1, 9).reshape(1, 8)}
+
+
+def toy_layer_cases(ref_layer, ref_norm, ref_attn):
+    """Whole MoE transformer layers of the toy model (layers 0 and 1, the
+    layer-1 input being layer 0's oracle output), each as the reference's
+    transformer_layer_moe computes it (oracles/transformer_layer.py:14-124),
+    plus the attention half's residual (input + attention, :74-104), which the
+    GPU test feeds to the MoE FFN sub-layer."""
+    c = TOY
+    p = toy_params()
+    out = []
+    for tag, tokens in TOY_BATCHES.items():
+        batch, seq = tokens.shape
+        pos = np.tile(np.arange(seq, dtype=np.int64), (batch, 1))
+        h = p["token_embd.weight"][tokens]
+        for li in range(c["n_layers"]):
+            b = f"blk.{li}"
+            normed = ref_norm.rms_norm(h.reshape(-1, c["n_embd"]), p[f"{b}.attn_norm.weight"], c["rms_eps"])
+            attn = ref_attn.attention_block(normed.reshape(batch, seq, c["n_embd"]), pos, p[f"{b}.attn_q.weight"],
+                                            p[f"{b}.attn_k.weight"], p[f"{b}.attn_v.weight"],
+                                            p[f"{b}.attn_output.weight"], p[f"{b}.attn_q.bias"],
+                                            p[f"{b}.attn_k.bias"], p[f"{b}.attn_v.bias"],
+                                            p[f"{b}.attn_output.bias"], False, c["n_head"], c["n_head_kv"],
+                                            c["n_embd"], c["rope_freq_base"], 1.0)
+            resid1 = h + attn
+            y = ref_layer.transformer_layer_moe(h, pos, p, li, c["n_head"], c["n_head_kv"], c["n_embd"], c["n_ff"],
+                                                c["n_expert"], c["n_expert_used"], rms_eps=c["rms_eps"],
+                                                rope_freq_base=c["rope_freq_base"])
+            out.append((f"layer_toy_{tag}_l{li}", dict(
+                layer_input=h.astype(np.float32), residual1=resid1.astype(np.float32),
+                ffn_norm_w=p[f"{b}.ffn_norm.weight"], rms_eps=np.float32(c["rms_eps"]),
+                gate_inp_w=p[f"{b}.ffn_gate_inp.weight"], up_exps_w=p[f"{b}.ffn_up_exps.weight"],
+                gate_exps_w=p[f"{b}.ffn_gate_exps.weight"], down_exps_w=p[f"{b}.ffn_down_exps.weight"],
+                n_expert=c["n_expert"], n_expert_used=c["n_expert_used"], n_embd=c["n_embd"], n_ff=c["n_ff"],
+                normalize_weights=False, expected=y.astype(np.float32))))
+            h = y
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="path to the frank-models source tree")
@@ -195,6 +274,12 @@ def main():
         np.savez_compressed(HERE / f"{name}.npz", residual=resid, ffn_norm_w=nw, rms_eps=eps, gate_inp_w=wr,
                             up_exps_w=wu, gate_exps_w=wg, down_exps_w=wd, n_expert=E, n_expert_used=k, n_embd=H,
                             n_ff=F, normalize_weights=norm, expected=resid + moe)
+    from oracles import attention as ref_attn
+    from oracles import transformer_layer as ref_layer
+
+    for name, arrays in toy_layer_cases(ref_layer, ref_norm, ref_attn):
+        if keep(name):
+            np.savez_compressed(HERE / f"{name}.npz", **arrays)
     print("wrote", len(list(HERE.glob("*.npz"))), "fixtures to", HERE)
 
 
