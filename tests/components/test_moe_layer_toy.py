@@ -41,7 +41,7 @@ def test_oracle_composes_the_layer(name):
     reference's whole layer (pins the composition on the CPU)."""
     g = load_golden(name)
     got = O.moe_ffn_sublayer(*_sublayer_args(g), grouped=False)
-    np.testing.assert_allclose(got.reshape(g["expected"].shape), g["expected"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(got.reshape(g["expected"].shape), g["expected"], rtol=1e-3, atol=1e-4)
 
 
 @pytest.mark.gpu
