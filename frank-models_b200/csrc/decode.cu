@@ -10,20 +10,24 @@
 //   top-k    softmax + top-k + renorm of every token (moe_ffn_block.mlir:
 //            72-128), the stable expert permutation and the list of active
 //            experts (mul_mat_id.mlir:51-53);
-//   gate/up  persistent blocks over (active expert, fr rows of F): the gate
-//            and up rows streamed once into shared memory with bulk copies
-//            and dotted with the expert's token rows (gathered straight
-//            from x), h = gate * silu(up) (swiglu.mlir:37-47);
-//   down     persistent blocks over (active expert, hr rows of H):
-//            d = down(h) * gate weight, fp32;
-//   combine  y[t] = sum of the k slots of t in slot order
-//            (moe_ffn_block.mlir:179-206), deterministic.
-// decode_fused_kernel runs all phases in one cooperative launch with three
-// grid barriers (after route, gate/up and down): every block computes the
-// top-k and the permutation of all tokens itself.  Blocks have eight compute
-// warps plus one warp that issues the streaming phases' bulk copies.  FRANK_DECODE_FUSED=0 runs
-// the same bodies as five launches chained by programmatic dependent launch.
-// No atomics on data: results are deterministic and identical in both forms.
+//   gate/up  the (gate row, up row) pairs of the active experts split evenly
+//            over persistent blocks, in items of up to fr rows of one
+//            expert: the rows streamed once into shared memory with bulk
+//            copies and dotted with the expert's token rows (gathered
+//            straight from x), h = gate * silu(up) (swiglu.mlir:37-47);
+//   down     block b owns the output columns [b H / nblk, (b+1) H / nblk)
+//            of every token and streams those rows of every active expert's
+//            down matrix: d = down(h) * gate weight, fp32, kept in shared
+//            memory; then y[t] = sum of the k slots of t in slot order
+//            (moe_ffn_block.mlir:179-206) for its columns, deterministic.
+// decode_fused_kernel runs all phases in one cooperative launch with two
+// grid barriers (after route and after gate/up): every block computes the
+// top-k and the permutation of all tokens itself, and requests its first
+// down weight rows before the second barrier.  Blocks have eight compute
+// warps plus one warp that issues the streaming phases' bulk copies.
+// FRANK_DECODE_FUSED=0 runs the same bodies as four launches chained by
+// programmatic dependent launch.  No atomics on data: results are
+// deterministic and identical in both forms.
 #include <cstdlib>
 
 #include "common.cuh"
@@ -33,6 +37,31 @@
 namespace {
 
 using namespace frank_topk;
+using frank::align_up;
+
+#ifdef FRANK_DECODE_TRACE
+// Measurement builds only: %globaltimer at the phase boundaries of every
+// block of the last fused launch (read with frank_decode_trace_read).
+__device__ unsigned long long g_decode_trace[1024][8];
+// per-item trace of block 0: [phase 0 gate/up, 1 down][item][landed, done, issued]
+__device__ unsigned long long g_decode_items[2][64][3];
+#define TRACE_ITEM(ph, j, w)                                                        \
+  do {                                                                              \
+    if (blockIdx.x == 0 && (j) < 64) g_decode_items[ph][j][w] = frank_mbar::global_ns(); \
+  } while (0)
+#define TRACE(i)                                                         \
+  do {                                                                   \
+    if (threadIdx.x == 0) g_decode_trace[blockIdx.x][i] = frank_mbar::global_ns();   \
+  } while (0)
+#else
+#define TRACE(i) \
+  do {           \
+  } while (0)
+#define TRACE_ITEM(ph, j, w) \
+  do {                       \
+  } while (0)
+#endif
+
 
 constexpr int kThreads = 256;           // compute threads (warps 0 .. kWarps-1)
 constexpr int kWarps = kThreads / 32;
@@ -74,7 +103,6 @@ struct DecodeWs {
   __nv_bfloat16* hs;    // [k*T, F]
   int32_t* active;      // experts with at least one row, ascending
   int32_t* nactive;
-  float* d;             // [k*T, H] down output x gate weight
   int32_t* err;         // device error word (bounded waits)
   unsigned* gbar;       // grid-barrier counter of the fused kernel (zeroed per call)
   const float* res;     // optional fp32 [T, H] residual added to y (may alias y)
@@ -83,13 +111,15 @@ struct DecodeWs {
 
 // Routing tables of one call in shared memory: expert row offsets [E+1],
 // active experts [E] (first *nact valid), token of each expert-sorted row,
-// gate weight of each expert-sorted row.
+// gate weight of each expert-sorted row, expert-sorted row of each flat
+// slot s = j*T + t.
 struct Meta {
   int32_t* off;
   int32_t* act;
   int32_t* nact;
   int32_t* tok;
   float* w;
+  int32_t* pos;
 };
 
 // Programmatic dependent launch: a kernel's blocks may start while the
@@ -177,16 +207,14 @@ constexpr size_t kFinalizeSmem = sizeof(float) * kWarps * kMaxE + sizeof(int32_t
 // Descending top-k (ties to the lower expert index) of one token's
 // probabilities p[E] by one warp, renormalised when asked: the selection
 // steps of warp_softmax_topk.
-__device__ __forceinline__ void warp_softmax_topk_probs(const float* p_in, int E, int k, int normalize, float* w_out,
-                                                        int32_t* id_out, int T, int t) {
+constexpr int kPerLane = kMaxE / 32;
+
+// The selection steps on one token's probabilities held in registers
+// (p[i] = probability of expert lane + 32 i, -1 where absent).
+__device__ __forceinline__ void warp_topk_select(float (&p)[kPerLane], int k, int normalize, float* w_out,
+                                                 int32_t* id_out, int T, int t) {
   const int lane = threadIdx.x & 31;
-  constexpr int kPer = kMaxE / 32;
-  float p[kPer];
-#pragma unroll
-  for (int i = 0; i < kPer; ++i) {
-    const int e = lane + 32 * i;
-    p[i] = e < E ? p_in[e] : -1.f;  // probabilities are >= 0; -1 marks "absent"
-  }
+  constexpr int kPer = kPerLane;
   float wsum = 0.f;
   for (int j = 0; j < k; ++j) {
     float bv = -2.f;
@@ -215,6 +243,18 @@ __device__ __forceinline__ void warp_softmax_topk_probs(const float* p_in, int E
   __syncwarp();
 }
 
+__device__ __forceinline__ void warp_softmax_topk_probs(const float* p_in, int E, int k, int normalize, float* w_out,
+                                                        int32_t* id_out, int T, int t) {
+  const int lane = threadIdx.x & 31;
+  float p[kPerLane];
+#pragma unroll
+  for (int i = 0; i < kPerLane; ++i) {
+    const int e = lane + 32 * i;
+    p[i] = e < E ? p_in[e] : -1.f;  // probabilities are >= 0; -1 marks "absent"
+  }
+  warp_topk_select(p, k, normalize, w_out, id_out, T, t);
+}
+
 // Softmax over the E experts and the descending top-k (ties to the lower
 // expert index), renormalised when asked, of all T tokens by one block.
 // Warps compute the probabilities (one token per warp, the arithmetic of
@@ -227,6 +267,37 @@ __device__ __forceinline__ void block_softmax_topk(const float* logits, int T, i
                                                    float* prob, float* w_out, int32_t* id_out) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int kPer = kMaxE / 32;
+  if (T <= kWarps) {
+    // one warp per token, probabilities kept in registers: no shared-memory
+    // round trip and one barrier (same arithmetic and selection as below)
+    if (warp < T) {
+      const int t = warp;
+      float v[kPer];
+      float mx = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? __ldcg(logits + (int64_t)e * T + t) : -INFINITY;
+        mx = fmaxf(mx, v[i]);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) {
+        const int e = lane + 32 * i;
+        v[i] = e < E ? expf(v[i] - mx) : 0.f;
+        sum += v[i];
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+      for (int i = 0; i < kPer; ++i) v[i] = lane + 32 * i < E ? v[i] / sum : -1.f;
+      warp_topk_select(v, k, normalize, w_out, id_out, T, t);
+    }
+    consumer_sync();
+    return;
+  }
   for (int t = warp; t < T; t += kWarps) {
     float v[kPer];
     float mx = -INFINITY;
@@ -369,6 +440,7 @@ __device__ __forceinline__ void permute_body(int T, int E, int k, const DecodeWs
     const float w = wts[s];
     m.tok[pos] = s % T;
     m.w[pos] = w;
+    m.pos[s] = pos;
     if (writer) {
       ws.sorted_slots[pos] = s;
       ws.slot_pos[s] = pos;
@@ -415,6 +487,7 @@ __device__ __forceinline__ void small_permute_body(int T, int E, int k, const De
       const float w = wts[lane];
       m.tok[pos] = lane % T;
       m.w[pos] = w;
+      m.pos[lane] = pos;
       if (writer) {
         ws.sorted_slots[pos] = lane;
         ws.slot_pos[lane] = pos;
@@ -438,23 +511,25 @@ decode_finalize_kernel(int T, int E, int k, int normalize, DecodeWs ws) {
   extern __shared__ __align__(16) float prob[];  // [T][E] (dynamic)
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
+  __shared__ int32_t m_pos[kMaxSlots];
   wait_prior_grid();
   allow_next_grid();
-  finalize_body(T, E, k, normalize, ws, scratch, prob, Meta{m_off, m_act, &m_nact, m_tok, m_w});
+  finalize_body(T, E, k, normalize, ws, scratch, prob, Meta{m_off, m_act, &m_nact, m_tok, m_w, m_pos});
 }
 
 
 __device__ __forceinline__ Meta load_meta(const DecodeWs& ws, int T, int E, int32_t* off, int32_t* act, int32_t* nact,
-                                          int32_t* tok, float* w) {
+                                          int32_t* tok, float* w, int32_t* pos) {
   for (int i = threadIdx.x; i <= E; i += blockDim.x) off[i] = __ldcg(ws.offsets + i);
   for (int i = threadIdx.x; i < E; i += blockDim.x) act[i] = __ldcg(ws.active + i);
   for (int i = threadIdx.x; i < ws.n_slots; i += blockDim.x) {
     tok[i] = __ldcg(ws.sorted_slots + i) % T;
     w[i] = __ldcg(ws.wsorted + i);
+    pos[i] = __ldcg(ws.slot_pos + i);
   }
   if (threadIdx.x == 0) *nact = __ldcg(ws.nactive);
   __syncthreads();
-  return Meta{off, act, nact, tok, w};
+  return Meta{off, act, nact, tok, w, pos};
 }
 
 // ----------------------------------------------- weight-streaming GEMVs --
@@ -466,127 +541,213 @@ __device__ __forceinline__ Meta load_meta(const DecodeWs& ws, int T, int E, int3
 // (active expert, chunk of rows), spread over persistent blocks.
 using namespace frank_mbar;
 
-// gate/up: item = (active expert e, fr rows of F starting at f0): stage =
-// fr gate rows then fr up rows ([2][fr][H] bf16).  Warp w < fr computes row
-// f0 + w for each token row: h = gate . x * silu(up . x).
+// Barriers of a streaming ring: full (one producer arrival + the bytes),
+// empty (one arrival per compute warp).
+__device__ __forceinline__ void init_ring(uint64_t* full, uint64_t* empty, int stages) {
+  for (int i = 0; i < stages; ++i) {
+    mbar_init(smem_u32(&full[i]), 1);
+    mbar_init(smem_u32(&empty[i]), kWarps);
+  }
+}
+
+
+// ------------------------------------------------ tensor-core dot products --
+// The streaming phases multiply a few weight rows by a few token rows: a
+// 16 x 8 output tile over K, i.e. warp MMAs m16n8k16 (bf16 in, fp32
+// accumulate).  The weight rows arrive by one contiguous bulk copy, so 16
+// rows sit at a stride of K * 2 bytes.  Instead of ldmatrix (whose 8 rows of
+// one 8 x 8 matrix would then share a bank group) each thread loads 16
+// contiguous bytes per row with one 128-bit load: thread t of a quad takes
+// the physical K elements [8t, 8t + 8) of every 32-element block and feeds
+// them to the fragment slots of logical k {2t, 2t+1, 2t+8, 2t+9} of the
+// block's two MMAs.  A and B use the same physical-to-logical map (it depends
+// on t only), so each output is still the full dot product.  The K blocks are
+// split evenly over the compute warps and their partial tiles summed in warp
+// order (deterministic).
+__host__ __device__ inline uint32_t tok_stride(int K) { return (uint32_t)K * 2 + 64; }
+constexpr int kMT = 16;  // weight rows per tile
+
+__device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// This warp's share of A [16 x K] (row i at a + i * ars) times the token
+// rows B^T [nb x K] (row n at b + n * brs, n < nb <= 8; columns n >= nb
+// repeat row nb - 1 and are ignored), written to red[warp] as a [16][8]
+// tile.  K % 16 == 0.
+__device__ __forceinline__ void warp_tile_mma(const uint8_t* a, uint32_t ars, const uint8_t* b, uint32_t brs, int K,
+                                              int nb, float* red) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int full = K / 32;
+  const int units = full + ((K & 31) ? 1 : 0);
+  const int u0 = units * warp / kWarps, u1 = units * (warp + 1) / kWarps;
+  const uint8_t* ap0 = a + (size_t)g * ars;
+  const uint8_t* ap1 = a + (size_t)(g + 8) * ars;
+  const uint8_t* bp = b + (size_t)min(g, nb - 1) * brs;
+  // four independent accumulators, each group's loads issued before its MMAs
+  float acc[4][4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) acc[q][0] = acc[q][1] = acc[q][2] = acc[q][3] = 0.f;
+  const int uf = min(u1, full);
+  for (int ub = u0; ub < uf; ub += 4) {
+    uint4 A0[4], A1[4], B[4];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (ub + q < uf) {
+        const int off = (ub + q) * 64 + t * 16;
+        A0[q] = *reinterpret_cast<const uint4*>(ap0 + off);
+        A1[q] = *reinterpret_cast<const uint4*>(ap1 + off);
+        B[q] = *reinterpret_cast<const uint4*>(bp + off);
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      if (ub + q < uf) {
+        mma_16816(acc[q], A0[q].x, A1[q].x, A0[q].y, A1[q].y, B[q].x, B[q].y);
+        mma_16816(acc[q], A0[q].z, A1[q].z, A0[q].w, A1[q].w, B[q].z, B[q].w);
+      }
+    }
+  }
+  if (u1 > full) {  // the last 16 elements: physical [4t, 4t + 4) for logical {2t, 2t+1, 2t+8, 2t+9}
+    const int off = full * 64 + t * 8;
+    const uint2 A0 = *reinterpret_cast<const uint2*>(ap0 + off);
+    const uint2 A1 = *reinterpret_cast<const uint2*>(ap1 + off);
+    const uint2 B = *reinterpret_cast<const uint2*>(bp + off);
+    mma_16816(acc[0], A0.x, A1.x, A0.y, A1.y, B.x, B.y);
+  }
+  float c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) c[i] = ((acc[0][i] + acc[1][i]) + acc[2][i]) + acc[3][i];
+  // m16n8 accumulator: c0, c1 at (g, 2t + {0, 1}), c2, c3 at (g + 8, 2t + {0, 1})
+  float* o = red + warp * (kMT * 8);
+  o[g * 8 + 2 * t] = c[0];
+  o[g * 8 + 2 * t + 1] = c[1];
+  o[(g + 8) * 8 + 2 * t] = c[2];
+  o[(g + 8) * 8 + 2 * t + 1] = c[3];
+}
+
+// sum over the warps' partial tiles, in warp order
+__device__ __forceinline__ float red_sum(const float* red, int i, int n) {
+  float s = 0.f;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) s += red[w * (kMT * 8) + i * 8 + n];
+  return s;
+}
+
+// gate/up: the nact * F (gate row, up row) pairs of the active experts are
+// split evenly over the blocks -- block b takes the flat pairs
+// [b R / nblk, (b+1) R / nblk), R = nact * F -- and a block walks its range in
+// items of at most fr <= 8 consecutive rows of one expert (an item ends at an
+// expert boundary).  Stage = 16 weight rows (the item's gate rows at 0..7,
+// its up rows at 8..15, one bulk copy each) and the expert's token rows.
+// One 16 x 8 tile gives gate . x and up . x of every (row, token):
+// h = gate . x * silu(up . x).
+struct GuCursor {
+  int64_t c, hi;  // next flat pair, end of this block's range
+  int F, fr;
+  __device__ __forceinline__ bool next(int& a, int& f0, int& rows) {
+    if (c >= hi) return false;
+    a = (int)(c / F);
+    f0 = (int)(c - (int64_t)a * F);
+    rows = (int)min((int64_t)min(fr, F - f0), hi - c);
+    c += rows;
+    return true;
+  }
+};
+
+__device__ __forceinline__ GuCursor gu_range(int nact, int F, int fr, int bid, int nblk) {
+  const int64_t R = (int64_t)nact * F;
+  return GuCursor{R * bid / nblk, R * (bid + 1) / nblk, F, fr};
+}
+
+__device__ __host__ inline uint32_t gu_stage_bytes(int H, int rcap) {
+  return (uint32_t)kMT * H * 2 + (uint32_t)rcap * tok_stride(H);
+}
+
 __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
                      const __nv_bfloat16* __restrict__ w_up, int T, int H, int F, int E, int fr, int rcap, int stages,
-                     DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, uint64_t* full, uint64_t* empty,
+                     DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw, float* red, uint64_t* full, uint64_t* empty,
                      int* s_abort, Meta m) {
   // routing tables in shared memory: refilling a stage needs no global round trip
   const int32_t* sm_off = m.off;
   const int32_t* sm_act = m.act;
   const int32_t* sm_tok = m.tok;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hv = H / 8;
-  // stage: [2][fr][H] weights, then [rcap][H] token rows of the item's expert
-  const uint32_t wbytes = 2u * fr * H * 2;
-  const uint32_t stage_bytes = wbytes + (uint32_t)rcap * H * 2;
+  const uint32_t xrow = (uint32_t)H * 2;  // weight row stride
+  const uint32_t ts = tok_stride(H);      // token row stride
+  const uint32_t stage_bytes = gu_stage_bytes(H, rcap);
   uint8_t* stage_base = dsm_raw;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) {
-      mbar_init(smem_u32(&full[i]), 1);
-      mbar_init(smem_u32(&empty[i]), kWarps);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
   const int nact = *m.nact;
-  __syncthreads();
-  const int nfc = (F + fr - 1) / fr;
-  const int items = nact * nfc;
-  const int mine = items > (int)bid ? (items - 1 - (int)bid) / (int)nblk + 1 : 0;
-  auto issue = [&](int j) {
-    const int item = bid + j * nblk;
-    const int e = sm_act[item / nfc];
-    const int f0 = (item % nfc) * fr;
-    const int rows = min(fr, F - f0);
-    const uint32_t bytes = (uint32_t)rows * H * 2;
-    const int s = j % stages;
-    const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
-    const uint32_t bar = smem_u32(&full[s]);
-    const int r0 = sm_off[e];
-    const int rc = min(rcap, sm_off[e + 1] - r0);
-    const uint32_t xrow = (uint32_t)H * 2;
-    mbar_expect_tx(bar, 2 * bytes + rc * xrow);
-    bulk_load(dst, w_gate + ((int64_t)e * F + f0) * H, bytes, bar);
-    bulk_load(dst + (uint32_t)fr * H * 2, w_up + ((int64_t)e * F + f0) * H, bytes, bar);
-    for (int r = 0; r < rc; ++r)
-      bulk_load(dst + wbytes + r * xrow, x + (int64_t)sm_tok[r0 + r] * H, xrow, bar);
-  };
   if (warp == kWarps) {
     // producer warp: refills a stage as soon as all compute warps released
     // it, so the compute warps never stall on issuing copies
-    if (lane == 0)
-      for (int j = 0; j < mine; ++j) {
+    if (lane == 0) {
+      fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
+      GuCursor cur = gu_range(nact, F, fr, bid, nblk);
+      int a, f0, rows;
+      for (int j = 0; cur.next(a, f0, rows); ++j) {
         const int s = j % stages;
         if (j >= stages && !mbar_wait(smem_u32(&empty[s]), (uint32_t)(j / stages - 1) & 1u, s_abort, ws.err)) break;
-        issue(j);
+        TRACE_ITEM(0, j, 2);
+        const int e = sm_act[a];
+        const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
+        const uint32_t bar = smem_u32(&full[s]);
+        const int r0 = sm_off[e];
+        const int rc = min(rcap, sm_off[e + 1] - r0);
+        mbar_expect_tx(bar, (uint32_t)(2 * rows + rc) * xrow);
+        bulk_load(dst, w_gate + ((int64_t)e * F + f0) * H, (uint32_t)rows * xrow, bar);
+        bulk_load(dst + 8 * xrow, w_up + ((int64_t)e * F + f0) * H, (uint32_t)rows * xrow, bar);
+        for (int r = 0; r < rc; ++r)
+          bulk_load(dst + kMT * xrow + r * ts, x + (int64_t)sm_tok[r0 + r] * H, xrow, bar);
       }
+    }
     return;
   }
-  for (int j = 0; j < mine; ++j) {
-    const int item = bid + j * nblk;
-    const int e = sm_act[item / nfc];
-    const int f0 = (item % nfc) * fr;
-    const int rows = min(fr, F - f0);
+  GuCursor cur = gu_range(nact, F, fr, bid, nblk);
+  int a, f0, rows, tile = 0;
+  for (int j = 0; cur.next(a, f0, rows); ++j) {
+    const int e = sm_act[a];
     const int s = j % stages;
     if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, s_abort, ws.err)) break;
-    const uint4* gsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
-    const uint4* usm = gsm + (size_t)fr * hv;
+    if (threadIdx.x == 0) TRACE_ITEM(0, j, 0);
+    uint8_t* st = stage_base + (size_t)s * stage_bytes;
+    uint8_t* tok = st + kMT * xrow;
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += rcap) {
       const int rc = min(rcap, cnt - c0);
-      uint4* xr = reinterpret_cast<uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
-      if (c0 > 0) {  // more than rcap rows: later chunks are gathered into the same area
+      if (c0 > 0) {  // more than rcap token rows: later chunks are gathered into the same area
+        const int hv = H / 8;
         for (int i = threadIdx.x; i < rc * hv; i += kThreads) {
           const int r = i / hv, v = i - r * hv;
-          xr[i] = reinterpret_cast<const uint4*>(x + (int64_t)sm_tok[r0 + c0 + r] * H)[v];
+          *reinterpret_cast<uint4*>(tok + r * ts + v * 16) =
+              reinterpret_cast<const uint4*>(x + (int64_t)sm_tok[r0 + c0 + r] * H)[v];
         }
         consumer_sync();
       }
-      if (warp < rows) {
-        const uint4* gr = gsm + (size_t)warp * hv;
-        const uint4* ur = usm + (size_t)warp * hv;
-        for (int r = 0; r < rc; ++r) {
-          float g = 0.f, u = 0.f;
-          // all shared-memory loads of a 256-slice round are issued before
-          // any is used (independent loads instead of a dependent chain)
-          for (int v0 = 0; v0 < hv; v0 += 32 * 8) {
-            uint4 gq[8], uq[8], xq[8];
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int v = v0 + lane + 32 * i;
-              const bool ok = v < hv;
-              gq[i] = ok ? gr[v] : make_uint4(0, 0, 0, 0);
-              uq[i] = ok ? ur[v] : make_uint4(0, 0, 0, 0);
-              xq[i] = ok ? xr[r * hv + v] : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              float gv[8], uv[8], xv[8];
-              bf16x8_to_f32(gq[i], gv);
-              bf16x8_to_f32(uq[i], uv);
-              bf16x8_to_f32(xq[i], xv);
-#pragma unroll
-              for (int q = 0; q < 8; ++q) {
-                g = fmaf(gv[q], xv[q], g);
-                u = fmaf(uv[q], xv[q], u);
-              }
-            }
-          }
-#pragma unroll
-          for (int o = 16; o; o >>= 1) {
-            g += __shfl_xor_sync(0xffffffffu, g, o);
-            u += __shfl_xor_sync(0xffffffffu, u, o);
-          }
-          if (lane == 0) ws.hs[(int64_t)(r0 + c0 + r) * F + f0 + warp] = __float2bfloat16_rn(g * silu_ref(u));
+      // partial tiles alternate between two buffers: one barrier per tile
+      float* rb = red + (tile++ & 1) * (kWarps * kMT * 8);
+      warp_tile_mma(st, xrow, tok, ts, H, rc, rb);
+      if (c0 + rcap >= cnt) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
+      }
+      consumer_sync();
+      if (threadIdx.x < 64) {
+        const int i = threadIdx.x >> 3, n = threadIdx.x & 7;
+        if (i < rows && n < rc) {
+          const float g = red_sum(rb, i, n), u = red_sum(rb, i + 8, n);
+          ws.hs[(int64_t)(r0 + c0 + n) * F + f0 + i] = __float2bfloat16_rn(g * silu_ref(u));
         }
       }
-      if (c0 + rcap < cnt) consumer_sync();  // the next chunk's rows overwrite xr
+      if (c0 + rcap < cnt) consumer_sync();  // the next chunk's rows overwrite the token area
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
+    if (threadIdx.x == 0) TRACE_ITEM(0, j, 1);
   }
 }
 
@@ -596,172 +757,215 @@ decode_gateup_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* _
                      DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   __shared__ __align__(8) uint64_t full[4], empty[4];
+  __shared__ __align__(16) float red[2 * kWarps * kMT * 8];
   __shared__ int s_abort;
-  if (threadIdx.x == 0) s_abort = 0;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    init_ring(full, empty, stages);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   wait_prior_grid();
   allow_next_grid();
-  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
+  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots], m_pos[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
-  const Meta m = load_meta(ws, T, E, m_off, m_act, &m_nact, m_tok, m_w);
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, empty,
+  const Meta m = load_meta(ws, T, E, m_off, m_act, &m_nact, m_tok, m_w, m_pos);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, red, full, empty,
               &s_abort, m);
 }
 
-// down: item = (active expert e, hr rows of H starting at h0): stage =
-// [hr][F] bf16.  Warp w computes rows h0 + w, h0 + w + 8, ...:
-// d[row, h] = (down_e[h] . h_row) * gate weight of the row, fp32.
-__device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr,
-                                          int rcap, int stages, DecodeWs ws, int bid, int nblk, uint8_t* dsm_raw,
-                                          uint64_t* full, uint64_t* empty, int* s_abort, Meta m) {
+// down + combine: block b owns the output columns [hb0, hb1) = [b H / nblk,
+// (b+1) H / nblk) of y for every token.  Its items are (active expert e,
+// at most hr <= 16 rows of its columns starting at h0); block b starts at
+// active expert b mod nact, so the blocks read different experts' rows at
+// the same time.  Stage = up to 16 rows of down_e (one bulk copy), then the
+// expert's h rows.  One 16 x 8 tile per item: d[row, h] = (down_e[h] .
+// h_row) * gate weight of the row, kept in shared memory (dsm [slots][nhmax]
+// fp32, by expert-sorted row).  After the last item the block sums the k
+// slots of each token in slot order j = 0..k-1 (moe_ffn_block.mlir:179-206),
+// adds the residual when there is one, and writes y[:, hb0:hb1): no global d
+// buffer, no combine pass and no barrier after the down rows.
+//
+// The first `pre` items' weight rows were already requested by
+// down_prefetch (before the grid barrier that publishes h); for those the
+// producer only adds the h rows to the stage.
+struct DnCursor {
+  int i, start, h0, nact, hb0, hb1, hr;
+  __device__ __forceinline__ bool next(int& ea, int& eh0, int& rows) {
+    if (i >= nact || hb0 >= hb1) return false;
+    ea = start + i < nact ? start + i : start + i - nact;
+    eh0 = h0;
+    rows = min(hr, hb1 - h0);
+    h0 += rows;
+    if (h0 >= hb1) {
+      h0 = hb0;
+      ++i;
+    }
+    return true;
+  }
+};
+
+__device__ __forceinline__ DnCursor dn_range(int nact, int H, int hr, int bid, int nblk) {
+  const int hb0 = (int)((int64_t)H * bid / nblk), hb1 = (int)((int64_t)H * (bid + 1) / nblk);
+  return DnCursor{0, nact > 0 ? bid % nact : 0, hb0, nact, hb0, hb1, hr};
+}
+
+__device__ __host__ inline uint32_t dn_stage_bytes(int F, int rcap) {
+  return (uint32_t)kMT * F * 2 + (uint32_t)rcap * tok_stride(F);
+}
+
+// The down ring: its first nb stages lie beside the gate/up ring (so they
+// can be filled while gate/up still runs), the rest over the gate/up ring's
+// memory, free once this block's gate/up items are done.
+struct DnRing {
+  uint8_t* beside;
+  uint8_t* front;
+  int nb;
+  uint32_t sb;  // stage bytes
+  __device__ __forceinline__ uint8_t* stage(int s) const {
+    return s < nb ? beside + (size_t)s * sb : front + (size_t)(s - nb) * sb;
+  }
+};
+
+__device__ __forceinline__ void mbar_expect_tx_only(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+__device__ __forceinline__ void issue_down_rows(const __nv_bfloat16* __restrict__ w_down, int e, int H, int F, int h0,
+                                                int rows, uint32_t dst, uint32_t bar) {
+  bulk_load(dst, w_down + ((int64_t)e * H + h0) * F, (uint32_t)rows * F * 2, bar);
+}
+
+// Producer lane: request the weight rows of this block's first down items
+// into the ring stages beside the gate/up ring.  Returns how many.
+__device__ __forceinline__ int down_prefetch(const __nv_bfloat16* __restrict__ w_down, int H, int F, int hr, int bid,
+                                             int nblk, DnRing ring, uint64_t* full, Meta m) {
+  DnCursor cur = dn_range(*m.nact, H, hr, bid, nblk);
+  int a, h0, rows, j = 0;
+  fence_proxy_async_smem();
+  for (; j < ring.nb && cur.next(a, h0, rows); ++j) {
+    const uint32_t bar = smem_u32(&full[j]);
+    mbar_expect_tx_only(bar, (uint32_t)rows * F * 2);
+    issue_down_rows(w_down, m.act[a], H, F, h0, rows, smem_u32(ring.stage(j)), bar);
+  }
+  return j;
+}
+
+template <class TY>
+__device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k,
+                                          int hr, int rcap, int stages, int pre, DecodeWs ws, int bid, int nblk,
+                                          DnRing ring, float* dsm, int nhmax, float* red, uint64_t* full,
+                                          uint64_t* empty, int* s_abort, Meta m, TY* y) {
   const int32_t* sm_off = m.off;
   const int32_t* sm_act = m.act;
   const float* sm_w = m.w;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int fv = F / 8;
-  // stage: [hr][F] weights, then [rcap][F] h rows of the item's expert
-  const uint32_t wbytes = (uint32_t)hr * F * 2;
-  const uint32_t stage_bytes = wbytes + (uint32_t)rcap * F * 2;
-  uint8_t* stage_base = dsm_raw;
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) {
-      mbar_init(smem_u32(&full[i]), 1);
-      mbar_init(smem_u32(&empty[i]), kWarps);
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  }
-  fence_proxy_async_smem();  // earlier generic use of this shared memory precedes the bulk copies
+  const uint32_t hrow = (uint32_t)F * 2;  // weight row stride
+  const uint32_t ts = tok_stride(F);      // h row stride
+  const uint32_t stage_bytes = dn_stage_bytes(F, rcap);
   const int nact = *m.nact;
-  __syncthreads();
-  const int nhc = (H + hr - 1) / hr;
-  const int items = nact * nhc;
-  const int mine = items > (int)bid ? (items - 1 - (int)bid) / (int)nblk + 1 : 0;
-  auto issue = [&](int j) {
-    const int item = bid + j * nblk;
-    const int e = sm_act[item / nhc];
-    const int h0 = (item % nhc) * hr;
-    const uint32_t bytes = (uint32_t)min(hr, H - h0) * F * 2;
-    const int s = j % stages;
-    const uint32_t bar = smem_u32(&full[s]);
-    const int r0 = sm_off[e];
-    const int rc = min(rcap, sm_off[e + 1] - r0);
-    const uint32_t hbytes = (uint32_t)rc * F * 2;
-    const uint32_t dst = smem_u32(stage_base + (size_t)s * stage_bytes);
-    mbar_expect_tx(bar, bytes + hbytes);
-    bulk_load(dst, w_down + ((int64_t)e * H + h0) * F, bytes, bar);
-    bulk_load(dst + wbytes, ws.hs + (int64_t)r0 * F, hbytes, bar);
-  };
   if (warp == kWarps) {
-    // producer warp: refills a stage as soon as all compute warps released
-    // it, so the compute warps never stall on issuing copies
-    if (lane == 0)
-      for (int j = 0; j < mine; ++j) {
+    // producer warp: refills a stage as soon as all compute warps released it
+    if (lane == 0) {
+      // the ring's later stages reuse the gate/up ring's memory
+      fence_proxy_async_smem();
+      DnCursor cur = dn_range(nact, H, hr, bid, nblk);
+      int a, h0, rows;
+      for (int j = 0; cur.next(a, h0, rows); ++j) {
         const int s = j % stages;
-        if (j >= stages && !mbar_wait(smem_u32(&empty[s]), (uint32_t)(j / stages - 1) & 1u, s_abort, ws.err)) break;
-        issue(j);
+        const int e = sm_act[a];
+        const uint32_t bar = smem_u32(&full[s]);
+        const int r0 = sm_off[e];
+        const int rc = min(rcap, sm_off[e + 1] - r0);
+        const uint32_t dst = smem_u32(ring.stage(s));
+        TRACE_ITEM(1, j, 2);
+        if (j < pre) {  // weights already requested
+          mbar_expect_tx(bar, (uint32_t)rc * hrow);
+        } else {
+          if (j >= stages && !mbar_wait(smem_u32(&empty[s]), (uint32_t)(j / stages - 1) & 1u, s_abort, ws.err))
+            break;
+          mbar_expect_tx(bar, (uint32_t)(rows + rc) * hrow);
+          issue_down_rows(w_down, e, H, F, h0, rows, dst, bar);
+        }
+        for (int r = 0; r < rc; ++r) bulk_load(dst + kMT * hrow + r * ts, ws.hs + (int64_t)(r0 + r) * F, hrow, bar);
       }
+    }
     return;
   }
-  for (int j = 0; j < mine; ++j) {
-    const int item = bid + j * nblk;
-    const int e = sm_act[item / nhc];
-    const int h0 = (item % nhc) * hr;
-    const int rows = min(hr, H - h0);
+  DnCursor cur = dn_range(nact, H, hr, bid, nblk);
+  const int hb0 = cur.hb0, nh = cur.hb1 - cur.hb0;
+  int a, h0, rows, tile = 0;
+  for (int j = 0; cur.next(a, h0, rows); ++j) {
+    const int e = sm_act[a];
     const int s = j % stages;
     if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, s_abort, ws.err)) break;
-    const uint4* wsm = reinterpret_cast<const uint4*>(stage_base + (size_t)s * stage_bytes);
+    if (threadIdx.x == 0) TRACE_ITEM(1, j, 0);
+    uint8_t* st = ring.stage(s);
+    uint8_t* hsm = st + kMT * hrow;
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += rcap) {
       const int rc = min(rcap, cnt - c0);
-      uint4* hr8 = reinterpret_cast<uint4*>(stage_base + (size_t)s * stage_bytes + wbytes);
       if (c0 > 0) {  // more than rcap rows: later chunks are loaded into the same area
-        for (int i = threadIdx.x; i < rc * fv; i += kThreads)
-          hr8[i] = reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0) * F)[i];
+        const int fv = F / 8;
+        for (int i = threadIdx.x; i < rc * fv; i += kThreads) {
+          const int r = i / fv, v = i - r * fv;
+          *reinterpret_cast<uint4*>(hsm + r * ts + v * 16) =
+              reinterpret_cast<const uint4*>(ws.hs + (int64_t)(r0 + c0 + r) * F)[v];
+        }
         consumer_sync();
       }
-      // each warp takes its rows jr = warp + 8*jj (jj < 4) together: four
-      // independent dot products in flight
-      for (int jb = 0; jb < rows; jb += 4 * kWarps) {
-        for (int r = 0; r < rc; ++r) {
-          float acc[4] = {0.f, 0.f, 0.f, 0.f};
-          for (int v0 = 0; v0 < fv; v0 += 32 * 4) {
-            uint4 hq[4];
-#pragma unroll
-            for (int i = 0; i < 4; ++i) {
-              const int v = v0 + lane + 32 * i;
-              hq[i] = v < fv ? hr8[r * fv + v] : make_uint4(0, 0, 0, 0);
-            }
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) {
-              const int jr = jb + warp + kWarps * jj;
-              const uint4* wr = wsm + (size_t)min(jr, rows - 1) * fv;
-#pragma unroll
-              for (int i = 0; i < 4; ++i) {
-                const int v = v0 + lane + 32 * i;
-                if (v < fv) {
-                  float wv[8], hv8[8];
-                  bf16x8_to_f32(wr[v], wv);
-                  bf16x8_to_f32(hq[i], hv8);
-#pragma unroll
-                  for (int q = 0; q < 8; ++q) acc[jj] = fmaf(wv[q], hv8[q], acc[jj]);
-                }
-              }
-            }
-          }
-#pragma unroll
-          for (int o = 16; o; o >>= 1)
-#pragma unroll
-            for (int jj = 0; jj < 4; ++jj) acc[jj] += __shfl_xor_sync(0xffffffffu, acc[jj], o);
-          if (lane < 4) {
-            const int jr = jb + warp + kWarps * lane;
-            const float a = lane == 0 ? acc[0] : lane == 1 ? acc[1] : lane == 2 ? acc[2] : acc[3];
-            if (jr < rows) {
-              const int row = r0 + c0 + r;
-              ws.d[(int64_t)row * H + h0 + jr] = a * sm_w[row];
-            }
-          }
+      float* rb = red + (tile++ & 1) * (kWarps * kMT * 8);
+      warp_tile_mma(st, hrow, hsm, ts, F, rc, rb);
+      if (c0 + rcap >= cnt) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
+      }
+      consumer_sync();
+      if (threadIdx.x < kMT * 8) {
+        const int i = threadIdx.x >> 3, n = threadIdx.x & 7;
+        if (i < rows && n < rc) {
+          const int row = r0 + c0 + n;
+          dsm[row * nhmax + (h0 - hb0) + i] = red_sum(rb, i, n) * sm_w[row];
         }
       }
       if (c0 + rcap < cnt) consumer_sync();  // the next chunk's rows overwrite the h area
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
+    if (threadIdx.x == 0) TRACE_ITEM(1, j, 1);
+  }
+  consumer_sync();  // every d value of this block is in dsm
+  TRACE(6);
+  // y[t, h] = sum_{j<k} d[slot j of t, h] in slot order, + residual
+  for (int i = threadIdx.x; i < T * nh; i += kThreads) {
+    const int t = i / nh, hh = i - t * nh;
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) acc += dsm[m.pos[j * T + t] * nhmax + hh];
+    const int64_t o = (int64_t)t * H + hb0 + hh;
+    if (ws.res) acc = ws.res[o] + acc;  // the sub-layer's residual add after the sum
+    y[o] = from_f32<TY>(acc);
   }
 }
 
+template <class TY>
 __global__ void __launch_bounds__(kBlockThreads)
-decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int H, int F, int E, int hr, int rcap, int stages,
-                   DecodeWs ws) {
+decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int hr, int rcap,
+                   int stages, int nhmax, TY* y, DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
-  __shared__ __align__(8) uint64_t full[4], empty[4];
+  __shared__ __align__(8) uint64_t full[8], empty[8];
+  __shared__ __align__(16) float red[2 * kWarps * kMT * 8];
   __shared__ int s_abort;
-  if (threadIdx.x == 0) s_abort = 0;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    init_ring(full, empty, stages);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   wait_prior_grid();
   allow_next_grid();
-  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
+  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots], m_pos[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
-  const Meta m = load_meta(ws, 1, E, m_off, m_act, &m_nact, m_tok, m_w);
-  down_body(w_down, H, F, E, hr, rcap, stages, ws, blockIdx.x, gridDim.x, dsm_raw, full, empty, &s_abort, m);
-}
-
-// --------------------------------------------------------------- combine --
-// y[t, h] = sum_{j<k} d[slot_pos[j*T + t], h] in slot order (deterministic).
-template <class TY>
-__device__ __forceinline__ void combine_body(int T, int H, int k, TY* y, const DecodeWs& ws, int64_t gtid,
-                                             int64_t nthreads) {
-  for (int64_t i = gtid; i < (int64_t)T * H; i += nthreads) {
-    const int t = (int)(i / H), h = (int)(i - (int64_t)t * H);
-    float acc = 0.f;
-    for (int j = 0; j < k; ++j) acc += __ldcg(ws.d + (int64_t)__ldcg(ws.slot_pos + j * T + t) * H + h);
-    if (ws.res) acc = ws.res[i] + acc;  // the sub-layer's residual add after the sum
-    y[i] = from_f32<TY>(acc);
-  }
-}
-
-template <class TY>
-__global__ void __launch_bounds__(kThreads)
-decode_combine_kernel(int T, int H, int k, TY* y, DecodeWs ws) {
-  wait_prior_grid();
-  combine_body<TY>(T, H, k, y, ws, (int64_t)blockIdx.x * kThreads + threadIdx.x, (int64_t)gridDim.x * kThreads);
+  const Meta m = load_meta(ws, T, E, m_off, m_act, &m_nact, m_tok, m_w, m_pos);
+  const DnRing ring{dsm_raw, dsm_raw, 0, dn_stage_bytes(F, rcap)};
+  float* dsm = reinterpret_cast<float*>(dsm_raw + (((size_t)stages * dn_stage_bytes(F, rcap) + 127) & ~(size_t)127));
+  down_body<TY>(w_down, T, H, F, E, k, hr, rcap, stages, 0, ws, blockIdx.x, gridDim.x, ring, dsm, nhmax, red,
+                full, empty, &s_abort, m, y);
 }
 
 // ---------------------------------------------------------- fused kernel --
@@ -815,26 +1019,48 @@ __device__ __forceinline__ FusedRoutingSmem carve_fused_routing(uint8_t* base, i
   return r;
 }
 
+// Placement of the streaming phases in the fused kernel's dynamic shared
+// memory: the gate/up ring at 0; the down ring right after it when both fit
+// (then the down weights of a block's first items are requested before the
+// grid barrier that publishes h, overlapping the barrier and the other
+// blocks' last gate/up items), else at 0 as well; the down phase's d values
+// after both.  The routing phases use the start of the area before either.
+struct DecodeSmem {
+  size_t dn_off, dsm_off, total;
+  int dn_beside;  // down stages beside the gate/up ring (requested before the barrier)
+  bool prefetch;
+};
+
 template <class TW, class TY>
 __global__ void __launch_bounds__(kBlockThreads, 1)
 decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ wr,
                     const __nv_bfloat16* __restrict__ w_gate, const __nv_bfloat16* __restrict__ w_up,
                     const __nv_bfloat16* __restrict__ w_down, int T, int H, int F, int E, int k, int normalize,
-                    int fr, int stages_gu, int hr, int stages_dn, int rcap, TY* y, DecodeWs ws) {
+                    int fr, int stages_gu, int hr, int stages_dn, int rcap, int nhmax, DecodeSmem lay, TY* y,
+                    DecodeWs ws) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
-  __shared__ __align__(8) uint64_t full_gu[4], full_dn[4], empty_gu[4], empty_dn[4];
+  __shared__ __align__(8) uint64_t full_gu[4], full_dn[8], empty_gu[4], empty_dn[8];
+  __shared__ __align__(16) float red[2 * kWarps * kMT * 8];
   __shared__ int s_abort;
-  if (threadIdx.x == 0) s_abort = 0;
+  if (threadIdx.x == 0) {
+    s_abort = 0;
+    init_ring(full_gu, empty_gu, stages_gu);
+    init_ring(full_dn, empty_dn, stages_dn);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
   const int bid = blockIdx.x, nblk = gridDim.x;
   const bool compute = threadIdx.x < kThreads;  // warps 0..kWarps-1; the last warp produces copies
+  TRACE(0);
   if (compute) route_body<TW>(x, wr, T, H, E, ws, reinterpret_cast<float*>(dsm_raw), bid, nblk);
+  TRACE(1);
   grid_barrier(ws.gbar, 1u * nblk, &s_abort, ws.err);
+  TRACE(2);
   // every block runs softmax / top-k for all T tokens and builds the (small)
   // permutation itself, so the streaming phases start without another
   // barrier; block 0 also publishes the routing
-  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots];
+  __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots], m_pos[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
-  const Meta m{m_off, m_act, &m_nact, m_tok, m_w};
+  const Meta m{m_off, m_act, &m_nact, m_tok, m_w, m_pos};
   if (compute) {
     const FusedRoutingSmem rs = carve_fused_routing(dsm_raw, T, E);
     block_softmax_topk(ws.logits, T, E, k, normalize, rs.prob, rs.w, rs.ids);
@@ -849,12 +1075,19 @@ decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
       permute_body(T, E, k, ws, rs.scratch, m, rs.ids, rs.w, bid == 0);
   }
   __syncthreads();  // the routing tables, for the producer warp too
-  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages_gu, ws, bid, nblk, dsm_raw, full_gu, empty_gu, &s_abort,
-              m);
+  TRACE(3);
+  gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages_gu, ws, bid, nblk, dsm_raw, red, full_gu, empty_gu,
+              &s_abort, m);
+  TRACE(4);
+  const DnRing ring{dsm_raw + lay.dn_off, dsm_raw, lay.dn_beside, dn_stage_bytes(F, rcap)};
+  int pre = 0;
+  if (lay.prefetch && threadIdx.x == kThreads)  // the producer lane, done issuing its gate/up copies
+    pre = down_prefetch(w_down, H, F, hr, bid, nblk, ring, full_dn, m);
   grid_barrier(ws.gbar, 2u * nblk, &s_abort, ws.err);
-  down_body(w_down, H, F, E, hr, rcap, stages_dn, ws, bid, nblk, dsm_raw, full_dn, empty_dn, &s_abort, m);
-  grid_barrier(ws.gbar, 3u * nblk, &s_abort, ws.err);
-  if (compute) combine_body<TY>(T, H, k, y, ws, (int64_t)bid * kThreads + threadIdx.x, (int64_t)nblk * kThreads);
+  TRACE(5);
+  down_body<TY>(w_down, T, H, F, E, k, hr, rcap, stages_dn, pre, ws, bid, nblk, ring,
+                reinterpret_cast<float*>(dsm_raw + lay.dsm_off), nhmax, red, full_dn, empty_dn, &s_abort, m, y);
+  TRACE(7);
 }
 
 template <typename... KArgs, typename... Args>
@@ -873,10 +1106,69 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
   return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
 }
 
+// Shared-memory staging of the two streaming phases.  An expert receives at
+// most T rows (the top-k ids of a token are distinct), so a stage holds
+// rcap = min(kRC, T) token rows (at a padded stride) beside its 16 weight
+// rows.  Gate/up items are up to fr = 8 row pairs, down items up to
+// hr = min(16, ceil(H / nblk)) rows.  A shape where two stages of either
+// phase do not fit leaves the decode path.
+struct DecodePlan {
+  int rcap, fr, hr, stages_gu, stages_dn, nhmax;
+  size_t stage_gu, stage_dn, dsm_bytes;
+  DecodeSmem lay;
+  bool ok;
+};
+
+// dynamic shared memory beside the kernels' static tables (< 12 KB)
+constexpr size_t kSmemDyn = 227 * 1024 - 12 * 1024;
+
+DecodePlan decode_plan(int64_t T, int64_t H, int64_t F, int64_t k, int nblk) {
+  DecodePlan p{};
+  p.rcap = (int)(T < kRC ? T : kRC);
+  p.nhmax = (int)((H + nblk - 1) / nblk);
+  p.dsm_bytes = align_up((size_t)k * T * p.nhmax * 4, 128);
+  int fr_env = 0, gu_env = 0;
+  if (const char* v = getenv("FRANK_DECODE_FR")) fr_env = atoi(v);
+  if (const char* v = getenv("FRANK_DECODE_GU_STAGES")) gu_env = atoi(v);
+  const size_t budget = kSmemDyn > p.dsm_bytes ? kSmemDyn - p.dsm_bytes : 0;
+  p.fr = fr_env > 0 && fr_env < 8 ? fr_env : 8;
+  p.hr = p.nhmax < kMT ? p.nhmax : kMT;
+  p.stage_gu = gu_stage_bytes((int)H, p.rcap);
+  p.stage_dn = dn_stage_bytes((int)F, p.rcap);
+  p.stages_gu = (int)(budget / p.stage_gu);
+  // about 128 KB in flight per SM covers the loaded HBM latency
+  auto depth = [](size_t stage) {
+    const int want = (int)((128 * 1024 + stage - 1) / stage);
+    return want < 2 ? 2 : (want > 4 ? 4 : want);
+  };
+  if (p.stages_gu > depth(p.stage_gu)) p.stages_gu = depth(p.stage_gu);
+  if (gu_env >= 2 && gu_env <= 4 && (size_t)gu_env * p.stage_gu <= budget) p.stages_gu = gu_env;
+  const size_t gu_bytes = (size_t)p.stages_gu * p.stage_gu;
+  // down ring: stages beside the gate/up ring (requested before the second
+  // grid barrier) and stages over the gate/up ring's memory; at most 8
+  const size_t rest = budget > gu_bytes + 128 ? budget - gu_bytes - 128 : 0;
+  int beside = (int)(rest / p.stage_dn);
+  const char* pf = getenv("FRANK_DECODE_PREFETCH");
+  if (beside < 2 || (pf && pf[0] == '0')) beside = 0;
+  if (beside > 4) beside = 4;
+  int front = (int)((beside ? gu_bytes : budget) / p.stage_dn);
+  if (front > 8 - beside) front = 8 - beside;
+  p.stages_dn = beside + front;
+  p.ok = p.stages_gu >= 2 && p.stages_dn >= 2 && H % 16 == 0 && F % 16 == 0;
+  p.lay.prefetch = beside > 0;
+  p.lay.dn_beside = beside;
+  p.lay.dn_off = beside ? align_up(gu_bytes, 128) : 0;
+  const size_t dn_end = beside ? p.lay.dn_off + (size_t)beside * p.stage_dn : (size_t)front * p.stage_dn;
+  const size_t ring_end = align_up(dn_end > gu_bytes ? dn_end : gu_bytes, 128);
+  p.lay.dsm_off = ring_end;
+  p.lay.total = ring_end + p.dsm_bytes;
+  return p;
+}
+
 template <class TW, class TY>
 int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, const void* wd, int64_t T, int64_t H,
-                 int64_t F, int64_t E, int64_t k, int normalize, int fr, int stages_gu, int hr, int stages_dn,
-                 int rcap, void* y, const DecodeWs& ws, size_t smem, cudaStream_t st) {
+                 int64_t F, int64_t E, int64_t k, int normalize, const DecodePlan& pl, void* y, const DecodeWs& ws,
+                 size_t smem, cudaStream_t st) {
   auto kern = decode_fused_kernel<TW, TY>;
   FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
   int per_sm = 0;
@@ -897,53 +1189,10 @@ int launch_fused(const void* x, const void* wr, const void* wg, const void* wu, 
   cfg.numAttrs = 1;
   FRANK_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, (const __nv_bfloat16*)x, (const TW*)wr, (const __nv_bfloat16*)wg,
                                     (const __nv_bfloat16*)wu, (const __nv_bfloat16*)wd, (int)T, (int)H, (int)F,
-                                    (int)E, (int)k, normalize, fr, stages_gu, hr, stages_dn, rcap, (TY*)y, ws));
+                                    (int)E, (int)k, normalize, pl.fr, pl.stages_gu, pl.hr, pl.stages_dn, pl.rcap,
+                                    pl.nhmax, pl.lay, (TY*)y, ws));
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
-}
-
-// Shared-memory staging of the two streaming phases.  An expert receives at
-// most T rows (the top-k ids of a token are distinct), so a stage holds
-// rcap = min(kRC, T) token rows beside its weights.  Rows per item start at
-// 32 KB of each gate/up matrix and 48 KB of down and halve until two stages
-// fit; a shape where even one row does not leaves the decode path.
-struct DecodePlan {
-  int rcap, fr, hr, stages_gu, stages_dn;
-  size_t stage_gu, stage_dn;
-  bool ok;
-};
-
-DecodePlan decode_plan(int64_t T, int64_t H, int64_t F) {
-  // dynamic shared memory beside the kernels' static tables (< 8 KB)
-  constexpr size_t kSmemDyn = 227 * 1024 - 8 * 1024;
-  DecodePlan p{};
-  p.rcap = (int)(T < kRC ? T : kRC);
-  p.fr = (int)(16384 / H < 1 ? 1 : (16384 / H > kWarps ? kWarps : 16384 / H));
-  p.hr = (int)(24576 / F < 1 ? 1 : (24576 / F > 32 ? 32 : 24576 / F));
-  for (;;) {
-    p.stage_gu = (size_t)2 * p.fr * H * 2 + (size_t)p.rcap * H * 2;
-    p.stages_gu = (int)(kSmemDyn / p.stage_gu);
-    if (p.stages_gu >= 2 || p.fr == 1) break;
-    p.fr /= 2;
-  }
-  for (;;) {
-    p.stage_dn = (size_t)p.hr * F * 2 + (size_t)p.rcap * F * 2;
-    p.stages_dn = (int)(kSmemDyn / p.stage_dn);
-    if (p.stages_dn >= 2 || p.hr == 1) break;
-    p.hr /= 2;
-  }
-  // about 96 KB in flight per SM is enough to stream at full rate; deeper
-  // rings only add shared-memory write traffic that slows the dot products
-  // of the stage being consumed (measured: T=1 with 3-4 stages of 49-68 KB,
-  // 45 us; 2 stages, 43 us)
-  auto depth = [](size_t stage) {
-    const int want = (int)((96 * 1024 + stage - 1) / stage);
-    return want < 2 ? 2 : (want > 4 ? 4 : want);
-  };
-  p.stages_gu = p.stages_gu > depth(p.stage_gu) ? depth(p.stage_gu) : p.stages_gu;
-  p.stages_dn = p.stages_dn > depth(p.stage_dn) ? depth(p.stage_dn) : p.stages_dn;
-  p.ok = p.stages_gu >= 2 && p.stages_dn >= 2;
-  return p;
 }
 
 }  // namespace
@@ -952,7 +1201,7 @@ namespace frank {
 
 bool decode_path_ok(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
   return dtype == FRANK_BF16 && T >= 1 && T <= 64 && k * T <= kMaxSlots && E <= kMaxE && H % 8 == 0 && F % 8 == 0 &&
-         k * T <= E && decode_plan(T, H, F).ok;
+         k * T <= E && decode_plan(T, H, F, k, num_sms()).ok;
 }
 
 size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
@@ -968,7 +1217,6 @@ size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t
   c.take<__nv_bfloat16>(n * F);
   c.take<int32_t>(E);
   c.take<int32_t>(1);
-  c.take<float>(n * H);
   c.take<unsigned>(1);
   return align_up(c.used, 256);
 }
@@ -1000,94 +1248,87 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.hs = c.take<__nv_bfloat16>(n * F);
   ws.active = c.take<int32_t>(E);
   ws.nactive = c.take<int32_t>(1);
-  ws.d = c.take<float>(n * H);
   ws.gbar = c.take<unsigned>(1);
   ws.res = residual;
   ws.n_slots = (int)n;
   ws.err = device_error_word();
-  const DecodePlan plan = decode_plan(T, H, F);
+  const int grid_p = num_sms();
+  const DecodePlan plan = decode_plan(T, H, F, k, grid_p);
   if (!plan.ok) {
     set_error("decode block: n_embd=%lld / n_ff=%lld too large for the streaming kernels", (long long)H,
               (long long)F);
     return FRANK_EINVAL;
   }
-  const int rcap = plan.rcap, fr = plan.fr, hr = plan.hr, stages_gu = plan.stages_gu, stages_dn = plan.stages_dn;
-  const size_t stage_gu = plan.stage_gu, stage_dn = plan.stage_dn;
   const char* fenv = getenv("FRANK_DECODE_FUSED");
   if (!(fenv && fenv[0] == '0')) {
     // one cooperative launch (decode_fused_kernel)
-    size_t smem = stages_gu * stage_gu;
-    if (stages_dn * stage_dn > smem) smem = stages_dn * stage_dn;
+    size_t smem = plan.lay.total;
     if (fused_routing_smem(T, E) > smem) smem = fused_routing_smem(T, E);
     mark(0, st);
     FRANK_CUDA_TRY(cudaMemsetAsync(ws.gbar, 0, sizeof(unsigned), st));
     int st_launch;
     if (wr_dtype == FRANK_F32 && y_dtype == FRANK_F32)
-      st_launch = launch_fused<float, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
-                                             stages_gu, hr, stages_dn, rcap, y, ws, smem, st);
+      st_launch = launch_fused<float, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, plan, y, ws,
+                                             smem, st);
     else if (wr_dtype == FRANK_F32)
-      st_launch = launch_fused<float, __nv_bfloat16>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
-                                                     stages_gu, hr, stages_dn, rcap, y, ws, smem, st);
+      st_launch = launch_fused<float, __nv_bfloat16>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize,
+                                                     plan, y, ws, smem, st);
     else if (y_dtype == FRANK_F32)
-      st_launch = launch_fused<__nv_bfloat16, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, fr,
-                                                     stages_gu, hr, stages_dn, rcap, y, ws, smem, st);
+      st_launch = launch_fused<__nv_bfloat16, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize,
+                                                     plan, y, ws, smem, st);
     else
       st_launch = launch_fused<__nv_bfloat16, __nv_bfloat16>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k,
-                                                             normalize, fr, stages_gu, hr, stages_dn, rcap, y, ws,
-                                                             smem, st);
+                                                             normalize, plan, y, ws, smem, st);
     FRANK_TRY(st_launch);
     for (int m = 1; m <= 6; ++m) mark(m, st);
   } else {
-  mark(0, st);
-  const unsigned rblocks = (unsigned)num_sms();
-  if (wr_dtype == FRANK_F32)
-    decode_route_kernel<float><<<rblocks, kThreads, 0, st>>>((const __nv_bfloat16*)x, (const float*)wr, (int)T,
-                                                             (int)H, (int)E, (int)k, normalize, ws);
-  else
-    decode_route_kernel<__nv_bfloat16><<<rblocks, kThreads, 0, st>>>(
-        (const __nv_bfloat16*)x, (const __nv_bfloat16*)wr, (int)T, (int)H, (int)E, (int)k, normalize, ws);
-  FRANK_LAUNCH_CHECK();
-  const size_t prob_smem = (size_t)T * E * sizeof(float);
-  FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                      (int)prob_smem));
-  FRANK_CUDA_TRY(launch_pdl(decode_finalize_kernel, dim3(1), dim3(kThreads), prob_smem, st, (int)T, (int)E, (int)k,
-                            normalize, ws));
-  FRANK_LAUNCH_CHECK();
-  mark(1, st);
-  mark(2, st);
-  mark(3, st);
-  ws.err = device_error_word();
-  const int grid_p = num_sms();
-  {
-    const size_t smem = stages_gu * stage_gu;
-    FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kBlockThreads), smem, st,
-                              (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
-                              (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, (int)E, fr, rcap, stages_gu,
-                              ws));
-    FRANK_LAUNCH_CHECK();
-  }
-  mark(4, st);
-  {
-    const size_t smem = stages_dn * stage_dn;
-    FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    FRANK_CUDA_TRY(launch_pdl(decode_down_kernel, dim3(grid_p), dim3(kBlockThreads), smem, st,
-                              (const __nv_bfloat16*)w_down_p, (int)H, (int)F, (int)E, hr, rcap, stages_dn, ws));
-    FRANK_LAUNCH_CHECK();
-  }
-  mark(5, st);
-  {
-    const int64_t tot = T * H;
-    const unsigned g = (unsigned)((tot + kThreads - 1) / kThreads);
-    if (y_dtype == FRANK_F32)
-      FRANK_CUDA_TRY(launch_pdl(decode_combine_kernel<float>, dim3(g), dim3(kThreads), 0, st, (int)T, (int)H,
-                                (int)k, (float*)y, ws));
+    // the same bodies as four launches chained by programmatic dependent launch
+    mark(0, st);
+    const unsigned rblocks = (unsigned)grid_p;
+    if (wr_dtype == FRANK_F32)
+      decode_route_kernel<float><<<rblocks, kThreads, 0, st>>>((const __nv_bfloat16*)x, (const float*)wr, (int)T,
+                                                               (int)H, (int)E, (int)k, normalize, ws);
     else
-      FRANK_CUDA_TRY(launch_pdl(decode_combine_kernel<__nv_bfloat16>, dim3(g), dim3(kThreads), 0, st, (int)T,
-                                (int)H, (int)k, (__nv_bfloat16*)y, ws));
+      decode_route_kernel<__nv_bfloat16><<<rblocks, kThreads, 0, st>>>(
+          (const __nv_bfloat16*)x, (const __nv_bfloat16*)wr, (int)T, (int)H, (int)E, (int)k, normalize, ws);
     FRANK_LAUNCH_CHECK();
-  }
-  mark(6, st);
+    const size_t prob_smem = (size_t)T * E * sizeof(float);
+    FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_finalize_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)prob_smem));
+    FRANK_CUDA_TRY(launch_pdl(decode_finalize_kernel, dim3(1), dim3(kThreads), prob_smem, st, (int)T, (int)E, (int)k,
+                              normalize, ws));
+    FRANK_LAUNCH_CHECK();
+    mark(1, st);
+    mark(2, st);
+    mark(3, st);
+    {
+      const size_t smem = (size_t)plan.stages_gu * plan.stage_gu;
+      FRANK_CUDA_TRY(
+          cudaFuncSetAttribute(decode_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      FRANK_CUDA_TRY(launch_pdl(decode_gateup_kernel, dim3(grid_p), dim3(kBlockThreads), smem, st,
+                                (const __nv_bfloat16*)x, (const __nv_bfloat16*)w_gate_p,
+                                (const __nv_bfloat16*)w_up_p, (int)T, (int)H, (int)F, (int)E, plan.fr, plan.rcap,
+                                plan.stages_gu, ws));
+      FRANK_LAUNCH_CHECK();
+    }
+    mark(4, st);
+    {
+      const size_t smem = align_up((size_t)plan.stages_dn * plan.stage_dn, 128) + plan.dsm_bytes;
+#define FRANK_DOWN_CASE(TY)                                                                                         \
+  FRANK_CUDA_TRY(cudaFuncSetAttribute(decode_down_kernel<TY>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)); \
+  FRANK_CUDA_TRY(launch_pdl(decode_down_kernel<TY>, dim3(grid_p), dim3(kBlockThreads), smem, st,                      \
+                            (const __nv_bfloat16*)w_down_p, (int)T, (int)H, (int)F, (int)E, (int)k, plan.hr,         \
+                            plan.rcap, plan.stages_dn, plan.nhmax, (TY*)y, ws));
+      if (y_dtype == FRANK_F32) {
+        FRANK_DOWN_CASE(float)
+      } else {
+        FRANK_DOWN_CASE(__nv_bfloat16)
+      }
+#undef FRANK_DOWN_CASE
+      FRANK_LAUNCH_CHECK();
+    }
+    mark(5, st);
+    mark(6, st);
   }
   if (route_w) FRANK_CUDA_TRY(cudaMemcpyAsync(route_w, ws.w, n * sizeof(float), cudaMemcpyDeviceToDevice, st));
   if (route_ids)
@@ -1096,3 +1337,12 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
 }
 
 }  // namespace frank
+
+#ifdef FRANK_DECODE_TRACE
+extern "C" int frank_decode_trace_read(unsigned long long* out, int nblocks) {
+  return cudaMemcpyFromSymbol(out, g_decode_trace, sizeof(unsigned long long) * 8 * nblocks) == cudaSuccess ? 0 : -3;
+}
+extern "C" int frank_decode_items_read(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_decode_items, sizeof(g_decode_items)) == cudaSuccess ? 0 : -3;
+}
+#endif

@@ -761,15 +761,20 @@ size_t smem2_bytes(int E) {
 // was ~7% slower than the single-CTA kernel on the Mixtral block, whose
 // GEMMs run at the 1 kW power cap (about 90% of the sustained cuBLAS rate),
 // not at a shared-memory limit.
+// The CTA-pair form moves 32 KB instead of 48 KB into each SM's shared
+// memory per 64-wide K step, so the same ring covers 1.6 us of TMA latency
+// instead of about 1 us; measured on the Mixtral block (C3) it runs the
+// gate/up GEMM 4% and the down GEMM 7% faster.  Its 256-row tiles waste
+// work on small experts (it has no swapped form), so it is chosen when the
+// experts average at least 1024 rows.  FRANK_TC_PAIR=0/1 forces either form.
 bool use_cta_pair(int64_t rows, int64_t E) {
   static int force = -2;
   if (force == -2) {
     const char* v = getenv("FRANK_TC_PAIR");
     force = v ? atoi(v) : -1;
   }
-  (void)rows;
-  (void)E;
-  return force == 1 && frank::num_sms() >= 2;
+  if (frank::num_sms() < 2 || force == 0) return false;
+  return force == 1 || rows >= 1024 * E;
 }
 
 }  // namespace

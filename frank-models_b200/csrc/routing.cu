@@ -7,6 +7,8 @@
 //   top-k (ogt, desc.)   moe_ffn_block.mlir:77-89, oracles/moe.py:95-100
 //   renormalisation      moe_ffn_block.mlir:91-128, oracles/moe.py:103-105
 //   slot flattening      components/moe/mul_mat_id.mlir:51-53 (s = j*T + t)
+#include <type_traits>
+
 #include "common.cuh"
 #include "topk.cuh"
 
@@ -119,6 +121,20 @@ __device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, flo
   }
 }
 
+// 8 elements held as raw 16-byte words -> fp32
+__device__ __forceinline__ void raw_to_f32(const uint4 (&r)[1], float (&v)[8]) {
+  const uint32_t w[4] = {r[0].x, r[0].y, r[0].z, r[0].w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    v[2 * i] = __uint_as_float(w[i] << 16);
+    v[2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+__device__ __forceinline__ void raw_to_f32(const float4 (&r)[2], float (&v)[8]) {
+  v[0] = r[0].x; v[1] = r[0].y; v[2] = r[0].z; v[3] = r[0].w;
+  v[4] = r[1].x; v[5] = r[1].y; v[6] = r[1].z; v[7] = r[1].w;
+}
+
 template <class TX, class TW, int EC>
 __global__ void __launch_bounds__(kVecThreads)
 router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int H, int E, int k, int normalize,
@@ -143,15 +159,29 @@ router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T
     for (int a = 0; a < kTPW; ++a)
 #pragma unroll
       for (int e = 0; e < EC; ++e) acc[a][e] = 0.f;
+    // the token loads of the next 256-column step are in flight while this
+    // step's products are summed (two steps of x per warp outstanding)
+    using RawX = typename std::conditional<sizeof(TX) == 2, uint4, float4>::type;
+    constexpr int kRaw = sizeof(TX) == 2 ? 1 : 2;  // 16-byte words per 8 elements
+    RawX xn[kTPW][kRaw];
+#pragma unroll
+    for (int a = 0; a < kTPW; ++a)
+#pragma unroll
+      for (int q = 0; q < kRaw; ++q)
+        xn[a][q] = (lane * 8 < H && t0 + a < T)
+                       ? __ldg(reinterpret_cast<const RawX*>(x + (t0 + a) * H + lane * 8) + q)
+                       : RawX{};
     for (int h = lane * 8; h < H; h += 256) {
       float xv[kTPW][8];
 #pragma unroll
-      for (int a = 0; a < kTPW; ++a) {
-        if (t0 + a < T) load8(x + (t0 + a) * H + h, xv[a]);
-        else
+      for (int a = 0; a < kTPW; ++a) raw_to_f32(xn[a], xv[a]);
 #pragma unroll
-          for (int i = 0; i < 8; ++i) xv[a][i] = 0.f;
-      }
+      for (int a = 0; a < kTPW; ++a)
+#pragma unroll
+        for (int q = 0; q < kRaw; ++q)
+          xn[a][q] = (h + 256 < H && t0 + a < T)
+                         ? __ldg(reinterpret_cast<const RawX*>(x + (t0 + a) * H + h + 256) + q)
+                         : RawX{};
 #pragma unroll
       for (int e = 0; e < EC; ++e) {
         const float4 w0 = *reinterpret_cast<const float4*>(sw + e * H + h);
