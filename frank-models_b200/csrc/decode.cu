@@ -104,7 +104,7 @@ struct DecodeWs {
   int32_t* active;      // experts with at least one row, ascending
   int32_t* nactive;
   int32_t* err;         // device error word (bounded waits)
-  unsigned* gbar;       // grid-barrier counter of the fused kernel (zeroed per call)
+  unsigned* gbar;       // [2] grid-barrier and exit counters of the fused kernel (zero between calls)
   const float* res;     // optional fp32 [T, H] residual added to y (may alias y)
   int n_slots;          // k * T
 };
@@ -1087,6 +1087,12 @@ decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   TRACE(5);
   down_body<TY>(w_down, T, H, F, E, k, hr, rcap, stages_dn, pre, ws, bid, nblk, ring,
                 reinterpret_cast<float*>(dsm_raw + lay.dsm_off), nhmax, red, full_dn, empty_dn, &s_abort, m, y);
+  // every block has passed the last barrier: the last one to leave zeroes
+  // both counters, so the workspace is ready for the next call
+  if (threadIdx.x == 0 && atomicAdd(ws.gbar + 1, 1u) == (unsigned)nblk - 1) {
+    ws.gbar[0] = 0;
+    ws.gbar[1] = 0;
+  }
   TRACE(7);
 }
 
@@ -1207,6 +1213,7 @@ bool decode_path_ok(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, int64
 size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t k) {
   Carve c(nullptr, 0);
   const int64_t n = k * T;
+  c.take<unsigned>(2);  // the workspace header: barrier counters (see frank_moe_ffn_block)
   c.take<float>(E * T);
   c.take<float>(n);
   c.take<int32_t>(n);
@@ -1217,7 +1224,6 @@ size_t decode_workspace_size(int64_t T, int64_t H, int64_t F, int64_t E, int64_t
   c.take<__nv_bfloat16>(n * F);
   c.take<int32_t>(E);
   c.take<int32_t>(1);
-  c.take<unsigned>(1);
   return align_up(c.used, 256);
 }
 
@@ -1238,6 +1244,9 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   const int64_t n = k * T;
   Carve c(workspace, ws_bytes);
   DecodeWs ws;
+  // the first 256 bytes of a block workspace: the fused kernel's barrier and
+  // exit counters, zero before the first call and left zero by every call
+  ws.gbar = c.take<unsigned>(2);
   ws.logits = c.take<float>(E * T);
   ws.w = c.take<float>(n);
   ws.ids = c.take<int32_t>(n);
@@ -1248,7 +1257,6 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
   ws.hs = c.take<__nv_bfloat16>(n * F);
   ws.active = c.take<int32_t>(E);
   ws.nactive = c.take<int32_t>(1);
-  ws.gbar = c.take<unsigned>(1);
   ws.res = residual;
   ws.n_slots = (int)n;
   ws.err = device_error_word();
@@ -1265,7 +1273,6 @@ int launch_decode_block(const void* x, int wr_dtype, const void* wr, const void*
     size_t smem = plan.lay.total;
     if (fused_routing_smem(T, E) > smem) smem = fused_routing_smem(T, E);
     mark(0, st);
-    FRANK_CUDA_TRY(cudaMemsetAsync(ws.gbar, 0, sizeof(unsigned), st));
     int st_launch;
     if (wr_dtype == FRANK_F32 && y_dtype == FRANK_F32)
       st_launch = launch_fused<float, float>(x, wr, w_gate_p, w_up_p, w_down_p, T, H, F, E, k, normalize, plan, y, ws,

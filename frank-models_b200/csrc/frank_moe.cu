@@ -154,6 +154,7 @@ static size_t moe_layout(int dtype, int64_t T, int64_t H, int64_t F, int64_t E, 
   const size_t esz = dtype == FRANK_F32 ? 4 : 2;
   Carve c(base, cap);
   MoeWs l;
+  c.take<char>(1);  // the workspace header (the decode kernel's counters; untouched here)
   l.w = c.take<float>(n);
   l.ids = c.take<int32_t>(n);
   l.sorted_slots = c.take<int32_t>(n);
@@ -427,11 +428,13 @@ int frank_moe_ffn_sublayer(int dtype, const float* residual, const float* norm_w
     return FRANK_ENOSPC;
   }
   cudaStream_t st = as_stream(stream);
-  const size_t xn_bytes = align_up((size_t)T * H * (dtype == FRANK_F32 ? 4 : 2), 256);
-  void* xn = workspace;
+  // the block's workspace first (its header stays at offset 0 for every T),
+  // the normalised tokens after it
+  const size_t blk_bytes = frank_moe_ffn_block_workspace_size(dtype, T, H, F, E, k);
+  void* xn = static_cast<char*>(workspace) + blk_bytes;
   FRANK_TRY(launch_rms_norm(residual, norm_w, T, H, eps, dtype, xn, st));
   return moe_block(dtype, xn, wr_dtype, wr, w_up_p, w_gate_p, w_down_p, T, E, k, H, F, normalize, FRANK_F32, out,
-                   route_w, route_ids, static_cast<char*>(workspace) + xn_bytes, ws_bytes - xn_bytes, st, residual);
+                   route_w, route_ids, workspace, blk_bytes, st, residual);
 }
 
 int frank_gather_rows(int dtype, const void* x, const int32_t* sorted_slots, int64_t rows, int64_t T, int64_t H,

@@ -14,6 +14,7 @@ import torch
 from . import _lib
 
 _DT = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}
+WORKSPACE_HEADER_BYTES = 256  # FRANK_WORKSPACE_HEADER_BYTES
 
 
 def _dt(t: torch.Tensor) -> int:
@@ -264,7 +265,10 @@ class MoEFFNBlock:
     def _workspace(self, T: int, device, need: int | None = None) -> torch.Tensor:
         need = self.workspace_bytes(T) if need is None else need
         if self._ws is None or self._ws.numel() < need or self._ws.device != device:
-            self._ws = torch.empty(max(need, 1), dtype=torch.uint8, device=device)
+            self._ws = torch.empty(max(need, WORKSPACE_HEADER_BYTES), dtype=torch.uint8, device=device)
+            # the header (the decode kernel's barrier counters) starts at zero;
+            # every call leaves it zero again
+            self._ws[:WORKSPACE_HEADER_BYTES].zero_()
         return self._ws
 
     def __call__(self, x: torch.Tensor, out: torch.Tensor | None = None, return_routing: bool = False):

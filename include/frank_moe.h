@@ -191,8 +191,16 @@ int frank_mul_mat_id(int dtype, const void* w_eoi, const void* input,
  * moe_ffn_block.mlir:45) or FRANK_BF16.
  * wr [E, H] is fp32 or bf16 (wr_dtype).  Packed weights:
  *   w_up_p, w_gate_p [E, F, H]; w_down_p [E, H, F]  (frank_prepack_experts)
+ * wr may also be a router pack (wr_dtype FRANK_ROUTER_PACKED).
  * Optional outputs (may be NULL): route_w [k,T] fp32, route_ids [k,T] int32.
+ * Workspace header: the first FRANK_WORKSPACE_HEADER_BYTES of the workspace
+ * hold the decode kernel's grid-barrier counters.  Zero them once before
+ * the first call with a workspace (cudaMemset); every call leaves them zero
+ * again (also one that gave up with FRANK_ETIMEOUT), so a workspace can be
+ * reused, resized from the same base or captured in a CUDA graph without a
+ * per-call reset.  Calls that share a workspace must not overlap.
  */
+#define FRANK_WORKSPACE_HEADER_BYTES 256
 size_t frank_moe_ffn_block_workspace_size(int dtype, int64_t T, int64_t H,
                                           int64_t F, int64_t E, int64_t k);
 int frank_moe_ffn_block(int dtype, const void* x, int wr_dtype, const void* wr,
@@ -221,7 +229,8 @@ int frank_rms_norm(const float* x, const float* weight, int64_t T, int64_t H,
  * norm_w: fp32 [H].  The normalised tokens are rounded to `dtype` (the block's
  * compute dtype) in the workspace; the residual add is fused into the block's
  * final sum over the k slots.  Other arguments as frank_moe_ffn_block.
- * Workspace: frank_moe_ffn_sublayer_workspace_size(dtype, T, H, F, E, k).
+ * Workspace: frank_moe_ffn_sublayer_workspace_size(dtype, T, H, F, E, k),
+ * with the same zeroed header as frank_moe_ffn_block's.
  */
 size_t frank_moe_ffn_sublayer_workspace_size(int dtype, int64_t T, int64_t H,
                                              int64_t F, int64_t E, int64_t k);

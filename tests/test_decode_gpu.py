@@ -86,3 +86,21 @@ def test_decode_repeated_calls_identical(monkeypatch):
     for _ in range(20):
         assert torch.equal(block(x), first)
     assert ops.read_device_error() == 0
+
+
+def test_decode_leaves_workspace_header_zero(monkeypatch):
+    """The fused kernel's grid-barrier counters live in the workspace header:
+    zeroed once at allocation, left zero by every call (no per-call reset),
+    also across a prefill-sized call that reuses the same workspace."""
+    cfg = configs.c5(2)
+    x, wr, wu, wg, wd = configs.block_inputs_torch(cfg, "cuda", seed=5)
+    block = ops.MoEFFNBlock(wr, wu, wg, wd, cfg.E, cfg.k, cfg.normalize)
+    monkeypatch.setenv("FRANK_DECODE_FUSED", "1")
+    first = block(x)
+    big = torch.randn(300, cfg.H, device="cuda").bfloat16()
+    block(big)  # tensor-core path on the same (grown) workspace
+    for _ in range(5):
+        assert torch.equal(block(x), first)
+    torch.cuda.synchronize()
+    assert int(block._ws[:ops.WORKSPACE_HEADER_BYTES].count_nonzero()) == 0
+    assert ops.read_device_error() == 0
