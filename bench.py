@@ -48,12 +48,13 @@ for _p in (REPO, REPO / "frank-models_b200"):
 METRIC = "moe_ffn_block tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMM launch.
-# Captured by ncu on the C3-shaped 2-expert case (558 MB read + 224 MB
-# written, profiles/tc_grouped_gemm_c3_profile_2experts.md); C3 runs the same
+# dram__bytes_read.sum + dram__bytes_write.sum of one gate/up GEMM launch
+# (the CTA-pair kernel, tc2_grouped_gemm_kernel<0>).  Captured by ncu on the
+# C3-shaped 2-expert case (626.7 MB read + 228.4 MB written,
+# profiles/tc_grouped_gemm_c3_profile_2experts.md); C3 runs the same
 # per-expert GEMM (4096 rows x 4096 x 2*14336) for 8 experts instead of 2, so
 # its traffic is that capture x 4.
-GATE_UP_TRAFFIC_BYTES = {"c3_mixtral_8x7b": 4 * (558.111e6 + 223.502e6)}
+GATE_UP_TRAFFIC_BYTES = {"c3_mixtral_8x7b": 4 * (626.727e6 + 228.440e6)}
 GATE_UP_TRAFFIC_SOURCE = {"c3_mixtral_8x7b": "ncu DRAM read + write of one gate/up launch on the C3-shaped "
                                              "2-expert case, x 4 (8 experts of the same GEMM shape)"}
 

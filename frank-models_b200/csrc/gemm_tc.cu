@@ -68,6 +68,7 @@ struct Params {
   const int32_t* row_rank;
   const int32_t* row_pos;
   float* peer_out[kMaxPeers];
+  int band_rows;           // rows per L2-resident band of activation rows
   int n_peers;             // entries of peer_out in use
   int64_t peer_rows;       // rows of every peer's return buffer
   int swap_small;          // experts with <= BM rows run as swapped (weight-row-major) tiles
@@ -155,7 +156,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // ------------------------------------------------------------- kernel --
-constexpr int kBandRows = 2048;
+// Activation rows of one band kept resident in L2 (a band's A rows are
+// read once while the CTAs sweep the weight tiles): about 64 MB.
+constexpr int64_t kBandBytes = 64ll << 20;
 
 // swapN != 0: a swapped tile.  The expert has at most BM rows, so the MMAs
 // run with the 128 weight rows of each B half as M and the expert's token
@@ -184,10 +187,11 @@ __device__ __forceinline__ Tile decode_tile(int t, const int* prefix, const Para
   const int mt = (r1 - r0 + bm - 1) / bm;
   const int nt = (prefix[e + 1] - prefix[e]) / mt;
   const int local = t - prefix[e];
-  // Bands of kBandRows rows (L2-resident: 2048 rows x K bf16 = 16 MiB at
-  // K = 4096); inside a band m runs fastest, so the CTAs running at the same
-  // time share both the band's activation rows and a few weight tiles.
-  const int G = kBandRows / bm;
+  // Bands of p.band_rows rows (L2-resident: band_rows x K bf16 <= 64 MB);
+  // inside a band m runs fastest, so the CTAs running at the same time share
+  // both the band's activation rows and a few weight tiles, and each weight
+  // tile is read from HBM once per band.
+  const int G = max(1, p.band_rows / bm);
   const int band = local / (G * nt);
   const int gm = min(G, mt - band * G);
   const int in = local - band * G * nt;
@@ -839,6 +843,14 @@ int launch_tc_grouped_gemm(int mode, const void* A, const void* B, const void* B
   p.row_pos = row_pos;
   for (int i = 0; i < kMaxPeers; ++i) p.peer_out[i] = (peer_out && i < n_peers) ? peer_out[i] : nullptr;
   p.n_peers = row_rank ? n_peers : 0;
+  {
+    // rows per band: a multiple of 256 (both tile heights) whose A rows fit
+    // the L2 budget, at most 8192 (gate/up at K = 4096: 8192 rows, one band
+    // per Mixtral expert; down at K = 14336: 2304 rows)
+    int64_t br = kBandBytes / (K * 2);
+    br = br / 256 * 256;
+    p.band_rows = (int)(br < 256 ? 256 : (br > 8192 ? 8192 : br));
+  }
   p.peer_rows = peer_rows;
   {
     const char* sw = getenv("FRANK_TC_SWAP");
