@@ -143,9 +143,29 @@ router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T
   __shared__ float lg[kVecThreads / 32][kTPW][EC];
   const int e0 = blockIdx.y * EC;
   const int ec = min(EC, E - e0);
-  for (int i = threadIdx.x; i < EC * H; i += kVecThreads) {
-    int e = i / H, h = i - e * H;
-    sw[i] = (e < ec) ? load_as_f32(wr, (int64_t)(e0 + e) * H + h) : 0.f;
+  // router rows -> shared memory, 8 elements per load, four loads in flight
+  // per thread before their stores (H % 8 == 0 on this path)
+  const int nv = EC * H / 8;
+  for (int i0 = threadIdx.x; i0 < nv; i0 += 4 * kVecThreads) {
+    float v[4][8];
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = i0 + q * kVecThreads;
+      const int e = i * 8 / H, h = i * 8 - e * H;
+      if (i < nv && e < ec) load8(wr + (int64_t)(e0 + e) * H + h, v[q]);
+      else
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[q][j] = 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int i = i0 + q * kVecThreads;
+      if (i < nv) {
+        float4* d = reinterpret_cast<float4*>(sw + (size_t)i * 8);
+        d[0] = make_float4(v[q][0], v[q][1], v[q][2], v[q][3]);
+        d[1] = make_float4(v[q][4], v[q][5], v[q][6], v[q][7]);
+      }
+    }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -501,7 +521,8 @@ int launch_router_topk(int x_dtype, const void* x, int wr_dtype, const void* wr,
   if (logits != nullptr && router_tc_ok(x_dtype, T, H, E) && (uintptr_t)x % 16 == 0)
     return launch_router_tc(x, wr_dtype, wr, wr3_pre, T, H, E, k, normalize, w, ids, logits, st);
   const size_t esz = x_dtype == FRANK_F32 ? 4 : 2;
-  const bool vec_ok = (H % 8 == 0) && ((uintptr_t)x % 16 == 0) && (H * 4 * 1 <= 160 * 1024) &&
+  const bool vec_ok = (H % 8 == 0) && ((uintptr_t)x % 16 == 0) && ((uintptr_t)wr % 16 == 0) &&
+                      (H * 4 * 1 <= 160 * 1024) &&
                       (E <= 8 || logits != nullptr) && (H * esz) % 16 == 0;
   if (!vec_ok) return launch_router_legacy(x_dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, st);
   if (x_dtype == FRANK_F32 && wr_dtype == FRANK_F32)
