@@ -35,6 +35,19 @@ struct PeerRows {
 __global__ void ep_plan_kernel(const int32_t* __restrict__ C, int P, int El, int me, int32_t* __restrict__ dst_base,
                                int32_t* __restrict__ local_off, int64_t capacity, int32_t* __restrict__ err) {
   const int E = P * El;
+  // a negative entry is not a count: then nothing is placed or computed
+  __shared__ int s_bad;
+  if (threadIdx.x == 0) s_bad = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < P * E; i += blockDim.x)
+    if (C[i] < 0) s_bad = 1;
+  __syncthreads();
+  if (s_bad) {
+    if (threadIdx.x == 0) atomicExch(err, FRANK_EINVAL);
+    for (int g = threadIdx.x; g < E; g += blockDim.x) dst_base[g] = (int32_t)capacity;  // refused by the dispatch
+    for (int e = threadIdx.x; e <= El; e += blockDim.x) local_off[e] = 0;              // no rows for the GEMMs
+    return;
+  }
   for (int g = threadIdx.x; g < E; g += blockDim.x) {
     const int p = g / El, e = g - p * El;
     int32_t base = 0;
@@ -76,6 +89,7 @@ __global__ void ep_return_map_kernel(const int32_t* __restrict__ C, int P, int E
     s_len = C[q * E + g];
   }
   __syncthreads();
+  if (s_start < 0 || s_len < 0) return;  // counts are never negative; refused by ep_plan_kernel
   for (int i = threadIdx.x; i < s_len && (int64_t)s_start + i < capacity; i += blockDim.x) {
     row_rank[s_start + i] = q;
     row_pos[s_start + i] = s_src + i;

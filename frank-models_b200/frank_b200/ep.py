@@ -293,7 +293,6 @@ class ExpertParallelMoE:
         import ctypes
 
         arr = lambda vals: (ctypes.c_void_p * self.P)(*vals)  # noqa: E731
-        counts = S["counts"] if S else torch.empty((self.P, self.E), dtype=torch.int32, device=dev)
         self._symm = {
             "T": T, "buf": buf, "hdl": hdl, "cap": cap, "ret_rows": n,
             "recv_x": buf[base[0]:base[0] + cap * H * 2].view(torch.bfloat16).view(cap, H),
@@ -306,7 +305,7 @@ class ExpertParallelMoE:
             "local_off": torch.empty(self.El + 1, dtype=torch.int32, device=dev),
             "row_rank": torch.empty(cap, dtype=torch.int32, device=dev),
             "row_pos": torch.empty(cap, dtype=torch.int32, device=dev),
-            "counts": counts,
+            "counts": self._counts,  # this step's gathered counts (allocated once, kept across growth)
             "flag": torch.zeros(1, dtype=torch.int32, device=dev),
             "hs": torch.empty(cap * self.F * 2 + 256, dtype=torch.uint8, device=dev),
         }
@@ -333,7 +332,7 @@ class ExpertParallelMoE:
         dev = x.device
         lib = _lib.load()
         st = torch.cuda.current_stream().cuda_stream
-        if self._symm is None:
+        if getattr(self, "_counts", None) is None or self._counts.device != dev:
             self._counts = torch.empty((self.P, self.E), dtype=torch.int32, device=dev)
         if self.profile:
             self._marks.append([])
@@ -344,11 +343,16 @@ class ExpertParallelMoE:
         sorted_slots, offsets, slot_pos, _ = ops.permute(ids, self.E)
         cnt = (offsets[1:] - offsets[:-1]).contiguous()
         self._mark()
-        counts = self._symm["counts"] if self._symm is not None else self._counts
+        counts = self._counts
         self._comm(dist.all_gather_into_tensor, counts, cnt, group=self.group)
         # the one host read per step: the buffers are sized from the counts
         # every rank now holds, so no rank can plan past a receive buffer
         t_max, rows_max = self.step_sizes(counts.cpu().numpy())
+        if t_max < T:
+            from ._lib import ENCCL, FrankError
+
+            raise FrankError(ENCCL, f"expert-parallel step on rank {self.rank}: gathered counts cover {t_max} "
+                                    f"tokens per rank, this rank holds {T}")
         S = self._symmetric(t_max, rows_max, dev)
         _lib.check(lib.frank_ep_plan(S["counts"].data_ptr(), self.P, self.El, self.rank, S["dst_base"].data_ptr(),
                                      S["local_off"].data_ptr(), S["row_rank"].data_ptr(), S["row_pos"].data_ptr(),
