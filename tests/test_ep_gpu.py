@@ -84,3 +84,23 @@ def test_ep_equals_single_gpu(cfg_name, mode, ragged):
     for rank, equal, det, err, dev_err in sorted(q.get(timeout=10) for _ in range(world)):
         assert equal, f"rank {rank}: max |ep - single| = {err}"
         assert det and dev_err == 0
+
+
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+def test_ep_single_rank(mode):
+    """The expert-parallel step with one rank (all experts local, the
+    exchange going through this GPU's own symmetric buffers): bit-identical
+    to the single-GPU block, two calls with a growing batch."""
+    from frank_b200 import configs
+
+    cfg = configs.BlockConfig("bf16_fg_ep1", T=700, H=1024, F=512, E=32, k=4, normalize=True, dtype="bf16",
+                              zipf=1.2)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_worker, args=(0, 1, _free_port(), cfg, mode, True, q))
+    p.start()
+    p.join(timeout=300)
+    assert p.exitcode == 0
+    rank, equal, det, err, dev_err = q.get(timeout=10)
+    assert equal, f"max |ep - single| = {err}"
+    assert det and dev_err == 0
