@@ -576,19 +576,21 @@ __device__ __forceinline__ void mma_16816(float (&c)[4], uint32_t a0, uint32_t a
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
-// This warp's share of A [16 x K] (row i at a + i * ars) times the token
-// rows B^T [nb x K] (row n at b + n * brs, n < nb <= 8; columns n >= nb
-// repeat row nb - 1 and are ignored), written to red[warp] as a [16][8]
-// tile.  K % 16 == 0.
-__device__ __forceinline__ void warp_tile_mma(const uint8_t* a, uint32_t ars, const uint8_t* b, uint32_t brs, int K,
-                                              int nb, float* red) {
+// This warp's share of A [16 x K] times the token rows B^T [nb x K] (row n
+// at b + n * brs, n < nb <= 8), written to red[warp] as a [16][8] tile.
+// A's rows 0..7 are the rows i < nlo at lo + i * ars, its rows 8..15 the
+// rows i - 8 < nhi at hi + (i - 8) * ars; rows beyond nlo / nhi, like token
+// columns beyond nb, repeat the last row and their outputs are ignored (so
+// a stage only holds the rows it uses).  K % 16 == 0.
+__device__ __forceinline__ void warp_tile_mma(const uint8_t* lo, int nlo, const uint8_t* hi, int nhi, uint32_t ars,
+                                              const uint8_t* b, uint32_t brs, int K, int nb, float* red) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t = lane & 3;
   const int full = K / 32;
   const int units = full + ((K & 31) ? 1 : 0);
   const int u0 = units * warp / kWarps, u1 = units * (warp + 1) / kWarps;
-  const uint8_t* ap0 = a + (size_t)g * ars;
-  const uint8_t* ap1 = a + (size_t)(g + 8) * ars;
+  const uint8_t* ap0 = lo + (size_t)min(g, max(nlo - 1, 0)) * ars;
+  const uint8_t* ap1 = hi + (size_t)min(g, max(nhi - 1, 0)) * ars;
   const uint8_t* bp = b + (size_t)min(g, nb - 1) * brs;
   // four independent accumulators, each group's loads issued before its MMAs
   float acc[4][4];
@@ -644,8 +646,8 @@ __device__ __forceinline__ float red_sum(const float* red, int i, int n) {
 // split evenly over the blocks -- block b takes the flat pairs
 // [b R / nblk, (b+1) R / nblk), R = nact * F -- and a block walks its range in
 // items of at most fr <= 8 consecutive rows of one expert (an item ends at an
-// expert boundary).  Stage = 16 weight rows (the item's gate rows at 0..7,
-// its up rows at 8..15, one bulk copy each) and the expert's token rows.
+// expert boundary).  Stage = the item's gate rows, then its up rows (one
+// bulk copy each, fr rows reserved for each) and the expert's token rows.
 // One 16 x 8 tile gives gate . x and up . x of every (row, token):
 // h = gate . x * silu(up . x).
 struct GuCursor {
@@ -666,8 +668,8 @@ __device__ __forceinline__ GuCursor gu_range(int nact, int F, int fr, int bid, i
   return GuCursor{R * bid / nblk, R * (bid + 1) / nblk, F, fr};
 }
 
-__device__ __host__ inline uint32_t gu_stage_bytes(int H, int rcap) {
-  return (uint32_t)kMT * H * 2 + (uint32_t)rcap * tok_stride(H);
+__device__ __host__ inline uint32_t gu_stage_bytes(int H, int fr, int rcap) {
+  return (uint32_t)(2 * fr) * H * 2 + (uint32_t)rcap * tok_stride(H);
 }
 
 __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w_gate,
@@ -681,7 +683,7 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t xrow = (uint32_t)H * 2;  // weight row stride
   const uint32_t ts = tok_stride(H);      // token row stride
-  const uint32_t stage_bytes = gu_stage_bytes(H, rcap);
+  const uint32_t stage_bytes = gu_stage_bytes(H, fr, rcap);
   uint8_t* stage_base = dsm_raw;
   const int nact = *m.nact;
   if (warp == kWarps) {
@@ -702,9 +704,9 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
         const int rc = min(rcap, sm_off[e + 1] - r0);
         mbar_expect_tx(bar, (uint32_t)(2 * rows + rc) * xrow);
         bulk_load(dst, w_gate + ((int64_t)e * F + f0) * H, (uint32_t)rows * xrow, bar);
-        bulk_load(dst + 8 * xrow, w_up + ((int64_t)e * F + f0) * H, (uint32_t)rows * xrow, bar);
+        bulk_load(dst + fr * xrow, w_up + ((int64_t)e * F + f0) * H, (uint32_t)rows * xrow, bar);
         for (int r = 0; r < rc; ++r)
-          bulk_load(dst + kMT * xrow + r * ts, x + (int64_t)sm_tok[r0 + r] * H, xrow, bar);
+          bulk_load(dst + 2 * fr * xrow + r * ts, x + (int64_t)sm_tok[r0 + r] * H, xrow, bar);
       }
     }
     return;
@@ -717,7 +719,7 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
     if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, s_abort, ws.err)) break;
     if (threadIdx.x == 0) TRACE_ITEM(0, j, 0);
     uint8_t* st = stage_base + (size_t)s * stage_bytes;
-    uint8_t* tok = st + kMT * xrow;
+    uint8_t* tok = st + 2 * fr * xrow;
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += rcap) {
       const int rc = min(rcap, cnt - c0);
@@ -732,7 +734,7 @@ __device__ __forceinline__ void gateup_body(const __nv_bfloat16* __restrict__ x,
       }
       // partial tiles alternate between two buffers: one barrier per tile
       float* rb = red + (tile++ & 1) * (kWarps * kMT * 8);
-      warp_tile_mma(st, xrow, tok, ts, H, rc, rb);
+      warp_tile_mma(st, rows, st + fr * xrow, rows, xrow, tok, ts, H, rc, rb);
       if (c0 + rcap >= cnt) {
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
@@ -809,8 +811,8 @@ __device__ __forceinline__ DnCursor dn_range(int nact, int H, int hr, int bid, i
   return DnCursor{0, nact > 0 ? bid % nact : 0, hb0, nact, hb0, hb1, hr};
 }
 
-__device__ __host__ inline uint32_t dn_stage_bytes(int F, int rcap) {
-  return (uint32_t)kMT * F * 2 + (uint32_t)rcap * tok_stride(F);
+__device__ __host__ inline uint32_t dn_stage_bytes(int F, int hr, int rcap) {
+  return (uint32_t)hr * F * 2 + (uint32_t)rcap * tok_stride(F);
 }
 
 // The down ring: its first nb stages lie beside the gate/up ring (so they
@@ -861,7 +863,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t hrow = (uint32_t)F * 2;  // weight row stride
   const uint32_t ts = tok_stride(F);      // h row stride
-  const uint32_t stage_bytes = dn_stage_bytes(F, rcap);
+  const uint32_t stage_bytes = dn_stage_bytes(F, hr, rcap);
   const int nact = *m.nact;
   if (warp == kWarps) {
     // producer warp: refills a stage as soon as all compute warps released it
@@ -886,7 +888,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
           mbar_expect_tx(bar, (uint32_t)(rows + rc) * hrow);
           issue_down_rows(w_down, e, H, F, h0, rows, dst, bar);
         }
-        for (int r = 0; r < rc; ++r) bulk_load(dst + kMT * hrow + r * ts, ws.hs + (int64_t)(r0 + r) * F, hrow, bar);
+        for (int r = 0; r < rc; ++r) bulk_load(dst + hr * hrow + r * ts, ws.hs + (int64_t)(r0 + r) * F, hrow, bar);
       }
     }
     return;
@@ -900,7 +902,7 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
     if (!mbar_wait(smem_u32(&full[s]), (uint32_t)(j / stages) & 1u, s_abort, ws.err)) break;
     if (threadIdx.x == 0) TRACE_ITEM(1, j, 0);
     uint8_t* st = ring.stage(s);
-    uint8_t* hsm = st + kMT * hrow;
+    uint8_t* hsm = st + hr * hrow;
     const int r0 = sm_off[e], cnt = sm_off[e + 1] - r0;
     for (int c0 = 0; c0 < cnt; c0 += rcap) {
       const int rc = min(rcap, cnt - c0);
@@ -914,7 +916,9 @@ __device__ __forceinline__ void down_body(const __nv_bfloat16* __restrict__ w_do
         consumer_sync();
       }
       float* rb = red + (tile++ & 1) * (kWarps * kMT * 8);
-      warp_tile_mma(st, hrow, hsm, ts, F, rc, rb);
+      // rows 8..15 of the tile: the item's rows past 8, or (none) its own rows again
+      warp_tile_mma(st, min(rows, 8), rows > 8 ? st + 8 * hrow : st, rows > 8 ? rows - 8 : rows, hrow, hsm, ts, F,
+                    rc, rb);
       if (c0 + rcap >= cnt) {
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&empty[s]));  // this warp is done with stage s
@@ -962,8 +966,8 @@ decode_down_kernel(const __nv_bfloat16* __restrict__ w_down, int T, int H, int F
   __shared__ int32_t m_off[kMaxE + 1], m_act[kMaxE], m_nact, m_tok[kMaxSlots], m_pos[kMaxSlots];
   __shared__ float m_w[kMaxSlots];
   const Meta m = load_meta(ws, T, E, m_off, m_act, &m_nact, m_tok, m_w, m_pos);
-  const DnRing ring{dsm_raw, dsm_raw, 0, dn_stage_bytes(F, rcap)};
-  float* dsm = reinterpret_cast<float*>(dsm_raw + (((size_t)stages * dn_stage_bytes(F, rcap) + 127) & ~(size_t)127));
+  const DnRing ring{dsm_raw, dsm_raw, 0, dn_stage_bytes(F, hr, rcap)};
+  float* dsm = reinterpret_cast<float*>(dsm_raw + (((size_t)stages * dn_stage_bytes(F, hr, rcap) + 127) & ~(size_t)127));
   down_body<TY>(w_down, T, H, F, E, k, hr, rcap, stages, 0, ws, blockIdx.x, gridDim.x, ring, dsm, nhmax, red,
                 full, empty, &s_abort, m, y);
 }
@@ -1079,7 +1083,7 @@ decode_fused_kernel(const __nv_bfloat16* __restrict__ x, const TW* __restrict__ 
   gateup_body(x, w_gate, w_up, T, H, F, E, fr, rcap, stages_gu, ws, bid, nblk, dsm_raw, red, full_gu, empty_gu,
               &s_abort, m);
   TRACE(4);
-  const DnRing ring{dsm_raw + lay.dn_off, dsm_raw, lay.dn_beside, dn_stage_bytes(F, rcap)};
+  const DnRing ring{dsm_raw + lay.dn_off, dsm_raw, lay.dn_beside, dn_stage_bytes(F, hr, rcap)};
   int pre = 0;
   if (lay.prefetch && threadIdx.x == kThreads)  // the producer lane, done issuing its gate/up copies
     pre = down_prefetch(w_down, H, F, hr, bid, nblk, ring, full_dn, m);
@@ -1137,10 +1141,16 @@ DecodePlan decode_plan(int64_t T, int64_t H, int64_t F, int64_t k, int nblk) {
   if (const char* v = getenv("FRANK_DECODE_FR")) fr_env = atoi(v);
   if (const char* v = getenv("FRANK_DECODE_GU_STAGES")) gu_env = atoi(v);
   const size_t budget = kSmemDyn > p.dsm_bytes ? kSmemDyn - p.dsm_bytes : 0;
-  p.fr = fr_env > 0 && fr_env < 8 ? fr_env : 8;
+  // rows per gate/up item: 8 (one 16-row tile of gate + up rows) unless two
+  // stages of that do not fit; rows per down item: the block's output rows,
+  // at most 16 and at most what keeps two stages within the budget
+  p.fr = 8;
+  while (p.fr > 1 && 2 * (size_t)gu_stage_bytes((int)H, p.fr, p.rcap) > budget) p.fr /= 2;
+  if (fr_env > 0 && fr_env < p.fr) p.fr = fr_env;
   p.hr = p.nhmax < kMT ? p.nhmax : kMT;
-  p.stage_gu = gu_stage_bytes((int)H, p.rcap);
-  p.stage_dn = dn_stage_bytes((int)F, p.rcap);
+  while (p.hr > 1 && 2 * (size_t)dn_stage_bytes((int)F, p.hr, p.rcap) > budget) p.hr = (p.hr + 1) / 2;
+  p.stage_gu = gu_stage_bytes((int)H, p.fr, p.rcap);
+  p.stage_dn = dn_stage_bytes((int)F, p.hr, p.rcap);
   p.stages_gu = (int)(budget / p.stage_gu);
   // about 128 KB in flight per SM covers the loaded HBM latency
   auto depth = [](size_t stage) {
