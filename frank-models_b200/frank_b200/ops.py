@@ -499,6 +499,43 @@ class GraphedMoEFFN:
         return self.y
 
 
+class GraphedHostMoEFFN:
+    """A decode step from host memory to host memory as ONE CUDA graph: the
+    copy of the tokens from the pinned host buffer ``x_host`` [T, H], the
+    block and the copy of the result into the pinned host buffer ``y_host``
+    [T, H] are captured together, so a step is a single graph launch.
+    Write the tokens into ``x_host``, call :meth:`replay` (returns an event
+    that completes when ``y_host`` holds the result), read ``y_host`` after
+    the event.  ``x_host`` must not be modified before the event of the
+    previous replay that reads it has completed."""
+
+    def __init__(self, block: "MoEFFNBlock", T: int, device=None):
+        device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.block = block
+        self.x_host = torch.zeros((T, block.H), dtype=block.dtype).pin_memory()
+        self.y_host = torch.zeros((T, block.H), dtype=block.out_dtype).pin_memory()
+        self.x = torch.zeros((T, block.H), dtype=block.dtype, device=device)
+        self.y = torch.empty((T, block.H), dtype=block.out_dtype, device=device)
+        block._workspace(T, device)
+        side = torch.cuda.Stream(device=device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            block(self.x, out=self.y)  # warm-up outside capture (attributes, tensor maps)
+        torch.cuda.current_stream(device).wait_stream(side)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph, stream=side):
+            self.x.copy_(self.x_host, non_blocking=True)
+            block(self.x, out=self.y)
+            self.y_host.copy_(self.y, non_blocking=True)
+        torch.cuda.current_stream(device).wait_stream(side)
+
+    def replay(self) -> torch.cuda.Event:
+        self.graph.replay()
+        done = torch.cuda.Event()
+        done.record()
+        return done
+
+
 def read_device_error() -> int:
     """Return and clear the device error word of bounded in-kernel waits."""
     import ctypes

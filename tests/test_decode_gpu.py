@@ -104,3 +104,19 @@ def test_decode_leaves_workspace_header_zero(monkeypatch):
     torch.cuda.synchronize()
     assert int(block._ws[:ops.WORKSPACE_HEADER_BYTES].count_nonzero()) == 0
     assert ops.read_device_error() == 0
+
+
+def test_graphed_host_step_equals_device_call():
+    """ops.GraphedHostMoEFFN: host tokens in, block, host result out as one
+    graph launch; bit-identical to a device call, across replays with new
+    tokens."""
+    cfg = configs.c5(4)
+    x, wr, wu, wg, wd = configs.block_inputs_torch(cfg, "cuda", seed=8)
+    block = ops.MoEFFNBlock(wr, wu, wg, wd, cfg.E, cfg.k, cfg.normalize)
+    g = ops.GraphedHostMoEFFN(block, cfg.T)
+    for seed in (1, 2, 3):
+        xs = torch.randn(cfg.T, cfg.H, generator=torch.Generator().manual_seed(seed)).bfloat16()
+        g.x_host.copy_(xs)
+        g.replay().synchronize()
+        assert torch.equal(g.y_host, block(xs.cuda()).cpu())
+    assert ops.read_device_error() == 0
