@@ -145,14 +145,14 @@ __global__ void ep_dispatch_kernel(const uint4* __restrict__ x, int64_t T, int64
 extern "C" {
 
 int frank_ep_plan(const int32_t* counts_all, int P, int El, int rank, int32_t* dst_base, int32_t* local_offsets,
-                  int32_t* row_rank, int32_t* row_pos, int64_t capacity, void* stream) {
+                  int32_t* row_rank, int32_t* row_pos, int64_t capacity, int32_t* overflow, void* stream) {
   if (P < 1 || P > kMaxPeers || El < 1 || rank < 0 || rank >= P || P * El > 1024) {
     frank::set_error("ep_plan: P=%d El=%d rank=%d out of range (P <= %d, P*El <= 1024)", P, El, rank, kMaxPeers);
     return FRANK_EINVAL;
   }
   cudaStream_t st = frank::as_stream(stream);
   ep_plan_kernel<<<1, 1024, 0, st>>>(counts_all, P, El, rank, dst_base, local_offsets, capacity,
-                                     frank::device_error_word());
+                                     overflow ? overflow : frank::device_error_word());
   FRANK_LAUNCH_CHECK();
   ep_return_map_kernel<<<P * El, 256, 0, st>>>(counts_all, P, El, rank, local_offsets, row_rank, row_pos,
                                                   capacity);
@@ -162,7 +162,8 @@ int frank_ep_plan(const int32_t* counts_all, int P, int El, int rank, int32_t* d
 
 int frank_ep_dispatch(const void* x, int64_t T, int64_t H, const float* w, const int32_t* sorted_slots,
                       const int32_t* offsets, int64_t E, int64_t El, int64_t n_slots, const int32_t* dst_base,
-                      void* const* peer_x, float* const* peer_w, int P, int64_t capacity, void* stream) {
+                      void* const* peer_x, float* const* peer_w, int P, int64_t capacity, int32_t* overflow,
+                      void* stream) {
   if (P < 1 || P > kMaxPeers || El < 1 || E != El * P) {
     frank::set_error("ep_dispatch: P=%d El=%lld E=%lld inconsistent", P, (long long)El, (long long)E);
     return FRANK_EINVAL;
@@ -185,7 +186,7 @@ int frank_ep_dispatch(const void* x, int64_t T, int64_t H, const float* w, const
   const int64_t cap = (int64_t)frank::num_sms() * 8;
   ep_dispatch_kernel<<<(unsigned)(blocks < cap ? blocks : cap), 256, 0, frank::as_stream(stream)>>>(
       (const uint4*)x, T, H * 2 / 16, w, sorted_slots, offsets, (int)E, (int)El, n_slots, dst_base, capacity,
-      frank::device_error_word(), peers);
+      overflow ? overflow : frank::device_error_word(), peers);
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
 }

@@ -65,9 +65,9 @@ SIGNATURES = {
                                   _c_vp, _c_vp, _c_size, _c_vp]),
     "frank_combine": (_c_int, [_c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
     "frank_copy_row_segments": (_c_int, [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp]),
-    "frank_ep_plan": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp]),
+    "frank_ep_plan": (_c_int, [_c_vp, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_vp, _c_vp]),
     "frank_ep_dispatch": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp,
-                                   _c_vp, _c_int, _c_i64, _c_vp]),
+                                   _c_vp, _c_int, _c_i64, _c_vp, _c_vp]),
     "frank_expert_ffn_scatter": (_c_int, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp,
                                           _c_vp, _c_vp, _c_vp, _c_int, _c_i64, _c_vp, _c_size, _c_vp]),
     "frank_read_device_error": (_c_int, [_c_vp, _c_vp]),

@@ -204,7 +204,7 @@ class ExpertParallelMoE:
                 self._comm(req.wait)
 
     # phase boundaries (nccl mode / p2p mode):
-    #   route+permute(+gather) | counts (+plan) | dispatch (+barrier) | expert GEMMs
+    #   route+permute(+gather) | counts (nccl: +plan) | dispatch (p2p: plan + dispatch + host size check, +barrier) | expert GEMMs
     #   | return (p2p: barrier only, the rows went back from the GEMM epilogue) | combine
     PHASES = ("route_permute", "counts_plan", "dispatch", "expert_ffn", "return", "combine")
 
@@ -307,6 +307,7 @@ class ExpertParallelMoE:
             "row_pos": torch.empty(cap, dtype=torch.int32, device=dev),
             "counts": self._counts,  # this step's gathered counts (allocated once, kept across growth)
             "flag": torch.zeros(1, dtype=torch.int32, device=dev),
+            "spec_flag": torch.zeros(1, dtype=torch.int32, device=dev),  # refusals of a plan on too small buffers
             "hs": torch.empty(cap * self.F * 2 + 256, dtype=torch.uint8, device=dev),
         }
         return self._symm
@@ -319,6 +320,19 @@ class ExpertParallelMoE:
         t_max = int(counts.sum(axis=1).max()) // self.k
         per_rank = counts.sum(axis=0).reshape(self.P, self.El).sum(axis=1)
         return t_max, int(per_rank.max())
+
+    def _check_tokens(self, t_max: int, T: int):
+        if t_max < T:
+            from ._lib import ENCCL, FrankError
+
+            raise FrankError(ENCCL, f"expert-parallel step on rank {self.rank}: gathered counts cover {t_max} "
+                                    f"tokens per rank, this rank holds {T}")
+
+    def _side_stream(self, dev):
+        if getattr(self, "_side", None) is None:
+            self._side = torch.cuda.Stream(device=dev)
+            self._counts_host = torch.empty((self.P, self.E), dtype=torch.int32).pin_memory()
+        return self._side
 
     def _barrier(self, flag):
         # stream-ordered: every rank's preceding kernels (and their stores into
@@ -345,22 +359,48 @@ class ExpertParallelMoE:
         self._mark()
         counts = self._counts
         self._comm(dist.all_gather_into_tensor, counts, cnt, group=self.group)
-        # the one host read per step: the buffers are sized from the counts
-        # every rank now holds, so no rank can plan past a receive buffer
-        t_max, rows_max = self.step_sizes(counts.cpu().numpy())
-        if t_max < T:
-            from ._lib import ENCCL, FrankError
 
-            raise FrankError(ENCCL, f"expert-parallel step on rank {self.rank}: gathered counts cover {t_max} "
-                                    f"tokens per rank, this rank holds {T}")
-        S = self._symmetric(t_max, rows_max, dev)
-        _lib.check(lib.frank_ep_plan(S["counts"].data_ptr(), self.P, self.El, self.rank, S["dst_base"].data_ptr(),
-                                     S["local_off"].data_ptr(), S["row_rank"].data_ptr(), S["row_pos"].data_ptr(),
-                                     S["cap"], st))
+        def plan_and_dispatch(S, overflow):
+            _lib.check(lib.frank_ep_plan(S["counts"].data_ptr(), self.P, self.El, self.rank, S["dst_base"].data_ptr(),
+                                         S["local_off"].data_ptr(), S["row_rank"].data_ptr(),
+                                         S["row_pos"].data_ptr(), S["cap"], overflow, st))
+            _lib.check(lib.frank_ep_dispatch(x.data_ptr(), T, H, w.data_ptr(), sorted_slots.data_ptr(),
+                                             offsets.data_ptr(), self.E, self.El, self.k * T,
+                                             S["dst_base"].data_ptr(), S["peer_x"], S["peer_w"], self.P, S["cap"],
+                                             overflow, st))
+
+        # The buffers must hold this step's rows, which only the gathered
+        # counts tell.  From the second step on, the counts are copied to the
+        # host on a side stream while the plan and the dispatch already run
+        # with the current buffers (rows past a buffer are refused into a
+        # scratch word); the host then checks the sizes.  Every rank sees the
+        # same counts, so if they do not fit, all ranks wait for the refused
+        # dispatch, grow their buffers together and redo plan and dispatch.
         self._mark()
-        _lib.check(lib.frank_ep_dispatch(x.data_ptr(), T, H, w.data_ptr(), sorted_slots.data_ptr(),
-                                         offsets.data_ptr(), self.E, self.El, self.k * T, S["dst_base"].data_ptr(),
-                                         S["peer_x"], S["peer_w"], self.P, S["cap"], st))
+        S = self._symm
+        if S is None:
+            t_max, rows_max = self.step_sizes(counts.cpu().numpy())
+            self._check_tokens(t_max, T)
+            S = self._symmetric(t_max, rows_max, dev)
+            plan_and_dispatch(S, None)
+        else:
+            gathered = torch.cuda.Event()
+            gathered.record()
+            side = self._side_stream(dev)
+            side.wait_event(gathered)
+            with torch.cuda.stream(side):
+                self._counts_host.copy_(counts, non_blocking=True)
+                copied = torch.cuda.Event()
+                copied.record(side)
+            plan_and_dispatch(S, S["spec_flag"].data_ptr())
+            copied.synchronize()
+            t_max, rows_max = self.step_sizes(self._counts_host.numpy())
+            self._check_tokens(t_max, T)
+            if S["T"] < t_max or S["cap"] < rows_max:
+                torch.cuda.synchronize()
+                self._comm(dist.barrier, group=self.group)  # every rank's refused dispatch has finished
+                S = self._symmetric(t_max, rows_max, dev)
+                plan_and_dispatch(S, None)
         self._barrier(S["flag"])
         self._mark()
         _lib.check(lib.frank_expert_ffn_scatter(

@@ -294,8 +294,11 @@ int frank_copy_row_segments(const void* src, void* dst,
  *   bf16 token row x[sorted_slots[r] % T] and gate weight w[sorted_slots[r]]
  *   into peer_x[p] / peer_w[p] (device addresses of every rank's receive
  *   buffers of `capacity` rows, P <= 8) at the planned rows.  A planned row
- *   outside [0, capacity) is skipped and FRANK_EINVAL is recorded in the
- *   device error word (frank_read_device_error).
+ *   outside [0, capacity) is skipped and FRANK_EINVAL is recorded in
+ *   *overflow, or in the device error word (frank_read_device_error) when
+ *   overflow is NULL.  A caller that plans with receive buffers sized from
+ *   an earlier step and checks this step's counts on the host afterwards
+ *   (redoing the step when they did not fit) passes its own overflow word.
  * frank_expert_ffn_scatter: frank_expert_ffn (bf16) whose fp32 output row r
  *   is stored at peer_out[row_rank[r]] + row_pos[r] * H, i.e. straight into
  *   the return buffer of the rank the row came from.  Every return buffer
@@ -303,20 +306,22 @@ int frank_copy_row_segments(const void* src, void* dst,
  *   is not stored and records FRANK_EINVAL in the device error word.
  * frank_ep_plan clamps the local expert offsets to `capacity`, so rows
  *   beyond the receive buffer are never read by the GEMMs either (and
- *   FRANK_EINVAL is recorded when the gathered counts exceed it).
+ *   FRANK_EINVAL is recorded, in *overflow if given, when the gathered
+ *   counts exceed it).
  * Stores to other GPUs complete with the kernels; the caller orders the
  *   ranks' steps (e.g. an NCCL collective on the same stream) before a rank
  *   reads what its peers wrote.  No kernel here waits on another GPU.
  */
 int frank_ep_plan(const int32_t* counts_all, int P, int El, int rank,
                   int32_t* dst_base, int32_t* local_offsets, int32_t* row_rank,
-                  int32_t* row_pos, int64_t capacity, void* stream);
+                  int32_t* row_pos, int64_t capacity, int32_t* overflow,
+                  void* stream);
 int frank_ep_dispatch(const void* x, int64_t T, int64_t H, const float* w,
                       const int32_t* sorted_slots, const int32_t* offsets,
                       int64_t E, int64_t El, int64_t n_slots,
                       const int32_t* dst_base, void* const* peer_x,
                       float* const* peer_w, int P, int64_t capacity,
-                      void* stream);
+                      int32_t* overflow, void* stream);
 int frank_expert_ffn_scatter(const void* xs, const float* w_rows,
                              const int32_t* offsets, int64_t E, int64_t rows,
                              int64_t H, int64_t F, const void* w_up_p,

@@ -34,8 +34,8 @@ def _worker(rank, world, port, cfg, mode, ragged, q):
 
         wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, dev, seed=0)
         x = configs.block_x_torch(cfg, dev, seed=10 + rank)
-        if ragged:  # rank r holds T - 37 r tokens
-            x = x[:cfg.T - 37 * rank].contiguous()
+        if ragged:  # rank r holds T - 37 r tokens (one rank: T / 2, so the next call must grow the buffers)
+            x = x[:(cfg.T // 2 if world == 1 else cfg.T - 37 * rank)].contiguous()
         El = cfg.E // world
         sl = slice(rank * El, (rank + 1) * El)
         moe = ep.ExpertParallelMoE(wr, wu[sl].contiguous(), wg[sl].contiguous(), wd[sl].contiguous(), cfg.E, cfg.k,
@@ -90,7 +90,9 @@ def test_ep_equals_single_gpu(cfg_name, mode, ragged):
 def test_ep_single_rank(mode):
     """The expert-parallel step with one rank (all experts local, the
     exchange going through this GPU's own symmetric buffers): bit-identical
-    to the single-GPU block, two calls with a growing batch."""
+    to the single-GPU block, two calls with a growing batch (the second
+    call's counts do not fit the first call's buffers: the step is planned
+    and dispatched into them, refused, and redone into grown buffers)."""
     from frank_b200 import configs
 
     cfg = configs.BlockConfig("bf16_fg_ep1", T=700, H=1024, F=512, E=32, k=4, normalize=True, dtype="bf16",
