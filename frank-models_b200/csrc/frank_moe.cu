@@ -223,7 +223,7 @@ extern "C" {
 
 const char* frank_last_error(void) { return g_err.c_str(); }
 
-int frank_abi_version(void) { return 101; }
+int frank_abi_version(void) { return 102; }
 
 int frank_num_sms(void) { return num_sms(); }
 

@@ -55,7 +55,7 @@ def test_calls_without_device_work(lib):
     from frank_b200 import _lib
 
     L = _lib.load()
-    assert L.frank_abi_version() == 101
+    assert L.frank_abi_version() == 102
     # size queries are pure host arithmetic
     assert L.frank_moe_ffn_block_workspace_size(1, 16384, 4096, 14336, 8, 2) > 16384 * 2 * 4096 * 2
     assert L.frank_permute_workspace_size(0, 8) > 0
