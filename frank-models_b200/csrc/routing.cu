@@ -7,6 +7,7 @@
 //   top-k (ogt, desc.)   moe_ffn_block.mlir:77-89, oracles/moe.py:95-100
 //   renormalisation      moe_ffn_block.mlir:91-128, oracles/moe.py:103-105
 //   slot flattening      components/moe/mul_mat_id.mlir:51-53 (s = j*T + t)
+#include <mutex>
 #include <type_traits>
 
 #include "common.cuh"
@@ -19,15 +20,16 @@ constexpr int kRouterTok = 32;    // tokens per router block
 constexpr int kRouterHc = 32;     // H chunk staged in shared memory
 constexpr int kRouterThreads = 256;
 
+template <int MaxE>
 __global__ void softmax_topk_kernel(const float* __restrict__ logits, int64_t T, int E, int k,
                                     int normalize, float* __restrict__ w, int32_t* __restrict__ ids) {
-  __shared__ float lg[8][kMaxE];
+  __shared__ float lg[8][MaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   int64_t t = (int64_t)blockIdx.x * 8 + warp;
   if (t >= T) return;
   for (int e = lane; e < E; e += 32) lg[warp][e] = logits[(int64_t)e * T + t];
   __syncwarp();
-  warp_softmax_topk(lg[warp], E, k, normalize, w, ids, T, t);
+  warp_softmax_topk<MaxE>(lg[warp], E, k, normalize, w, ids, T, t);
 }
 
 // Router: a block handles kRouterTok tokens.  x and wr are staged through
@@ -135,44 +137,64 @@ __device__ __forceinline__ void raw_to_f32(const float4 (&r)[2], float (&v)[8]) 
   v[4] = r[1].x; v[5] = r[1].y; v[6] = r[1].z; v[7] = r[1].w;
 }
 
-template <class TX, class TW, int EC>
+template <class TX, class TW, int EC, int S>
 __global__ void __launch_bounds__(kVecThreads)
 router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T, int H, int E, int k, int normalize,
                   float* __restrict__ logits, float* __restrict__ w, int32_t* __restrict__ ids) {
-  extern __shared__ float sw[];                          // [EC][H] fp32
+  // [EC][2][H / 8][4] fp32: row e's 8-column group c is split into two planes
+  // (columns 8c..8c+3 in plane 0, 8c+4..8c+7 in plane 1), so that the
+  // 16-byte reads of consecutive lanes fall on consecutive banks
+  extern __shared__ float sw[];
   __shared__ float lg[kVecThreads / 32][kTPW][EC];
   const int e0 = blockIdx.y * EC;
   const int ec = min(EC, E - e0);
   // router rows -> shared memory, 8 elements per load, four loads in flight
-  // per thread before their stores (H % 8 == 0 on this path)
+  // per thread before their stores (H % 8 == 0 on this path).  Every block
+  // reads the same rows: each starts at its own 128-byte-aligned rotation so
+  // that the blocks do not all ask the same L2 lines at the same time.
   const int nv = EC * H / 8;
-  for (int i0 = threadIdx.x; i0 < nv; i0 += 4 * kVecThreads) {
+  int rot = (int)(((int64_t)blockIdx.x * nv) / gridDim.x) & ~3;
+  if (rot >= nv) rot = 0;
+  for (int j0 = threadIdx.x; j0 < nv; j0 += 4 * kVecThreads) {
     float v[4][8];
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int i = i0 + q * kVecThreads;
+      int i = j0 + q * kVecThreads + rot;
+      if (i >= nv) i -= nv;
       const int e = i * 8 / H, h = i * 8 - e * H;
-      if (i < nv && e < ec) load8(wr + (int64_t)(e0 + e) * H + h, v[q]);
+      if (j0 + q * kVecThreads < nv && e < ec) load8(wr + (int64_t)(e0 + e) * H + h, v[q]);
       else
 #pragma unroll
         for (int j = 0; j < 8; ++j) v[q][j] = 0.f;
     }
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
-      const int i = i0 + q * kVecThreads;
-      if (i < nv) {
-        float4* d = reinterpret_cast<float4*>(sw + (size_t)i * 8);
+      int i = j0 + q * kVecThreads + rot;
+      if (i >= nv) i -= nv;
+      if (j0 + q * kVecThreads < nv) {
+        const int e = i * 8 / H, c = i - e * (H / 8);
+        float4* d = reinterpret_cast<float4*>(sw + (size_t)e * H) + c;
         d[0] = make_float4(v[q][0], v[q][1], v[q][2], v[q][3]);
-        d[1] = make_float4(v[q][4], v[q][5], v[q][6], v[q][7]);
+        d[H / 8] = make_float4(v[q][4], v[q][5], v[q][6], v[q][7]);
       }
     }
   }
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // The block's warps are S column slices x (16 / S) token groups: with few
+  // tokens the H dimension is split so that every SM has work.  Slice s of
+  // warp w is w % S; its columns [hs, he) are 8-aligned.
+  constexpr int kWarps = kVecThreads / 32;
+  const int gpb = kWarps / S;  // token groups per block step
+  const int s = warp % S, gi = warp / S;
+  const int hs = (int)(((int64_t)s * (H / 8)) / S) * 8, he = (int)(((int64_t)(s + 1) * (H / 8)) / S) * 8;
   const int64_t groups = (T + kTPW - 1) / kTPW;
+  const int64_t units = (groups + gpb - 1) / gpb;
   const bool fused = (E <= EC);
-  for (int64_t g = (int64_t)blockIdx.x * (kVecThreads / 32) + warp; g < groups;
-       g += (int64_t)gridDim.x * (kVecThreads / 32)) {
+  // the unit loop is uniform over the block (its bound depends on blockIdx
+  // only), so the block barriers of the slice reduction are reached by all
+  for (int64_t u = blockIdx.x; u < units; u += gridDim.x) {
+    const int64_t g = u * gpb + gi;
     const int64_t t0 = g * kTPW;
     float acc[kTPW][EC];
 #pragma unroll
@@ -188,10 +210,10 @@ router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T
     for (int a = 0; a < kTPW; ++a)
 #pragma unroll
       for (int q = 0; q < kRaw; ++q)
-        xn[a][q] = (lane * 8 < H && t0 + a < T)
-                       ? __ldg(reinterpret_cast<const RawX*>(x + (t0 + a) * H + lane * 8) + q)
+        xn[a][q] = (hs + lane * 8 < he && t0 + a < T)
+                       ? __ldg(reinterpret_cast<const RawX*>(x + (t0 + a) * H + hs + lane * 8) + q)
                        : RawX{};
-    for (int h = lane * 8; h < H; h += 256) {
+    for (int h = hs + lane * 8; t0 < T && h < he; h += 256) {
       float xv[kTPW][8];
 #pragma unroll
       for (int a = 0; a < kTPW; ++a) raw_to_f32(xn[a], xv[a]);
@@ -199,13 +221,14 @@ router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T
       for (int a = 0; a < kTPW; ++a)
 #pragma unroll
         for (int q = 0; q < kRaw; ++q)
-          xn[a][q] = (h + 256 < H && t0 + a < T)
+          xn[a][q] = (h + 256 < he && t0 + a < T)
                          ? __ldg(reinterpret_cast<const RawX*>(x + (t0 + a) * H + h + 256) + q)
                          : RawX{};
 #pragma unroll
       for (int e = 0; e < EC; ++e) {
-        const float4 w0 = *reinterpret_cast<const float4*>(sw + e * H + h);
-        const float4 w1 = *reinterpret_cast<const float4*>(sw + e * H + h + 4);
+        const float4* we = reinterpret_cast<const float4*>(sw + e * H) + h / 8;
+        const float4 w0 = we[0];
+        const float4 w1 = we[H / 8];
         const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
         for (int a = 0; a < kTPW; ++a)
@@ -222,24 +245,46 @@ router_vec_kernel(const TX* __restrict__ x, const TW* __restrict__ wr, int64_t T
         for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
         acc[a][e] = v;
       }
-    if (fused) {
-      if (lane == 0)
+    // warp sums -> shared memory; with S > 1 slice 0 adds the slices'
+    // partials in slice order, one (token, expert) entry per lane
+    if (lane == 0)
 #pragma unroll
+      for (int a = 0; a < kTPW; ++a)
+#pragma unroll
+        for (int e = 0; e < EC; ++e) lg[warp][a][e] = acc[a][e];
+    if (S > 1) {
+      __syncthreads();
+      if (s == 0)
+        for (int l = lane; l < kTPW * EC; l += 32) {
+          float v = lg[warp][l / EC][l % EC];
+          for (int s2 = 1; s2 < S; ++s2) v += lg[warp + s2][l / EC][l % EC];
+          lg[warp][l / EC][l % EC] = v;
+        }
+      __syncthreads();
+      // the block's gpb x kTPW tokens are spread over all its warps
+      for (int j = warp; j < gpb * kTPW; j += kWarps) {
+        const int gj = j / kTPW, a = j - gj * kTPW;
+        const int64_t t = (u * gpb + gj) * kTPW + a;
+        if (t >= T) continue;
+        if (fused) {
+          warp_softmax_topk<32>(lg[gj * S][a], E, k, normalize, w, ids, T, t);
+        } else {
+          for (int e = lane; e < ec; e += 32) logits[(int64_t)(e0 + e) * T + t] = lg[gj * S][a][e];
+        }
+      }
+    } else if (t0 < T) {
+      __syncwarp();
+      if (fused) {
         for (int a = 0; a < kTPW; ++a)
+          if (t0 + a < T) warp_softmax_topk<32>(lg[warp][a], E, k, normalize, w, ids, T, t0 + a);
+      } else if (lane < kTPW && t0 + lane < T) {
 #pragma unroll
-          for (int e = 0; e < EC; ++e) lg[warp][a][e] = acc[a][e];
-      __syncwarp();
-      for (int a = 0; a < kTPW; ++a)
-        if (t0 + a < T) warp_softmax_topk(lg[warp][a], E, k, normalize, w, ids, T, t0 + a);
-      __syncwarp();
-    } else if (lane < kTPW) {
-#pragma unroll
-      for (int a = 0; a < kTPW; ++a)
-        if (a == lane && t0 + a < T)
-#pragma unroll
-          for (int e = 0; e < EC; ++e)
-            if (e < ec) logits[(int64_t)(e0 + e) * T + t0 + a] = acc[a][e];
+        for (int e = 0; e < EC; ++e)
+          if (e < ec) logits[(int64_t)(e0 + e) * T + t0 + lane] = lg[warp][lane][e];
+      }
     }
+    if (S > 1) __syncthreads();  // lg is rewritten by the next unit
+    else __syncwarp();
   }
 }
 
@@ -268,16 +313,17 @@ __global__ void router_split_kernel(const TW* __restrict__ wr, int E, int H, __n
 
 // One warp per token: logits[e] = (p[e] + p[E+e]) + p[2E+e] from the [T, 3E]
 // GEMM output, then softmax + top-k.
+template <int MaxE>
 __global__ void softmax_topk3_kernel(const float* __restrict__ l3, int64_t T, int E, int k, int normalize,
                                      float* __restrict__ w, int32_t* __restrict__ ids) {
-  __shared__ float lg[8][kMaxE];
+  __shared__ float lg[8][MaxE];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t t = (int64_t)blockIdx.x * 8 + warp;
   if (t >= T) return;
   const float* row = l3 + t * 3 * E;
   for (int e = lane; e < E; e += 32) lg[warp][e] = (row[e] + row[E + e]) + row[2 * E + e];
   __syncwarp();
-  warp_softmax_topk(lg[warp], E, k, normalize, w, ids, T, t);
+  warp_softmax_topk<MaxE>(lg[warp], E, k, normalize, w, ids, T, t);
 }
 
 // ---------------------------------------------------------------- permute --
@@ -405,7 +451,14 @@ namespace frank {
 int launch_softmax_topk(const float* logits, int64_t T, int64_t E, int64_t k, int normalize,
                         float* w, int32_t* ids, cudaStream_t st) {
   if (T == 0) return FRANK_OK;
-  softmax_topk_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(logits, T, (int)E, (int)k, normalize, w, ids);
+  // the per-lane arrays are sized by the next multiple of 32 >= E (32..256)
+#define FRANK_SOFTMAX_LAUNCH(MAXE) \
+  softmax_topk_kernel<MAXE><<<(unsigned)((T + 7) / 8), 256, 0, st>>>(logits, T, (int)E, (int)k, normalize, w, ids)
+  if (E <= 32) FRANK_SOFTMAX_LAUNCH(32);
+  else if (E <= 64) FRANK_SOFTMAX_LAUNCH(64);
+  else if (E <= 128) FRANK_SOFTMAX_LAUNCH(128);
+  else FRANK_SOFTMAX_LAUNCH(kMaxE);
+#undef FRANK_SOFTMAX_LAUNCH
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
 }
@@ -430,17 +483,37 @@ static int launch_router_legacy(int x_dtype, const void* x, int wr_dtype, const 
   return FRANK_OK;
 }
 
-template <class TX, class TW, int EC>
-static int launch_router_vec_t(const void* x, const void* wr, int64_t T, int64_t H, int64_t E, int64_t k,
+template <class TX, class TW, int EC, int S>
+static int launch_router_vec_s(const void* x, const void* wr, int64_t T, int64_t H, int64_t E, int64_t k,
                                int normalize, float* logits, float* w, int32_t* ids, cudaStream_t st) {
-  auto kern = router_vec_kernel<TX, TW, EC>;
+  auto kern = router_vec_kernel<TX, TW, EC, S>;
   const size_t smem = (size_t)EC * H * sizeof(float);
-  FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  // attribute and occupancy are fixed per kernel, device and size: queried
+  // once per device (and again when a larger H needs more shared memory)
+  constexpr int kDevs = 64;
+  static std::mutex mu;
+  static size_t set_smem[kDevs] = {};
+  static int occ[kDevs] = {};
+  int dev = 0;
+  FRANK_CUDA_TRY(cudaGetDevice(&dev));
   int per_sm = 0;
-  FRANK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kVecThreads, smem));
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if (dev >= kDevs || set_smem[dev] < smem) {
+      FRANK_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+      FRANK_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kVecThreads, smem));
+      if (dev < kDevs) {
+        set_smem[dev] = smem;
+        occ[dev] = per_sm;
+      }
+    } else {
+      per_sm = occ[dev];
+    }
+  }
   const int64_t passes = (E + EC - 1) / EC;
   const int64_t groups = (T + kTPW - 1) / kTPW;
-  int64_t gx = (groups + kVecThreads / 32 - 1) / (kVecThreads / 32);
+  const int64_t gpb = (kVecThreads / 32) / S;
+  int64_t gx = (groups + gpb - 1) / gpb;
   int64_t cap = (int64_t)num_sms() * (per_sm > 0 ? per_sm : 1);
   cap = (cap + passes - 1) / passes;
   if (gx > cap) gx = cap;
@@ -450,6 +523,24 @@ static int launch_router_vec_t(const void* x, const void* wr, int64_t T, int64_t
   FRANK_LAUNCH_CHECK();
   if (passes > 1) FRANK_TRY(launch_softmax_topk(logits, T, E, k, normalize, w, ids, st));
   return FRANK_OK;
+}
+
+// H is split over S warps of a block when the token groups alone fill fewer
+// than one block per SM for each pass over the experts.
+template <class TX, class TW, int EC>
+static int launch_router_vec_t(const void* x, const void* wr, int64_t T, int64_t H, int64_t E, int64_t k,
+                               int normalize, float* logits, float* w, int32_t* ids, cudaStream_t st) {
+  const int64_t passes = (E + EC - 1) / EC;
+  const int64_t groups = (T + kTPW - 1) / kTPW;
+  const int64_t want = ((int64_t)num_sms() + passes - 1) / passes;  // blocks per pass
+  int S = 1;
+  while (S < 8 && groups * S < want * (kVecThreads / 32) && H / 8 >= 32 * 2 * S) S *= 2;  // each slice keeps >= 32 lanes x 8 columns
+  switch (S) {
+    case 1: return launch_router_vec_s<TX, TW, EC, 1>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+    case 2: return launch_router_vec_s<TX, TW, EC, 2>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+    case 4: return launch_router_vec_s<TX, TW, EC, 4>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+    default: return launch_router_vec_s<TX, TW, EC, 8>(x, wr, T, H, E, k, normalize, logits, w, ids, st);
+  }
 }
 
 template <class TX, class TW>
@@ -508,7 +599,13 @@ static int launch_router_tc(const void* x, int wr_dtype, const void* wr, const _
   // one group of T rows: no offsets array needed
   FRANK_TRY(launch_tc_grouped_gemm(2, x, wr3_pre ? wr3_pre : wr3, nullptr, nullptr, 1, T, 3 * E, H, nullptr, l3, st,
                                    nullptr, nullptr, nullptr, 0, 0));
-  softmax_topk3_kernel<<<(unsigned)((T + 7) / 8), 256, 0, st>>>(l3, T, (int)E, (int)k, normalize, w, ids);
+#define FRANK_SOFTMAX3_LAUNCH(MAXE) \
+  softmax_topk3_kernel<MAXE><<<(unsigned)((T + 7) / 8), 256, 0, st>>>(l3, T, (int)E, (int)k, normalize, w, ids)
+  if (E <= 32) FRANK_SOFTMAX3_LAUNCH(32);
+  else if (E <= 64) FRANK_SOFTMAX3_LAUNCH(64);
+  else if (E <= 128) FRANK_SOFTMAX3_LAUNCH(128);
+  else FRANK_SOFTMAX3_LAUNCH(kMaxE);
+#undef FRANK_SOFTMAX3_LAUNCH
   FRANK_LAUNCH_CHECK();
   return FRANK_OK;
 }

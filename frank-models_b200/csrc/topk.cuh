@@ -12,11 +12,14 @@ constexpr int kMaxK = 32;   // top-k bound
 
 // One warp: softmax over E logits held in shared memory (stride 1), then k
 // rounds of arg-max.  Ties resolve to the lowest expert index.  Lane l owns
-// experts l, l+32, ...
+// experts l, l+32, ...  MaxE: a compile-time bound on E (a multiple of 32)
+// that sizes the per-lane arrays.
+template <int MaxE = kMaxE>
 __device__ inline void warp_softmax_topk(const float* lg, int E, int k, int normalize,
                                   float* w_out, int32_t* id_out, int64_t T, int64_t t) {
+  static_assert(MaxE % 32 == 0 && MaxE <= kMaxE, "MaxE: a multiple of 32, at most kMaxE");
   const int lane = threadIdx.x & 31;
-  constexpr int kPer = kMaxE / 32;
+  constexpr int kPer = MaxE / 32;
   float p[kPer];
   float mx = -INFINITY;
 #pragma unroll

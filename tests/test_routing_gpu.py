@@ -45,7 +45,10 @@ def test_softmax_topk_ties_lowest_index():
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
-@pytest.mark.parametrize("E,k,H,T", [(8, 2, 4096, 512), (128, 8, 2048, 300), (8, 1, 64, 33)])
+# (the vector router splits H over up to 8 warps when the tokens alone do
+# not fill the SMs: 1032 columns split into uneven 8-aligned slices)
+@pytest.mark.parametrize("E,k,H,T", [(8, 2, 4096, 512), (128, 8, 2048, 300), (8, 1, 64, 33), (8, 2, 4096, 2048),
+                                     (6, 2, 1032, 97), (8, 2, 4096, 1), (8, 2, 4096, 16384)])
 def test_router_matches_oracle(dtype, E, k, H, T):
     rng = np.random.default_rng(H + T)
     x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(dtype)
