@@ -19,7 +19,7 @@ int launch_router_pack(int, const void*, int64_t, int64_t, void*, cudaStream_t);
 size_t router_scratch_bytes(int, int64_t, int64_t, int64_t);
 size_t permute_workspace_size(int64_t, int64_t);
 int launch_permute(const int32_t*, int64_t, int64_t, int32_t*, int32_t*, int32_t*, int32_t*, void*, size_t,
-                   cudaStream_t);
+                   cudaStream_t, const float* = nullptr, float* = nullptr);
 int launch_swiglu(int, const void*, const void*, void*, int64_t, cudaStream_t);
 int launch_prepack(int, const void*, int64_t, int64_t, int64_t, int, void*, cudaStream_t);
 int launch_gather_rows(int, const void*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
@@ -365,8 +365,8 @@ int moe_block(int dtype, const void* x, int wr_dtype, const void* wr, const void
   FRANK_TRY(launch_router_topk(dtype, x, wr_dtype, wr, T, H, E, k, normalize, w, ids, L.logits, st, wr3));
   prof_mark(1, st);
   // 2. stable expert permutation                    mul_mat_id.mlir:51-61
-  FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, nullptr, L.perm_ws, L.perm_bytes, st));
-  FRANK_TRY(launch_sorted_weights(w, L.sorted_slots, n, L.wsorted, st));
+  FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, nullptr, L.perm_ws, L.perm_bytes, st,
+                           w, L.wsorted));
   prof_mark(2, st);
   // 3. expert-sorted activation rows (replicate + permute, :130-144, mul_mat_id.mlir:64-84)
   FRANK_TRY(launch_gather_rows(dtype, x, L.sorted_slots, n, T, H, L.xs, st));

@@ -36,7 +36,7 @@
 namespace frank {
 size_t permute_workspace_size(int64_t, int64_t);
 int launch_permute(const int32_t*, int64_t, int64_t, int32_t*, int32_t*, int32_t*, int32_t*, void*, size_t,
-                   cudaStream_t);
+                   cudaStream_t, const float* = nullptr, float* = nullptr);
 }  // namespace frank
 
 namespace {

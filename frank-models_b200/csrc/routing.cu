@@ -444,6 +444,105 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int64_t 
   if (slot_pos) slot_pos[s] = pos;
 }
 
+// Small batches (n <= kSmallRounds * 1024 slots, E <= kSmallMaxE): the whole
+// permutation in one block.  Round r takes slots [1024 r, 1024 r + 1024),
+// one per thread; a slot's rank among the same expert's slots is the
+// expert's running count before the round + the same-expert slots of lower
+// warps + those of lower lanes (warp match), which is the stable order.  The
+// expert totals are then scanned in the block and every thread scatters the
+// slots it kept in registers (and, if asked, their gate weights into expert-
+// sorted order).  Same results as the three-pass form.
+constexpr int kSmallThreads = 1024;
+constexpr int kSmallRounds = 8;
+constexpr int kSmallMaxE = 256;
+
+__global__ void __launch_bounds__(kSmallThreads)
+permute_small_kernel(const int32_t* __restrict__ ids, int n, int E, int32_t* __restrict__ sorted_slots,
+                     int32_t* __restrict__ offsets, int32_t* __restrict__ slot_pos, int32_t* __restrict__ err,
+                     const float* __restrict__ w, float* __restrict__ w_sorted) {
+  constexpr int kWarps = kSmallThreads / 32;
+  __shared__ int32_t running[kSmallMaxE];
+  __shared__ int32_t warp_cnt[kWarps][kSmallMaxE];
+  __shared__ int32_t warp_sums[kWarps];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int e = tid; e < E; e += kSmallThreads) running[e] = 0;
+  for (int i = tid; i < kWarps * kSmallMaxE; i += kSmallThreads) (&warp_cnt[0][0])[i] = 0;
+  __syncthreads();
+  int my_e[kSmallRounds], my_rank[kSmallRounds];
+#pragma unroll
+  for (int r = 0; r < kSmallRounds; ++r) {
+    my_e[r] = -1;
+    my_rank[r] = 0;
+    if (r * kSmallThreads >= n) continue;  // uniform over the block
+    const int s = r * kSmallThreads + tid;
+    int e = -1;
+    if (s < n) {
+      e = ids[s];
+      if (e < 0 || e >= E) {
+        if (err) *err = 1;
+        e = e < 0 ? 0 : E - 1;
+      }
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    const int leader = __ffs(peers) - 1;
+    if (e >= 0 && lane == leader) warp_cnt[warp][e] = __popc(peers);
+    __syncthreads();
+    bool last = false;
+    if (e >= 0) {
+      int before = running[e];
+      for (int w = 0; w < warp; ++w) before += warp_cnt[w][e];
+      my_rank[r] = before + __popc(peers & ((1u << lane) - 1u));
+      my_e[r] = e;
+      // the expert's last slot of the round advances its running count
+      last = (lane == 31 - __clz(peers));
+      for (int w = warp + 1; w < kWarps && last; ++w)
+        if (warp_cnt[w][e] != 0) last = false;
+    }
+    __syncthreads();
+    if (last) running[e] = my_rank[r] + 1;
+    if (e >= 0 && lane == leader) warp_cnt[warp][e] = 0;
+    __syncthreads();
+  }
+  // exclusive scan of the expert totals (E <= kSmallMaxE <= kSmallThreads)
+  const int v = tid < E ? running[tid] : 0;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += u;
+  }
+  if (lane == 31) warp_sums[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int ws = warp_sums[lane];
+    int wi = ws;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += u;
+    }
+    warp_sums[lane] = wi - ws;
+  }
+  __syncthreads();
+  const int excl = warp_sums[warp] + incl - v;
+  __syncthreads();  // everyone has read running[] before it becomes the offsets
+  if (tid < E) {
+    running[tid] = excl;
+    offsets[tid] = excl;
+    if (tid == E - 1) offsets[E] = excl + v;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kSmallRounds; ++r) {
+    if (my_e[r] < 0) continue;
+    const int s = r * kSmallThreads + tid;
+    const int32_t pos = running[my_e[r]] + my_rank[r];
+    sorted_slots[pos] = s;
+    if (slot_pos) slot_pos[s] = pos;
+    if (w_sorted) w_sorted[pos] = w[s];
+  }
+}
+
 }  // namespace
 
 namespace frank {
@@ -636,8 +735,12 @@ size_t permute_workspace_size(int64_t n, int64_t E) {
   return align_up(n * 4, 256) + 2 * align_up(nc * E * 4, 256) + 256;
 }
 
+int launch_sorted_weights(const float*, const int32_t*, int64_t, float*, cudaStream_t);
+
+// w / w_sorted (both or neither): also w_sorted[r] = w[sorted_slots[r]].
 int launch_permute(const int32_t* ids, int64_t n, int64_t E, int32_t* sorted_slots, int32_t* offsets,
-                   int32_t* slot_pos, int32_t* err, void* ws, size_t ws_bytes, cudaStream_t st) {
+                   int32_t* slot_pos, int32_t* err, void* ws, size_t ws_bytes, cudaStream_t st, const float* w,
+                   float* w_sorted) {
   if (E < 1 || E > kPermMaxE) {
     set_error("permute: E=%lld outside [1, %d]", (long long)E, kPermMaxE);
     return FRANK_EINVAL;
@@ -648,6 +751,12 @@ int launch_permute(const int32_t* ids, int64_t n, int64_t E, int32_t* sorted_slo
   }
   if (n == 0) {
     FRANK_CUDA_TRY(cudaMemsetAsync(offsets, 0, (E + 1) * sizeof(int32_t), st));
+    return FRANK_OK;
+  }
+  if (n <= (int64_t)kSmallRounds * kSmallThreads && E <= kSmallMaxE) {
+    permute_small_kernel<<<1, kSmallThreads, 0, st>>>(ids, (int)n, (int)E, sorted_slots, offsets, slot_pos, err,
+                                                      w, w_sorted);
+    FRANK_LAUNCH_CHECK();
     return FRANK_OK;
   }
   int64_t nc = (n + kChunk - 1) / kChunk;
@@ -662,6 +771,7 @@ int launch_permute(const int32_t* ids, int64_t n, int64_t E, int32_t* sorted_slo
   permute_scatter_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(ids, n, (int)E, local_rank, base,
                                                                        sorted_slots, slot_pos);
   FRANK_LAUNCH_CHECK();
+  if (w_sorted) return launch_sorted_weights(w, sorted_slots, n, w_sorted, st);
   return FRANK_OK;
 }
 
