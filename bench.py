@@ -560,7 +560,21 @@ def run_frank_ep(args, cfg, dev, rank, world, local):
         runner = ep.ExpertParallelMoE.synthetic(c4, rank, world, dev, seed=0)
         xa = configs.block_x_torch(c4, dev, seed=0)
         Tr = c4.T // world
-        extra = {c4.name: measure(c4, Tr, xa[rank * Tr:(rank + 1) * Tr].contiguous(), e2e=False)}
+        xr = xa[rank * Tr:(rank + 1) * Tr].contiguous()
+        del xa
+        extra = {c4.name: measure(c4, Tr, xr, e2e=False)}
+        extra[c4.name]["placement"] = "contiguous expert ranges"
+        # the same, with the experts placed by the load of a calibration
+        # batch (other seeded tokens of the same distribution)
+        xc = configs.block_x_torch(c4, dev, seed=1)[rank * Tr:(rank + 1) * Tr].contiguous()
+        placement = ep.balanced_placement(ep.measure_expert_load(xc, runner.wr, c4.k, c4.normalize, c4.E), world)
+        del xc
+        runner = None
+        torch.cuda.empty_cache()
+        runner = ep.ExpertParallelMoE.synthetic(c4, rank, world, dev, seed=0, placement=placement)
+        bal = measure(c4, Tr, xr, e2e=False)
+        bal["placement"] = "load-balanced from a calibration batch (seed 1)"
+        extra[c4.name + "_balanced"] = bal
     if rank == 0:
         line = {
             "metric": METRIC, "value": strong["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,

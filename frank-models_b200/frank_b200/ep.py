@@ -8,7 +8,9 @@ tokens; a step is
 
  1. router + softmax + top-k on the local tokens            (local kernels)
  2. stable expert permutation: because the experts of a rank are
-    contiguous, expert-sorted rows are already grouped by destination rank
+    contiguous (in placement order: by default expert ids themselves, or
+    a load-balanced placement that renames them first), expert-sorted rows
+    are already grouped by destination rank
  3. all-to-all of the per-(rank, local expert) row counts   (NCCL)
  4. grouped NCCL send/recv of the bf16 token rows and their gate weights,
     one chunk per (peer, local expert), each received straight into its
@@ -85,6 +87,42 @@ def plan_exchange(send_cnt: np.ndarray, recv_cnt: np.ndarray):
     return send_splits, recv_splits, seg, local_offsets
 
 
+def balanced_placement(load, P: int) -> np.ndarray:
+    """Expert placement that evens out the rows the ranks process.
+
+    load[g]: rows routed to global expert g (e.g. from a calibration batch);
+    returns the E expert ids in rank-major order: rank p owns
+    ``placement[p*E/P:(p+1)*E/P]``.  Greedy longest-processing-time with
+    equal expert counts: experts by decreasing load (ties to the lower id)
+    each go to the least-loaded rank that still has room (ties to the lower
+    rank); each rank's experts are kept in ascending id order.  Deterministic,
+    so every rank computes the same placement from the same load."""
+    load = np.asarray(load, dtype=np.int64).reshape(-1)
+    E = load.size
+    if P < 1 or E % P:
+        raise ValueError(f"balanced_placement: {E} experts do not split over {P} ranks")
+    El = E // P
+    order = sorted(range(E), key=lambda g: (-int(load[g]), g))
+    rank_load = [0] * P
+    owned = [[] for _ in range(P)]
+    for g in order:
+        p = min((q for q in range(P) if len(owned[q]) < El), key=lambda q: (rank_load[q], q))
+        owned[p].append(g)
+        rank_load[p] += int(load[g])
+    return np.array([g for q in range(P) for g in sorted(owned[q])], dtype=np.int64)
+
+
+def measure_expert_load(x, wr, k: int, normalize: bool, n_expert: int, group=None, prims=None) -> np.ndarray:
+    """Rows every global expert receives from a calibration batch: each rank
+    routes its own tokens ``x``; the per-expert counts are summed over the
+    ranks of ``group`` (collective: every rank calls it)."""
+    pr = prims if prims is not None else CudaPrims()
+    _, ids = pr.route(x, wr, k, normalize)
+    cnt = torch.bincount(ids.reshape(-1).long(), minlength=n_expert)[:n_expert].to(torch.int64)
+    dist.all_reduce(cnt, group=group)
+    return cnt.cpu().numpy()
+
+
 class CudaPrims:
     """Device primitives backed by the C ABI (libfrankmoe.so)."""
 
@@ -115,12 +153,17 @@ class ExpertParallelMoE:
 
     wr: full router [E, H]; w_*_local: this rank's packed experts
     ([E/P, F, H] up/gate, [E/P, H, F] down), i.e. experts
-    [rank*E/P, (rank+1)*E/P).
+    [rank*E/P, (rank+1)*E/P), or with ``placement`` (the E expert ids in
+    rank-major order, see :func:`balanced_placement`) the experts
+    ``placement[rank*E/P:(rank+1)*E/P]`` in that order.  A placement only
+    renames the experts between routing and permutation (ids -> position in
+    the placement), so every row meets the same expert weights and the same
+    kernels: the output does not change with it, the rows per rank do.
     """
 
     def __init__(self, wr, w_up_local, w_gate_local, w_down_local, n_expert: int, n_expert_used: int,
                  normalize_weights: bool, group=None, prims=None, out_dtype=torch.float32, mode: str | None = None,
-                 step_timeout_s: float | None = None, monitor_group=None):
+                 step_timeout_s: float | None = None, monitor_group=None, placement=None):
         self.group = group
         self.P = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -135,6 +178,17 @@ class ExpertParallelMoE:
         self.H, self.F = w_down_local.shape[1], w_down_local.shape[2]
         self.prims = prims if prims is not None else CudaPrims()
         self.out_dtype = out_dtype
+        self.placement = None
+        self._slot_of = None
+        if placement is not None:
+            pl = np.asarray(placement, dtype=np.int64).reshape(-1)
+            if pl.size != self.E or not np.array_equal(np.sort(pl), np.arange(self.E)):
+                raise ValueError(f"placement must be a permutation of the {self.E} expert ids")
+            if not np.array_equal(pl, np.arange(self.E)):
+                self.placement = pl
+                slot_of = np.empty(self.E, dtype=np.int32)
+                slot_of[pl] = np.arange(self.E, dtype=np.int32)
+                self._slot_of_host = torch.from_numpy(slot_of)
         self.last_plan = None
         self.profile = False       # record CUDA events between the phases of each call
         self._marks = []
@@ -167,17 +221,29 @@ class ExpertParallelMoE:
                 self.monitor_group = dist.new_group(ranks=list(range(dist.get_world_size())), backend="gloo")
 
     @classmethod
-    def synthetic(cls, cfg, rank, world, device, seed=0, group=None):
+    def synthetic(cls, cfg, rank, world, device, seed=0, group=None, placement=None):
         """Seeded synthetic weights of configuration ``cfg``; every rank draws
-        the full set with the same seed and keeps its own experts."""
+        the full set with the same seed and keeps its own experts (those of
+        ``placement`` when given)."""
         from . import configs
 
         wr, wu, wg, wd = configs.block_weights_packed_torch(cfg, device, seed=seed)
         El = cfg.E // world
-        sl = slice(rank * El, (rank + 1) * El)
+        if placement is None:
+            sl = slice(rank * El, (rank + 1) * El)
+        else:
+            sl = torch.as_tensor(np.asarray(placement, dtype=np.int64)[rank * El:(rank + 1) * El], device=device)
         wu, wg, wd = (w[sl].contiguous() for w in (wu, wg, wd))
         torch.cuda.empty_cache()
-        return cls(wr, wu, wg, wd, cfg.E, cfg.k, cfg.normalize, group=group)
+        return cls(wr, wu, wg, wd, cfg.E, cfg.k, cfg.normalize, group=group, placement=placement)
+
+    def _placed(self, ids: torch.Tensor) -> torch.Tensor:
+        """Routed expert ids -> positions in the placement (identity without one)."""
+        if self.placement is None:
+            return ids
+        if self._slot_of is None or self._slot_of.device != ids.device:
+            self._slot_of = self._slot_of_host.to(ids.device)
+        return self._slot_of[ids.long()].contiguous()
 
     def _exchange(self, send_buf, recv_buf, send_chunks, recv_chunks):
         """Grouped point-to-point exchange of row chunks.  send_chunks[p] /
@@ -354,7 +420,7 @@ class ExpertParallelMoE:
         if getattr(self, "_wr_pack", None) is None:
             self._wr_pack = ops.router_pack(self.wr)
         w, ids = ops.router_topk(x, self.wr, self.k, self.normalize, pack=self._wr_pack)
-        sorted_slots, offsets, slot_pos, _ = ops.permute(ids, self.E)
+        sorted_slots, offsets, slot_pos, _ = ops.permute(self._placed(ids), self.E)
         cnt = (offsets[1:] - offsets[:-1]).contiguous()
         self._mark()
         counts = self._counts
@@ -424,7 +490,7 @@ class ExpertParallelMoE:
             self._marks.append([])
         self._mark()
         w, ids = pr.route(x, self.wr, self.k, self.normalize)
-        sorted_slots, offsets, slot_pos = pr.permute(ids, self.E)
+        sorted_slots, offsets, slot_pos = pr.permute(self._placed(ids), self.E)
         xs, ws = pr.gather(x, w, sorted_slots)
         # per-(destination rank, its local expert) counts
         cnt = (offsets[1:] - offsets[:-1]).to(torch.int64).reshape(self.P, self.El)

@@ -56,7 +56,7 @@ class NumpyPrims:
         return out
 
 
-def _worker(rank, world, port, cfg, q):
+def _worker(rank, world, port, cfg, q, placed=False):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -72,8 +72,16 @@ def _worker(rank, world, port, cfg, q):
         x = np.random.default_rng(100 + rank).standard_normal((T, H)).astype(np.float32)
         El = E // world
         sl = slice(rank * El, (rank + 1) * El)
+        placement = None
+        if placed:
+            # calibration batch of other tokens: every rank ends with the same placement
+            xc = np.random.default_rng(200 + rank).standard_normal((T, H)).astype(np.float32)
+            load = ep.measure_expert_load(torch.from_numpy(xc), torch.from_numpy(wr), k, norm, E,
+                                          prims=NumpyPrims())
+            placement = ep.balanced_placement(load, world)
+            sl = placement[rank * El:(rank + 1) * El]
         moe = ep.ExpertParallelMoE(torch.from_numpy(wr), torch.from_numpy(wu[sl]), torch.from_numpy(wg[sl]),
-                                   torch.from_numpy(wd[sl]), E, k, norm, prims=NumpyPrims())
+                                   torch.from_numpy(wd[sl]), E, k, norm, prims=NumpyPrims(), placement=placement)
         y = moe(torch.from_numpy(x)).numpy()
         ref = O.moe_ffn_block_grouped(x.astype(np.float64), wr.astype(np.float64),
                                       wu.transpose(1, 2, 0).astype(np.float64),
@@ -81,7 +89,8 @@ def _worker(rank, world, port, cfg, q):
                                       wd.transpose(1, 2, 0).astype(np.float64), E, k, H, F, norm)
         err = float(np.max(np.abs(y - ref)))
         send_cnt, recv_cnt = moe.last_plan
-        q.put((rank, err, int(send_cnt.sum()), int(recv_cnt.sum())))
+        q.put((rank, err, int(send_cnt.sum()), int(recv_cnt.sum()),
+               None if placement is None else placement.tolist()))
     finally:
         dist.destroy_process_group()
 
@@ -94,17 +103,19 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("world,cfg", [
-    (2, (37, 16, 12, 8, 2, False)),
-    (2, (50, 8, 8, 4, 3, True)),
-    (4, (29, 16, 8, 16, 4, False)),
-    (4, (1, 8, 8, 8, 2, True)),     # a single token per rank: most ranks receive nothing from some peers
+@pytest.mark.parametrize("world,cfg,placed", [
+    (2, (37, 16, 12, 8, 2, False), False),
+    (2, (50, 8, 8, 4, 3, True), False),
+    (4, (29, 16, 8, 16, 4, False), False),
+    (4, (1, 8, 8, 8, 2, True), False),   # a single token per rank: most ranks receive nothing from some peers
+    (2, (37, 16, 12, 8, 2, False), True),  # load-balanced expert placement from a calibration batch
+    (4, (29, 16, 8, 16, 4, True), True),
 ])
-def test_expert_parallel_matches_single_device(world, cfg):
+def test_expert_parallel_matches_single_device(world, cfg, placed):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, q, placed)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
@@ -112,21 +123,54 @@ def test_expert_parallel_matches_single_device(world, cfg):
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     res = sorted(q.get(timeout=10) for _ in range(world))
     T, k = cfg[0], cfg[4]
-    for rank, err, sent, recvd in res:
+    for rank, err, sent, recvd, _ in res:
         assert err < 1e-4, f"rank {rank}: max abs error {err}"
         assert sent == T * k
     assert sum(r[3] for r in res) == world * T * k
+    if placed:
+        pls = [r[4] for r in res]
+        assert all(pl == pls[0] for pl in pls)  # every rank derived the same placement
+        assert sorted(pls[0]) == list(range(cfg[3]))
 
 
-def test_plan_exchange_layout():
-    from frank_b200.ep import plan_exchange
+def test_balanced_placement():
+    from frank_b200.ep import balanced_placement
 
-    recv = np.array([[2, 0, 1], [1, 3, 0]])  # from rank 0: e0=2,e1=0,e2=1 ; from rank 1: e0=1,e1=3,e2=0
-    send = np.array([[1, 1, 1], [2, 2, 2]])
-    ss, rs, seg, off = plan_exchange(send, recv)
-    assert ss.tolist() == [3, 6] and rs.tolist() == [3, 4]
-    assert off.tolist() == [0, 3, 6, 7]
-    # source-major: [r0e0 r0e0 r0e2 | r1e0 r1e1 r1e1 r1e1]; expert-major: [e0: r0 r0 r1 | e1: r1 r1 r1 | e2: r0]
-    assert seg.src_start.tolist() == [0, 2, 2, 3, 4, 7]
-    assert seg.dst_start.tolist() == [0, 3, 6, 2, 3, 7]
-    assert seg.length.tolist() == [2, 0, 1, 1, 3, 0]
+    # Zipf-like load over 8 experts on 2 ranks: the two heaviest go to different ranks
+    load = np.array([100, 50, 33, 25, 20, 17, 14, 12])
+    pl = balanced_placement(load, 2)
+    assert sorted(pl.tolist()) == list(range(8))
+    r0, r1 = set(pl[:4].tolist()), set(pl[4:].tolist())
+    assert 0 in r0 and 1 in r1
+    loads = [load[list(r0)].sum(), load[list(r1)].sum()]
+    assert max(loads) <= 146  # optimum 143 (100 + the three lightest); contiguous halves give 208 / 63
+    assert list(pl[:4]) == sorted(pl[:4]) and list(pl[4:]) == sorted(pl[4:])
+    # equal loads: experts dealt round-robin (ties to the lower id, then the lower rank)
+    assert balanced_placement(np.ones(8), 4).tolist() == [0, 4, 1, 5, 2, 6, 3, 7]
+    # deterministic, and every rank gets E/P experts
+    pl2 = balanced_placement(np.arange(16)[::-1] ** 2, 4)
+    assert pl2.tolist() == balanced_placement(np.arange(16)[::-1] ** 2, 4).tolist()
+    with pytest.raises(ValueError):
+        balanced_placement(np.ones(6), 4)
+
+
+def test_placement_validation():
+    from frank_b200 import ep
+
+    port = _free_port()
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    try:
+        E, H, F = 4, 8, 8
+        wr = torch.zeros(E, H)
+        w = (torch.zeros(E, F, H), torch.zeros(E, F, H), torch.zeros(E, H, F))
+        for bad in ([0, 0, 1, 2], [0, 1, 2], [0, 1, 2, 4]):
+            with pytest.raises(ValueError):
+                ep.ExpertParallelMoE(wr, *w, E, 2, False, prims=NumpyPrims(), placement=bad)
+        # the identity placement is the contiguous split (no renaming)
+        moe = ep.ExpertParallelMoE(wr, *w, E, 2, False, prims=NumpyPrims(), placement=[0, 1, 2, 3])
+        assert moe.placement is None
+        moe = ep.ExpertParallelMoE(wr, *w, E, 2, False, prims=NumpyPrims(), placement=[2, 0, 3, 1])
+        ids = torch.tensor([[0, 1], [2, 3]], dtype=torch.int32)
+        assert moe._placed(ids).tolist() == [[1, 3], [0, 2]]
+    finally:
+        dist.destroy_process_group()

@@ -22,7 +22,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, cfg, mode, ragged, q):
+def _worker(rank, world, port, cfg, mode, ragged, q, placed=False):
     import torch.distributed as dist
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
@@ -38,8 +38,15 @@ def _worker(rank, world, port, cfg, mode, ragged, q):
             x = x[:(cfg.T // 2 if world == 1 else cfg.T - 37 * rank)].contiguous()
         El = cfg.E // world
         sl = slice(rank * El, (rank + 1) * El)
+        placement = None
+        if placed:  # experts placed by the load of a calibration batch of other tokens
+            xc = configs.block_x_torch(cfg, dev, seed=50 + rank)
+            placement = ep.balanced_placement(ep.measure_expert_load(xc, wr, cfg.k, cfg.normalize, cfg.E), world)
+            if world == 1:  # one rank holds every expert: still renamed, in reverse order
+                placement = placement[::-1].copy()
+            sl = torch.as_tensor(placement[rank * El:(rank + 1) * El], device=dev)
         moe = ep.ExpertParallelMoE(wr, wu[sl].contiguous(), wg[sl].contiguous(), wd[sl].contiguous(), cfg.E, cfg.k,
-                                   cfg.normalize, mode=mode)
+                                   cfg.normalize, mode=mode, placement=placement)
         y = moe(x)
         if ragged and rank == world - 1:
             # the last rank's batch grows to T: every rank's buffers grow together
@@ -54,6 +61,34 @@ def _worker(rank, world, port, cfg, mode, ragged, q):
                float((y - ref).abs().max().item()), ops.read_device_error()))
     finally:
         dist.destroy_process_group()
+
+
+def _fg_cfg():
+    from frank_b200 import configs
+
+    return configs.BlockConfig("bf16_fg_ep", T=1000, H=2048, F=768, E=128, k=8, normalize=False, dtype="bf16",
+                               zipf=1.2)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
+@pytest.mark.parametrize("mode", ["p2p", "nccl"])
+def test_ep_balanced_placement_equals_single_gpu(mode):
+    """Experts placed by load (Zipf-skewed routing): the same output bit for
+    bit, with the rows spread more evenly than the contiguous split."""
+    cfg = _fg_cfg()
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg, mode, False, q, True)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    for rank, equal, det, err, dev_err in sorted(q.get(timeout=10) for _ in range(world)):
+        assert equal, f"rank {rank}: max |ep - single| = {err}"
+        assert det and dev_err == 0
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs >= 2 GPUs")
@@ -86,20 +121,22 @@ def test_ep_equals_single_gpu(cfg_name, mode, ragged):
         assert det and dev_err == 0
 
 
+@pytest.mark.parametrize("placed", [False, True], ids=["contiguous", "placed"])
 @pytest.mark.parametrize("mode", ["p2p", "nccl"])
-def test_ep_single_rank(mode):
+def test_ep_single_rank(mode, placed):
     """The expert-parallel step with one rank (all experts local, the
     exchange going through this GPU's own symmetric buffers): bit-identical
     to the single-GPU block, two calls with a growing batch (the second
     call's counts do not fit the first call's buffers: the step is planned
-    and dispatched into them, refused, and redone into grown buffers)."""
+    and dispatched into them, refused, and redone into grown buffers).
+    ``placed``: the experts renamed by a (reversed) placement."""
     from frank_b200 import configs
 
     cfg = configs.BlockConfig("bf16_fg_ep1", T=700, H=1024, F=512, E=32, k=4, normalize=True, dtype="bf16",
                               zipf=1.2)
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    p = ctx.Process(target=_worker, args=(0, 1, _free_port(), cfg, mode, True, q))
+    p = ctx.Process(target=_worker, args=(0, 1, _free_port(), cfg, mode, True, q, placed))
     p.start()
     p.join(timeout=300)
     assert p.exitcode == 0
