@@ -464,10 +464,12 @@ def run_frank(args, cfg):
         from frank_b200 import configs
 
         extra = {}
-        for c in (configs.c5(1), configs.c5(8), configs.C4):
+        for c in (configs.c5(1), configs.c5(8), configs.c5(32), configs.c5(64), configs.C4):
             r = bench_block_1gpu(args, c, dev, local, cpu=not args.no_cpu_baseline)
             torch.cuda.empty_cache()
             extra[c.name] = r
+        extra[configs.C2.name] = bench_mul_mat_id(args, configs.C2)
+        torch.cuda.empty_cache()
         line["extra_configs"] = extra
     print(json.dumps(line), flush=True)
 
@@ -597,6 +599,12 @@ def run_frank_ep(args, cfg, dev, rank, world, local):
 
 def run_mul_mat_id(args, cfg):
     """mul_mat_id alone (bf16 in, fp32 accumulate and output), one GPU."""
+    print(json.dumps(bench_mul_mat_id(args, cfg)), flush=True)
+
+
+def bench_mul_mat_id(args, cfg):
+    """The mul_mat_id bench line (dict): grouped GEMM over expert-sorted
+    columns, inputs resident on the device."""
     import numpy as np
     import torch
 
@@ -628,14 +636,18 @@ def run_mul_mat_id(args, cfg):
     ms = ev0.elapsed_time(ev1) / args.steps
     pk, pk_kind = peaks()
     tf = cfg.flops / (ms / 1e3) / 1e12
+    gpk, gkey = _gemm_peak(pk, ms * args.steps / 1e3)
     line = {"metric": "mul_mat_id tokens/s", "value": cfg.T / (ms / 1e3), "unit": "tokens/s", "n_gpus": 1,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": {"workload": cfg.name, "n_tokens": cfg.T, "n_in": cfg.n_in, "n_out": cfg.n_out,
                        "n_expert": cfg.E, "n_expert_used": cfg.k, "output": "fp32 [n_out, k, T]"},
             "tflops": tf, "frac_of_sustained_bf16": tf / float(pk["bf16_tflops_sustained"]),
+            "roofline": {"kernel": "mul_mat_id (gather_cols + tc_grouped_gemm + scatter_out)", "bound": "tensor",
+                         "achieved": tf, "peak": gpk, "unit": "TFLOP/s", "frac": tf / gpk,
+                         "peak_source": f"{pk_kind} {gkey} (the whole call timed)", "traffic": None},
             "gpu_launches": int(ops.launch_count() - l0), "clocks": clk.summary()}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def cpu_baseline_from_device(cfg, x, block):
