@@ -86,6 +86,43 @@ __global__ void gather_cols_kernel(const T* __restrict__ in, const int32_t* __re
   }
 }
 
+// Tiled form (16-byte vectors; n_slots and I multiples of the vector, 16-byte
+// aligned buffers): a block takes 64 slots x 64 columns, reads the 64 input
+// rows i along the slot axis (in[i, s0:s0+64], contiguous), transposes them
+// through shared memory, and writes each slot's 64 columns into its sorted
+// row xs[slot_pos[s], i0:i0+64].  Every global access is a 16-byte vector.
+constexpr int kTT = 64;  // tile edge of the tiled transposes
+
+template <class T>
+__global__ void __launch_bounds__(256)
+gather_cols_tiled_kernel(const T* __restrict__ in, const int32_t* __restrict__ slot_pos, int64_t n_slots,
+                         int64_t I, T* __restrict__ xs) {
+  constexpr int V = 16 / sizeof(T);  // elements per vector
+  constexpr int VR = kTT / V;        // vectors per tile row
+  __shared__ float tile[kTT][kTT + 1];  // [slot][column]
+  const int64_t s0 = (int64_t)blockIdx.x * kTT, i0 = (int64_t)blockIdx.y * kTT;
+  for (int q = threadIdx.x; q < kTT * VR; q += blockDim.x) {
+    const int ii = q / VR, v = q - ii * VR;  // input row i0+ii, slots s0+V*v ...
+    const int64_t i = i0 + ii, s = s0 + (int64_t)v * V;
+    uint4 u = make_uint4(0, 0, 0, 0);
+    if (i < I && s < n_slots) u = __ldg(reinterpret_cast<const uint4*>(in + i * n_slots + s));
+    const T* e = reinterpret_cast<const T*>(&u);
+#pragma unroll
+    for (int j = 0; j < V; ++j) tile[v * V + j][ii] = load_as_f32(e, j);  // exact for bf16 and f32
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < kTT * VR; q += blockDim.x) {
+    const int ss = q / VR, v = q - ss * VR;  // slot s0+ss, columns i0+V*v ...
+    const int64_t s = s0 + ss, i = i0 + (int64_t)v * V;
+    if (s >= n_slots || i >= I) continue;
+    uint4 u;
+    T* e = reinterpret_cast<T*>(&u);
+#pragma unroll
+    for (int j = 0; j < V; ++j) e[j] = from_f32<T>(tile[ss][v * V + j]);
+    *reinterpret_cast<uint4*>(xs + (int64_t)slot_pos[s] * I + i) = u;
+  }
+}
+
 // ---------------------------------------- mul_mat_id output scatter ----
 // ys[r, o] (expert-sorted rows) -> out[o, slot] with slot = sorted_slots[r]
 // (mul_mat_id.mlir:96-117).  Reads rows through slot_pos so that the write
@@ -104,6 +141,36 @@ __global__ void scatter_out_kernel(const float* __restrict__ ys, const int32_t* 
   for (int yy = threadIdx.y; yy < 32; yy += blockDim.y) {
     int64_t o = o0 + yy, s = s0 + threadIdx.x;
     if (o < O && s < n_slots) out[o * n_slots + s] = tile[threadIdx.x][yy];
+  }
+}
+
+// Tiled form (n_slots and O multiples of 4, 16-byte aligned buffers): a
+// block takes 64 slots x 64 outputs; each slot's row of ys is read as 16
+// float4 (256 contiguous bytes), transposed through shared memory, and each
+// output row out[o, s0:s0+64] is written as 16 float4.
+__global__ void __launch_bounds__(256)
+scatter_out_tiled_kernel(const float* __restrict__ ys, const int32_t* __restrict__ slot_pos, int64_t n_slots,
+                         int64_t O, float* __restrict__ out) {
+  constexpr int VR = kTT / 4;
+  __shared__ float tile[kTT][kTT + 1];  // [output][slot]
+  const int64_t s0 = (int64_t)blockIdx.x * kTT, o0 = (int64_t)blockIdx.y * kTT;
+  for (int q = threadIdx.x; q < kTT * VR; q += blockDim.x) {
+    const int ss = q / VR, v = q - ss * VR;  // slot s0+ss, outputs o0+4v ...
+    const int64_t s = s0 + ss, o = o0 + 4 * v;
+    float4 f = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (s < n_slots && o < O) f = __ldg(reinterpret_cast<const float4*>(ys + (int64_t)slot_pos[s] * O + o));
+    tile[4 * v + 0][ss] = f.x;
+    tile[4 * v + 1][ss] = f.y;
+    tile[4 * v + 2][ss] = f.z;
+    tile[4 * v + 3][ss] = f.w;
+  }
+  __syncthreads();
+  for (int q = threadIdx.x; q < kTT * VR; q += blockDim.x) {
+    const int oo = q / VR, v = q - oo * VR;  // output o0+oo, slots s0+4v ...
+    const int64_t o = o0 + oo, s = s0 + 4 * v;
+    if (o >= O || s >= n_slots) continue;
+    *reinterpret_cast<float4*>(out + o * n_slots + s) =
+        make_float4(tile[oo][4 * v], tile[oo][4 * v + 1], tile[oo][4 * v + 2], tile[oo][4 * v + 3]);
   }
 }
 
@@ -300,9 +367,22 @@ int launch_gather_rows(int dtype, const void* x, const int32_t* sorted_slots, in
   return FRANK_OK;
 }
 
+// slot_pos (may be null): the tiled form's inverse of sorted_slots.
 int launch_gather_cols(int dtype, const void* in, const int32_t* sorted_slots, int64_t n_slots, int64_t I, void* xs,
-                       cudaStream_t st) {
+                       cudaStream_t st, const int32_t* slot_pos) {
   if (n_slots == 0 || I == 0) return FRANK_OK;
+  const int64_t vec = dtype == FRANK_F32 ? 4 : 8;
+  if (slot_pos && n_slots % vec == 0 && I % vec == 0 && (uintptr_t)in % 16 == 0 && (uintptr_t)xs % 16 == 0 &&
+      (I + kTT - 1) / kTT <= 65535) {
+    dim3 grid((unsigned)((n_slots + kTT - 1) / kTT), (unsigned)((I + kTT - 1) / kTT));
+    if (dtype == FRANK_F32)
+      gather_cols_tiled_kernel<float><<<grid, 256, 0, st>>>((const float*)in, slot_pos, n_slots, I, (float*)xs);
+    else
+      gather_cols_tiled_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)in, slot_pos, n_slots,
+                                                                     I, (__nv_bfloat16*)xs);
+    FRANK_LAUNCH_CHECK();
+    return FRANK_OK;
+  }
   if ((I + 31) / 32 > 65535) {
     set_error("gather_cols: I=%lld too large", (long long)I);
     return FRANK_EINVAL;
@@ -320,6 +400,13 @@ int launch_gather_cols(int dtype, const void* in, const int32_t* sorted_slots, i
 int launch_scatter_out(const float* ys, const int32_t* slot_pos, int64_t n_slots, int64_t O, float* out,
                        cudaStream_t st) {
   if (n_slots == 0 || O == 0) return FRANK_OK;
+  if (n_slots % 4 == 0 && O % 4 == 0 && (uintptr_t)ys % 16 == 0 && (uintptr_t)out % 16 == 0 &&
+      (O + kTT - 1) / kTT <= 65535) {
+    dim3 grid((unsigned)((n_slots + kTT - 1) / kTT), (unsigned)((O + kTT - 1) / kTT));
+    scatter_out_tiled_kernel<<<grid, 256, 0, st>>>(ys, slot_pos, n_slots, O, out);
+    FRANK_LAUNCH_CHECK();
+    return FRANK_OK;
+  }
   if ((O + 31) / 32 > 65535) {
     set_error("scatter_out: O=%lld too large", (long long)O);
     return FRANK_EINVAL;

@@ -23,7 +23,8 @@ int launch_permute(const int32_t*, int64_t, int64_t, int32_t*, int32_t*, int32_t
 int launch_swiglu(int, const void*, const void*, void*, int64_t, cudaStream_t);
 int launch_prepack(int, const void*, int64_t, int64_t, int64_t, int, void*, cudaStream_t);
 int launch_gather_rows(int, const void*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t);
-int launch_gather_cols(int, const void*, const int32_t*, int64_t, int64_t, void*, cudaStream_t);
+int launch_gather_cols(int, const void*, const int32_t*, int64_t, int64_t, void*, cudaStream_t,
+                       const int32_t* = nullptr);
 int launch_scatter_out(const float*, const int32_t*, int64_t, int64_t, float*, cudaStream_t);
 int launch_combine(int, const float*, const int32_t*, int64_t, int64_t, int64_t, void*, cudaStream_t,
                    const float* residual = nullptr);
@@ -307,7 +308,7 @@ int frank_mul_mat_id(int dtype, const void* w_eoi, const void* input, const int3
   MmidWs L;
   mmid_layout(dtype, O, I, E, k, T, workspace, ws_bytes, &L);
   FRANK_TRY(launch_permute(ids, n, E, L.sorted_slots, L.offsets, L.slot_pos, err_flag, L.perm_ws, L.perm_bytes, st));
-  FRANK_TRY(launch_gather_cols(dtype, input, L.sorted_slots, n, I, L.xs, st));
+  FRANK_TRY(launch_gather_cols(dtype, input, L.sorted_slots, n, I, L.xs, st, L.slot_pos));
   if (dtype == FRANK_F32) {
     FRANK_TRY(launch_grouped_gemm_f32(0, (const float*)L.xs, (const float*)w_eoi, nullptr, L.offsets, E, n, O, I,
                                       nullptr, L.ys, st));

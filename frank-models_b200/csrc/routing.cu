@@ -453,7 +453,7 @@ __global__ void permute_scatter_kernel(const int32_t* __restrict__ ids, int64_t 
 // slots it kept in registers (and, if asked, their gate weights into expert-
 // sorted order).  Same results as the three-pass form.
 constexpr int kSmallThreads = 1024;
-constexpr int kSmallRounds = 8;
+constexpr int kSmallRounds = 4;  // past 4096 slots the three passes are as fast (measured at 8192)
 constexpr int kSmallMaxE = 256;
 
 __global__ void __launch_bounds__(kSmallThreads)

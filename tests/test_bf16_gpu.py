@@ -38,6 +38,7 @@ def _f64(t):
     (144, 72, 6, 2, 129, "one"),           # ragged N (144 % 256 != 0), K % 64 != 0, all on one expert
     (256, 64, 16, 4, 200, "sparse"),       # empty experts
     (1024, 512, 8, 2, 1000, "uniform"),
+    (208, 136, 8, 2, 260, "uniform"),      # tiled transposes with partial 64-wide tiles on every axis
 ])
 def test_mul_mat_id_bf16(O_, I, E, k, T, kind):
     rng = np.random.default_rng(O_ + T)

@@ -71,10 +71,10 @@ def test_router_matches_oracle(dtype, E, k, H, T):
 @pytest.mark.parametrize("E,k,T,kind", [(8, 2, 16384, "uniform"), (128, 8, 8192, "zipf"), (128, 8, 1, "uniform"),
                                         (8, 2, 3, "one"), (64, 4, 777, "sparse"), (1024, 2, 5000, "uniform"),
                                         (8, 2, 0, "uniform"),
-                                        # one-block form: n <= 8192 slots and E <= 256; the
+                                        # one-block form: n <= 4096 slots and E <= 256; the
                                         # three-pass form past either limit
-                                        (8, 2, 2048, "uniform"), (256, 8, 1024, "zipf"),
-                                        (256, 8, 1025, "uniform"), (8, 2, 4097, "one"), (257, 1, 100, "uniform")])
+                                        (8, 2, 2048, "uniform"), (256, 8, 512, "zipf"),
+                                        (256, 8, 513, "uniform"), (8, 2, 2049, "one"), (257, 1, 100, "uniform")])
 def test_permute_bitexact(E, k, T, kind):
     rng = np.random.default_rng(T + E)
     if kind == "uniform":
